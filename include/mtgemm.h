@@ -1,0 +1,128 @@
+/*
+ * mtgemm.h -- C ABI of libmtgemm.so, the B200 (sm_100a) engine for miniTensor's fp32
+ * dense-contraction path: matmul / bmm / Linear / Conv2D-as-GEMM.
+ *
+ * The reference (dionkadi/miniTensor) reaches its GPU kernels through C++ templates
+ * declared in include/TensorOps.hpp:697-728 and defined in src/gpu_ops.cpp. Each
+ * mt_*_gpu function below replaces one of them for T = float, with the same argument
+ * meaning, so a binding only maps a Tensor<float> to an mt_tensor (storage pointer,
+ * view offset, shape, strides -- exactly the fields of include/TensorImpl.hpp) and
+ * turns a non-zero status into the reference's exception (INTEGRATION.md shows it).
+ *
+ * Conventions (the reference's, include/TensorOps.hpp:993-1149, include/GpuUtils.hpp):
+ *   - All pointers are device pointers. The caller allocates every output with its final
+ *     shape; the callee overwrites it (gradient accumulation stays with the caller).
+ *   - Inputs are borrowed views: data + offset is element (0,...,0); strides are in
+ *     elements; stride 0 marks a broadcast (expand) dimension. Unlike the reference's
+ *     matmul_gpu (src/gpu_ops.cpp:1125-1127), view offsets are always honoured.
+ *   - Launches are asynchronous on `stream` (NULL = legacy default stream, the
+ *     reference's active_stream() default); nothing synchronises inside a call, no call
+ *     allocates device memory unless stated, so calls can be captured in CUDA graphs.
+ *   - Every function returns an mt_status and never throws; mt_last_error() gives the
+ *     thread-local message of the last failure.
+ */
+#ifndef MTGEMM_H
+#define MTGEMM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(_WIN32)
+#define MT_API __declspec(dllexport)
+#else
+#define MT_API __attribute__((visibility("default")))
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MT_MAX_DIMS 8 /* include/Defines.hpp:8 MAX_DIMS */
+
+/* A strided view, field for field the reference's TensorImpl
+ * (include/TensorImpl.hpp:153-160: storage_, shape_, strides_, offset_). */
+typedef struct mt_tensor {
+    float* data;                   /* storage base = Tensor<float>::data() (include/Tensor.hpp:80) */
+    uint64_t offset;               /* Tensor::offset(), elements */
+    uint32_t ndim;                 /* <= MT_MAX_DIMS */
+    uint64_t shape[MT_MAX_DIMS];
+    uint64_t strides[MT_MAX_DIMS]; /* elements; 0 = broadcast */
+} mt_tensor;
+
+typedef enum mt_status {
+    MT_OK = 0,
+    MT_EINVAL = 1,        /* shape/argument error (reference: std::invalid_argument) */
+    MT_EUNSUPPORTED = 2,  /* valid request this build does not serve */
+    MT_ECUDA = 3,         /* CUDA runtime error (reference: GPU_CHECK -> std::runtime_error) */
+    MT_ETIMEOUT = 4,      /* a device-side bounded wait gave up (mt_device_status) */
+    MT_ENOMEM = 5
+} mt_status;
+
+/* Arithmetic of the fp32-input contraction. */
+typedef enum mt_mode {
+    MT_MODE_DEFAULT = -1, /* process default: env MT_GEMM_MODE (strict|tf32|tf32x3), else TF32X3 */
+    MT_STRICT_FP32 = 0,   /* FFMA only (SIMT kernel), k ascending per output */
+    MT_TF32 = 1,          /* tcgen05 kind::tf32, one MMA per k-step */
+    MT_TF32X3 = 2         /* tcgen05 split precision hi*hi + hi*lo + lo*hi (fp32-accurate) */
+} mt_mode;
+
+/* Fused epilogue flags (applied after the full k-sum, in this order). */
+enum {
+    MT_EPI_NONE = 0,
+    MT_EPI_BIAS_ROW = 1, /* C[m,n] += bias[m] */
+    MT_EPI_BIAS_COL = 2, /* C[m,n] += bias[n]   (Linear: bias [1,out]) */
+    MT_EPI_RELU = 4      /* C = max(C, 0) */
+};
+
+/* ---- mirrors of the reference GPU entry points (T = float) -------------------------- */
+
+/* include/TensorOps.hpp:703 matmul_gpu(A, B, C): C[M,N] = A[M,K] * B[K,N].
+ * Called by matmul() (include/TensorOps.hpp:1026) for contiguous operands. */
+MT_API int mt_matmul_gpu(const mt_tensor* A, const mt_tensor* B, const mt_tensor* C, void* stream);
+
+/* include/TensorOps.hpp:704 matmul_gpu_strided: same contract, arbitrary 2-D strides
+ * (the transposed views of MatmulBackward, include/Autograd.hpp:131-141). */
+MT_API int mt_matmul_gpu_strided(const mt_tensor* A, const mt_tensor* B, const mt_tensor* C, void* stream);
+
+/* include/TensorOps.hpp:705 matmul_gpu_v2 and :706 matmul_gpu_bk16 (benchmark names of
+ * the same GEMM, src/gpu_ops.cpp:1167-1197). */
+MT_API int mt_matmul_gpu_v2(const mt_tensor* A, const mt_tensor* B, const mt_tensor* C, void* stream);
+MT_API int mt_matmul_gpu_bk16(const mt_tensor* A, const mt_tensor* B, const mt_tensor* C, void* stream);
+
+/* Replaces the per-batch loop of bmm() (include/TensorOps.hpp:933-991, which makes both
+ * operands contiguous and launches one matmul_gpu per batch): one launch over
+ * C[b,M,N] = A[b,M,K] * B[b,K,N]; a batch stride of 0 (expand) is read in place. */
+MT_API int mt_bmm_gpu(const mt_tensor* A, const mt_tensor* B, const mt_tensor* C, void* stream);
+
+/* Linear<float>::forward (include/Module.hpp:112-114: matmul(x, W) + bias) as one GEMM
+ * with the bias add (and optional ReLU) fused into the epilogue. X [M,in], W [in,out]
+ * (the reference's layout), bias [1,out] or [out] or NULL, Y [M,out]. */
+MT_API int mt_linear_fwd_gpu(const mt_tensor* X, const mt_tensor* W, const mt_tensor* bias,
+                             const mt_tensor* Y, int relu, void* stream);
+
+/* ---- general entry point ----------------------------------------------------------- */
+
+/* C = epi(A * B) for 2-D or 3-D (batched) views with an explicit mode. `bias` is a device
+ * pointer of M (BIAS_ROW) or N (BIAS_COL) floats, shared by all batches. */
+MT_API int mt_gemm(const mt_tensor* A, const mt_tensor* B, const mt_tensor* C,
+                   const float* bias, int epi, int mode, void* stream);
+
+/* ---- process settings and diagnostics ---------------------------------------------- */
+
+MT_API int mt_set_default_mode(int mode);   /* returns the previous default */
+MT_API int mt_get_default_mode(void);
+MT_API const char* mt_last_error(void);     /* thread-local */
+/* Kernel chosen by this thread's last successful call, e.g. "umma_tf32x3 bn=256 a=K b=MN". */
+MT_API const char* mt_last_path(void);
+/* Kernels launched by this library since load (all threads). */
+MT_API uint64_t mt_launch_count(void);
+/* Synchronises the current device and returns its device status word (0 = clean,
+ * else the code of the first bounded wait that gave up); reset != 0 clears it. */
+MT_API int mt_device_status(int reset);
+/* Library version string. */
+MT_API const char* mt_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MTGEMM_H */

@@ -1,0 +1,437 @@
+// mt_api.cu -- the C ABI of libmtgemm.so (declared in include/mtgemm.h): argument
+// checks with the reference's error semantics, view -> problem mapping, kernel
+// selection, TMA tensor-map encoding and launches.
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "mtgemm.h"
+#include "mt_common.cuh"
+#include "simt_gemm.cuh"
+#include "umma_gemm.cuh"
+
+namespace {
+
+using mt::GemmProblem;
+
+thread_local std::string t_err;
+thread_local std::string t_path;
+std::atomic<uint64_t> g_launches{0};
+std::atomic<int> g_default_mode{-2};   // -2: not yet read from the environment
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    t_err = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(MT_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+int resolve_mode(int mode) {
+    if (mode >= MT_STRICT_FP32 && mode <= MT_TF32X3) return mode;
+    int d = g_default_mode.load();
+    if (d == -2) {
+        d = MT_TF32X3;
+        if (const char* e = std::getenv("MT_GEMM_MODE")) {
+            if (!strcmp(e, "strict") || !strcmp(e, "fp32")) d = MT_STRICT_FP32;
+            else if (!strcmp(e, "tf32")) d = MT_TF32;
+            else if (!strcmp(e, "tf32x3") || !strcmp(e, "3xtf32")) d = MT_TF32X3;
+        }
+        int expect = -2;
+        g_default_mode.compare_exchange_strong(expect, d);
+        d = g_default_mode.load();
+    }
+    return d;
+}
+
+// ------------------------------- device properties -------------------------------
+struct DevInfo {
+    int sms = 0;
+    int cc = 0;
+};
+
+DevInfo dev_info() {
+    static std::mutex mu;
+    static DevInfo cache[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> g(mu);
+    DevInfo& d = cache[dev & 63];
+    if (d.sms == 0) {
+        cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+        int maj = 0, mnr = 0;
+        cudaDeviceGetAttribute(&maj, cudaDevAttrComputeCapabilityMajor, dev);
+        cudaDeviceGetAttribute(&mnr, cudaDevAttrComputeCapabilityMinor, dev);
+        d.cc = maj * 10 + mnr;
+    }
+    return d;
+}
+
+// ------------------------------- TMA descriptors ---------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// 3-D fp32 map {d0 (contiguous), d1, d2} with byte strides s1, s2 and box {b0, b1, 1}.
+bool encode_3d(CUtensorMap* m, const float* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1,
+               uint64_t s2, uint32_t b0, uint32_t b1, int swizzle_bytes) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {d0, d1, d2};
+    cuuint64_t strides[2] = {s1, s2};
+    cuuint32_t box[3] = {b0, b1, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    CUtensorMapSwizzle sw = swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                          : swizzle_bytes == 64  ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                 : CU_TENSOR_MAP_SWIZZLE_NONE;
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+uint64_t round16(uint64_t x) { return (x + 15) & ~uint64_t(15); }
+
+// ------------------------------- views -> problem --------------------------------
+struct View {
+    const float* ptr;
+    int64_t d[3];   // batch, rows, cols
+    int64_t s[3];
+};
+
+int to_view(const mt_tensor* t, int want_ndim, const char* name, View& v) {
+    if (!t) return fail(MT_EINVAL, "%s: null tensor", name);
+    if ((int)t->ndim != want_ndim) return fail(MT_EINVAL, "%s: expected a %d-D tensor, got %u-D", name, want_ndim, t->ndim);
+    v.ptr = t->data ? t->data + t->offset : nullptr;
+    if (want_ndim == 2) {
+        v.d[0] = 1; v.s[0] = 0;
+        v.d[1] = (int64_t)t->shape[0]; v.s[1] = (int64_t)t->strides[0];
+        v.d[2] = (int64_t)t->shape[1]; v.s[2] = (int64_t)t->strides[1];
+    } else {
+        for (int i = 0; i < 3; ++i) { v.d[i] = (int64_t)t->shape[i]; v.s[i] = (int64_t)t->strides[i]; }
+    }
+    if (v.d[1] * v.d[2] * v.d[0] > 0 && !t->data) return fail(MT_EINVAL, "%s: null data pointer", name);
+    return MT_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// ------------------------------- launchers ---------------------------------------
+int launch_simt(const GemmProblem& p, cudaStream_t st) {
+    using namespace mt;
+    int la = kLdGeneric, lb = kLdGeneric;
+    const bool okA = aligned16(p.A) && ((p.batch == 1 || p.sa_b % 4 == 0));
+    const bool okB = aligned16(p.B) && ((p.batch == 1 || p.sb_b % 4 == 0));
+    if (okA && p.sa_k == 1 && p.sa_m % 4 == 0) la = kLdKContigVec;
+    else if (okA && p.sa_m == 1 && p.sa_k % 4 == 0) la = kLdMNContigVec;
+    if (okB && p.sb_n == 1 && p.sb_k % 4 == 0) lb = kLdMNContigVec;
+    else if (okB && p.sb_k == 1 && p.sb_n % 4 == 0) lb = kLdKContigVec;
+    dim3 grid((unsigned)((p.N + simt::BN - 1) / simt::BN), (unsigned)((p.M + simt::BM - 1) / simt::BM),
+              (unsigned)p.batch);
+    if (grid.y > 65535 || grid.z > 65535) return fail(MT_EUNSUPPORTED, "simt: grid too large (M=%lld batch=%lld)",
+                                                      (long long)p.M, (long long)p.batch);
+#define MT_SIMT_CASE(LA, LB) \
+    if (la == LA && lb == LB) simt::gemm_kernel<LA, LB><<<grid, simt::THREADS, 0, st>>>(p);
+    MT_SIMT_CASE(kLdKContigVec, kLdMNContigVec)
+    else MT_SIMT_CASE(kLdKContigVec, kLdKContigVec)
+    else MT_SIMT_CASE(kLdKContigVec, kLdGeneric)
+    else MT_SIMT_CASE(kLdMNContigVec, kLdMNContigVec)
+    else MT_SIMT_CASE(kLdMNContigVec, kLdKContigVec)
+    else MT_SIMT_CASE(kLdMNContigVec, kLdGeneric)
+    else MT_SIMT_CASE(kLdGeneric, kLdMNContigVec)
+    else MT_SIMT_CASE(kLdGeneric, kLdKContigVec)
+    else MT_SIMT_CASE(kLdGeneric, kLdGeneric)
+#undef MT_SIMT_CASE
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess && e != cudaErrorStreamCaptureUnsupported) return cuda_fail(e, "simt gemm launch");
+    g_launches.fetch_add(1);
+    static const char* names[3] = {"K", "MN", "gen"};
+    t_path = std::string("simt_fp32 a=") + names[la] + " b=" + names[lb];
+    return MT_OK;
+}
+
+template <int BN, int SWB, bool AMN, bool BMN, bool X3, int STAGES>
+int launch_umma_inst(const CUtensorMap& ta, const CUtensorMap& tb, const mt::umma::Params& up, int grid,
+                     cudaStream_t st) {
+    using G = mt::umma::Cfg<BN, SWB, X3, STAGES>;
+    auto kern = mt::umma::gemm_kernel<BN, SWB, AMN, BMN, X3, STAGES>;
+    static std::atomic<uint64_t> attr_set_mask{0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(attr_set_mask.load() & bit)) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)G::SMEM_BYTES);
+        if (e != cudaSuccess) return cuda_fail(e, "umma gemm: set smem attribute");
+        attr_set_mask.fetch_or(bit);
+    }
+    kern<<<grid, G::THREADS, G::SMEM_BYTES, st>>>(ta, tb, up);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess && e != cudaErrorStreamCaptureUnsupported) return cuda_fail(e, "umma gemm launch");
+    g_launches.fetch_add(1);
+    return MT_OK;
+}
+
+// Returns MT_OK when launched, MT_EUNSUPPORTED when the views do not fit the tensor-core
+// kernel (the caller then uses the SIMT kernel).
+int launch_umma(const GemmProblem& p, bool x3, cudaStream_t st) {
+    DevInfo di = dev_info();
+    if (di.cc != 100) return fail(MT_EUNSUPPORTED, "umma: device is sm_%d, kernel built for sm_100a", di.cc);
+    if (p.M > INT32_MAX || p.N > INT32_MAX || p.K > INT32_MAX || p.batch > INT32_MAX)
+        return fail(MT_EUNSUPPORTED, "umma: extent beyond 2^31");
+    // Output: unit stride along n, 4-byte element rows.
+    if (p.sc_n != 1 && !(p.N == 1)) return fail(MT_EUNSUPPORTED, "umma: C needs unit n-stride");
+    // Operand A: K-major needs sa_k == 1; M-major needs sa_m == 1. Strides multiple of 16 B.
+    auto mult4 = [](int64_t s) { return s % 4 == 0; };
+    const bool a_batched = p.batch > 1 && p.sa_b != 0;
+    const bool b_batched = p.batch > 1 && p.sb_b != 0;
+    if (!aligned16(p.A) || !aligned16(p.B)) return fail(MT_EUNSUPPORTED, "umma: operand not 16-byte aligned");
+    if (a_batched && !mult4(p.sa_b)) return fail(MT_EUNSUPPORTED, "umma: A batch stride");
+    if (b_batched && !mult4(p.sb_b)) return fail(MT_EUNSUPPORTED, "umma: B batch stride");
+    int a_mn = -1, b_mn = -1;
+    if ((p.sa_k == 1 || p.K == 1) && (p.M == 1 || mult4(p.sa_m))) a_mn = 0;
+    else if ((p.sa_m == 1 || p.M == 1) && (p.K == 1 || mult4(p.sa_k))) a_mn = 1;
+    if ((p.sb_n == 1 || p.N == 1) && (p.K == 1 || mult4(p.sb_k))) b_mn = 1;
+    else if ((p.sb_k == 1 || p.K == 1) && (p.N == 1 || mult4(p.sb_n))) b_mn = 0;
+    if (a_mn < 0 || b_mn < 0) return fail(MT_EUNSUPPORTED, "umma: operand strides not TMA-expressible");
+
+    const int swb = x3 ? 64 : 128;
+    const uint32_t bke = swb / 4, chunk = swb / 4;
+    const int64_t tiles_m = (p.M + 127) / 128;
+    const bool small = tiles_m * ((p.N + 255) / 256) * p.batch < (int64_t)di.sms || p.N <= 128;
+    const int bn = small ? 128 : 256;
+
+    // Sizes of unit dims get a harmless 16-byte stride.
+    auto st_or = [](int64_t extent, int64_t stride_elems, uint64_t fallback_bytes) -> uint64_t {
+        return extent > 1 ? (uint64_t)stride_elems * 4 : fallback_bytes;
+    };
+    CUtensorMap ta, tb;
+    bool ok;
+    if (a_mn == 0) {   // dims {K, M, batch}
+        uint64_t s1 = st_or(p.M, p.sa_m, round16(p.K * 4));
+        uint64_t s2 = a_batched ? (uint64_t)p.sa_b * 4 : round16(s1 * p.M);
+        ok = encode_3d(&ta, p.A, p.K, p.M, a_batched ? p.batch : 1, s1, s2, bke, 128, swb);
+    } else {           // dims {M, K, batch}
+        uint64_t s1 = st_or(p.K, p.sa_k, round16(p.M * 4));
+        uint64_t s2 = a_batched ? (uint64_t)p.sa_b * 4 : round16(s1 * p.K);
+        ok = encode_3d(&ta, p.A, p.M, p.K, a_batched ? p.batch : 1, s1, s2, chunk, bke, swb);
+    }
+    if (!ok) return fail(MT_EUNSUPPORTED, "umma: A tensor map rejected");
+    if (b_mn == 0) {   // dims {K, N, batch}
+        uint64_t s1 = st_or(p.N, p.sb_n, round16(p.K * 4));
+        uint64_t s2 = b_batched ? (uint64_t)p.sb_b * 4 : round16(s1 * p.N);
+        ok = encode_3d(&tb, p.B, p.K, p.N, b_batched ? p.batch : 1, s1, s2, bke, bn, swb);
+    } else {           // dims {N, K, batch}
+        uint64_t s1 = st_or(p.K, p.sb_k, round16(p.N * 4));
+        uint64_t s2 = b_batched ? (uint64_t)p.sb_b * 4 : round16(s1 * p.K);
+        ok = encode_3d(&tb, p.B, p.N, p.K, b_batched ? p.batch : 1, s1, s2, chunk, bke, swb);
+    }
+    if (!ok) return fail(MT_EUNSUPPORTED, "umma: B tensor map rejected");
+
+    mt::umma::Params up;
+    up.M = (int)p.M; up.N = (int)p.N; up.K = (int)p.K; up.batch = (int)p.batch;
+    up.a_batched = a_batched; up.b_batched = b_batched;
+    up.C = p.C; up.sc_b = p.sc_b; up.sc_m = p.sc_m;
+    up.bias = p.bias; up.epi = p.epi;
+    up.vec_store = aligned16(p.C) && p.sc_m % 4 == 0 && (p.batch == 1 || p.sc_b % 4 == 0) && p.N % 4 == 0;
+    up.tiles_m = (int)tiles_m;
+    up.tiles_n = (int)((p.N + bn - 1) / bn);
+    up.num_tiles = (long long)up.tiles_m * up.tiles_n * p.batch;
+    const int grid = (int)std::min<long long>(up.num_tiles, (long long)di.sms);
+
+    int rc;
+#define MT_UMMA_DISPATCH(BN_, SWB_, X3_, ST_)                                                       \
+    if (a_mn == 0 && b_mn == 0) rc = launch_umma_inst<BN_, SWB_, false, false, X3_, ST_>(ta, tb, up, grid, st); \
+    else if (a_mn == 0 && b_mn == 1) rc = launch_umma_inst<BN_, SWB_, false, true, X3_, ST_>(ta, tb, up, grid, st); \
+    else if (a_mn == 1 && b_mn == 0) rc = launch_umma_inst<BN_, SWB_, true, false, X3_, ST_>(ta, tb, up, grid, st); \
+    else rc = launch_umma_inst<BN_, SWB_, true, true, X3_, ST_>(ta, tb, up, grid, st);
+    if (!x3) {
+        if (bn == 256) { MT_UMMA_DISPATCH(256, 128, false, 4) }
+        else { MT_UMMA_DISPATCH(128, 128, false, 6) }
+    } else {
+        if (bn == 256) { MT_UMMA_DISPATCH(256, 64, true, 4) }
+        else { MT_UMMA_DISPATCH(128, 64, true, 6) }
+    }
+#undef MT_UMMA_DISPATCH
+    if (rc == MT_OK) {
+        char buf[96];
+        snprintf(buf, sizeof buf, "umma_%s bn=%d a=%s b=%s", x3 ? "tf32x3" : "tf32", bn, a_mn ? "MN" : "K",
+                 b_mn ? "MN" : "K");
+        t_path = buf;
+    }
+    return rc;
+}
+
+int run_gemm(GemmProblem p, int mode, cudaStream_t st) {
+    if (p.M == 0 || p.N == 0 || p.batch == 0) { t_path = "empty"; return MT_OK; }
+    if ((p.epi & (MT_EPI_BIAS_ROW | MT_EPI_BIAS_COL)) && !p.bias) return fail(MT_EINVAL, "bias epilogue without bias");
+    if (p.K == 0) {
+        int blocks = (int)std::min<int64_t>((p.batch * p.M * p.N + 255) / 256, 4096);
+        mt::simt::fill_epilogue_kernel<<<blocks, 256, 0, st>>>(p);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess && e != cudaErrorStreamCaptureUnsupported) return cuda_fail(e, "fill launch");
+        g_launches.fetch_add(1);
+        t_path = "fill_k0";
+        return MT_OK;
+    }
+    mode = resolve_mode(mode);
+    // Column-major output: compute C^T = B^T A^T so the kernel always writes rows.
+    if (p.sc_n != 1 && p.sc_m == 1 && mode != MT_STRICT_FP32) {
+        GemmProblem q = p;
+        q.A = p.B; q.sa_b = p.sb_b; q.sa_m = p.sb_n; q.sa_k = p.sb_k;
+        q.B = p.A; q.sb_b = p.sa_b; q.sb_k = p.sa_k; q.sb_n = p.sa_m;
+        q.sc_m = p.sc_n; q.sc_n = 1;
+        q.M = p.N; q.N = p.M;
+        q.epi = (p.epi & MT_EPI_RELU) | ((p.epi & MT_EPI_BIAS_ROW) ? MT_EPI_BIAS_COL : 0) |
+                ((p.epi & MT_EPI_BIAS_COL) ? MT_EPI_BIAS_ROW : 0);
+        p = q;
+    }
+    if (mode != MT_STRICT_FP32) {
+        std::string saved = t_err;
+        int rc = launch_umma(p, mode == MT_TF32X3, st);
+        if (rc == MT_OK) return MT_OK;
+        if (rc != MT_EUNSUPPORTED) return rc;
+        t_err = saved;   // not an error: the SIMT kernel serves this view
+    }
+    return launch_simt(p, st);
+}
+
+int gemm_from_views(const View& a, const View& b, const View& c, const float* bias, int epi, int mode,
+                    void* stream) {
+    GemmProblem p;
+    p.A = a.ptr; p.sa_b = a.s[0]; p.sa_m = a.s[1]; p.sa_k = a.s[2];
+    p.B = b.ptr; p.sb_b = b.s[0]; p.sb_k = b.s[1]; p.sb_n = b.s[2];
+    p.C = const_cast<float*>(c.ptr); p.sc_b = c.s[0]; p.sc_m = c.s[1]; p.sc_n = c.s[2];
+    p.M = a.d[1]; p.K = a.d[2]; p.N = b.d[2]; p.batch = c.d[0];
+    p.bias = bias; p.epi = epi;
+    if (p.batch > 1 && p.sc_b == 0) return fail(MT_EINVAL, "C must not be a broadcast view");
+    return run_gemm(p, mode, static_cast<cudaStream_t>(stream));
+}
+
+// include/TensorOps.hpp:993-1005 checks: 2-D operands, A.K == B.K; plus C's shape.
+int matmul_2d(const mt_tensor* A, const mt_tensor* B, const mt_tensor* C, void* stream, const char* who) {
+    View a, b, c;
+    int rc;
+    if ((rc = to_view(A, 2, who, a)) || (rc = to_view(B, 2, who, b)) || (rc = to_view(C, 2, who, c))) return rc;
+    if (a.d[2] != b.d[1]) return fail(MT_EINVAL, "%s: Dimension mismatch: A columns must match B rows.", who);
+    if (c.d[1] != a.d[1] || c.d[2] != b.d[2])
+        return fail(MT_EINVAL, "%s: C must be [%lld,%lld]", who, (long long)a.d[1], (long long)b.d[2]);
+    return gemm_from_views(a, b, c, nullptr, MT_EPI_NONE, MT_MODE_DEFAULT, stream);
+}
+
+}  // namespace
+
+extern "C" {
+
+MT_API int mt_matmul_gpu(const mt_tensor* A, const mt_tensor* B, const mt_tensor* C, void* stream) {
+    return matmul_2d(A, B, C, stream, "matmul_gpu");
+}
+MT_API int mt_matmul_gpu_strided(const mt_tensor* A, const mt_tensor* B, const mt_tensor* C, void* stream) {
+    return matmul_2d(A, B, C, stream, "matmul_gpu_strided");
+}
+MT_API int mt_matmul_gpu_v2(const mt_tensor* A, const mt_tensor* B, const mt_tensor* C, void* stream) {
+    return matmul_2d(A, B, C, stream, "matmul_gpu_v2");
+}
+MT_API int mt_matmul_gpu_bk16(const mt_tensor* A, const mt_tensor* B, const mt_tensor* C, void* stream) {
+    return matmul_2d(A, B, C, stream, "matmul_gpu_bk16");
+}
+
+// include/TensorOps.hpp:937-943 checks: 3-D, equal batch, A.K == B.K.
+MT_API int mt_bmm_gpu(const mt_tensor* A, const mt_tensor* B, const mt_tensor* C, void* stream) {
+    View a, b, c;
+    int rc;
+    if ((rc = to_view(A, 3, "bmm", a)) || (rc = to_view(B, 3, "bmm", b)) || (rc = to_view(C, 3, "bmm", c))) return rc;
+    if (a.d[0] != b.d[0]) return fail(MT_EINVAL, "bmm: batch dimension mismatch.");
+    if (a.d[2] != b.d[1]) return fail(MT_EINVAL, "bmm: inner dimension mismatch (A.K != B.K).");
+    if (c.d[0] != a.d[0] || c.d[1] != a.d[1] || c.d[2] != b.d[2]) return fail(MT_EINVAL, "bmm: C shape mismatch");
+    if (a.d[0] == 1) { a.s[0] = 0; b.s[0] = 0; c.s[0] = 0; }
+    return gemm_from_views(a, b, c, nullptr, MT_EPI_NONE, MT_MODE_DEFAULT, stream);
+}
+
+MT_API int mt_linear_fwd_gpu(const mt_tensor* X, const mt_tensor* W, const mt_tensor* bias, const mt_tensor* Y,
+                             int relu, void* stream) {
+    View x, w, y;
+    int rc;
+    if ((rc = to_view(X, 2, "linear", x)) || (rc = to_view(W, 2, "linear", w)) || (rc = to_view(Y, 2, "linear", y)))
+        return rc;
+    if (x.d[2] != w.d[1]) return fail(MT_EINVAL, "linear: x features (%lld) != weight in (%lld)", (long long)x.d[2], (long long)w.d[1]);
+    if (y.d[1] != x.d[1] || y.d[2] != w.d[2]) return fail(MT_EINVAL, "linear: Y shape mismatch");
+    const float* bp = nullptr;
+    if (bias) {
+        uint64_t n = 1;
+        for (uint32_t i = 0; i < bias->ndim; ++i) n *= bias->shape[i];
+        if ((int64_t)n != w.d[2]) return fail(MT_EINVAL, "linear: bias must hold out_features elements");
+        if (bias->ndim >= 1 && bias->strides[bias->ndim - 1] != 1 && n > 1)
+            return fail(MT_EINVAL, "linear: bias must be contiguous");
+        bp = bias->data + bias->offset;
+    }
+    int epi = (bp ? MT_EPI_BIAS_COL : 0) | (relu ? MT_EPI_RELU : 0);
+    return gemm_from_views(x, w, y, bp, epi, MT_MODE_DEFAULT, stream);
+}
+
+MT_API int mt_gemm(const mt_tensor* A, const mt_tensor* B, const mt_tensor* C, const float* bias, int epi, int mode,
+                   void* stream) {
+    if (!A || !B || !C) return fail(MT_EINVAL, "gemm: null tensor");
+    int nd = (int)C->ndim;
+    if (nd != 2 && nd != 3) return fail(MT_EINVAL, "gemm: 2-D or 3-D views only");
+    if (mode < MT_MODE_DEFAULT || mode > MT_TF32X3) return fail(MT_EINVAL, "gemm: bad mode %d", mode);
+    if (epi & ~7) return fail(MT_EINVAL, "gemm: bad epilogue flags %d", epi);
+    View a, b, c;
+    int rc;
+    if ((rc = to_view(A, nd, "gemm A", a)) || (rc = to_view(B, nd, "gemm B", b)) || (rc = to_view(C, nd, "gemm C", c)))
+        return rc;
+    if (a.d[0] != c.d[0] || b.d[0] != c.d[0]) return fail(MT_EINVAL, "gemm: batch mismatch");
+    if (a.d[2] != b.d[1]) return fail(MT_EINVAL, "gemm: inner dimension mismatch (A.K != B.K)");
+    if (c.d[1] != a.d[1] || c.d[2] != b.d[2]) return fail(MT_EINVAL, "gemm: C shape mismatch");
+    if (c.d[0] == 1) { a.s[0] = 0; b.s[0] = 0; c.s[0] = 0; }
+    return gemm_from_views(a, b, c, bias, epi, mode, stream);
+}
+
+MT_API int mt_set_default_mode(int mode) {
+    int prev = resolve_mode(MT_MODE_DEFAULT);
+    if (mode >= MT_STRICT_FP32 && mode <= MT_TF32X3) g_default_mode.store(mode);
+    return prev;
+}
+MT_API int mt_get_default_mode(void) { return resolve_mode(MT_MODE_DEFAULT); }
+MT_API const char* mt_last_error(void) { return t_err.c_str(); }
+MT_API const char* mt_last_path(void) { return t_path.c_str(); }
+MT_API uint64_t mt_launch_count(void) { return g_launches.load(); }
+
+MT_API int mt_device_status(int reset) {
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return -cuda_fail(e, "device_status sync");
+    int v = 0;
+    e = cudaMemcpyFromSymbol(&v, mt::g_dev_status, sizeof(int));
+    if (e != cudaSuccess) return -cuda_fail(e, "device_status read");
+    if (reset) {
+        int z = 0;
+        cudaMemcpyToSymbol(mt::g_dev_status, &z, sizeof(int));
+    }
+    return v;
+}
+
+MT_API const char* mt_version(void) { return "minitensor_b200 mtgemm 0.1 (sm_100a)"; }
+
+}  // extern "C"

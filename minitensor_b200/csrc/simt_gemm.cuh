@@ -1,0 +1,219 @@
+// simt_gemm.cuh -- FFMA-only fp32 GEMM: the strict-fp32 mode and the path for shapes or
+// views the tensor-core kernel cannot take (unaligned views, tiny problems).
+//
+// C[b,m,n] = epi( sum_k A[b,m,k] * B[b,k,n] ), every operand an arbitrary strided view
+// (element strides; batch stride 0 = broadcast operand, as produced by expand()).
+// Each output element is accumulated over k in ascending order in one fp32 register,
+// the order of the reference's matmul_cpu (include/TensorOps.hpp:150-159), with FFMA.
+//
+// Tile 128x128x8, 256 threads, 8x8 outputs per thread (two 4x4 quadrants 64 apart so the
+// shared-memory reads are conflict-free float4 broadcasts), register-staged double
+// buffering of the next k-tile, 128-bit global loads when the contiguous dimension and
+// the view alignment allow them.
+#pragma once
+
+#include "mt_common.cuh"
+
+namespace mt {
+
+struct GemmProblem {
+    const float* A; int64_t sa_b, sa_m, sa_k;
+    const float* B; int64_t sb_b, sb_k, sb_n;
+    float* C;       int64_t sc_b, sc_m, sc_n;
+    int64_t M, N, K, batch;
+    const float* bias;   // may be null
+    int epi;             // MT_EPI_* flags
+};
+
+enum : int { kEpiBiasRow = 1, kEpiBiasCol = 2, kEpiRelu = 4 };
+
+// Loader layouts for the A tile (BM x BK) and the B tile (BK x BN).
+enum : int { kLdKContigVec = 0, kLdMNContigVec = 1, kLdGeneric = 2 };
+
+namespace simt {
+constexpr int BM = 128, BN = 128, BK = 8, THREADS = 256;
+
+__device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+
+// Each thread fetches 4 elements of the A tile into registers.
+template <int LA>
+__device__ __forceinline__ void load_a(const GemmProblem& p, const float* A, int64_t m0, int64_t k0, int t,
+                                       float (&v)[4]) {
+    if (LA == kLdMNContigVec) {
+        // 8 k-rows x 32 float4 along m.
+        int k = t >> 5, mq = (t & 31) * 4;
+        int64_t gk = k0 + k, gm = m0 + mq;
+        if (gk < p.K && gm + 3 < p.M) {
+            float4 x = ldg4(A + gm + gk * p.sa_k);
+            v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                v[i] = (gk < p.K && gm + i < p.M) ? __ldg(A + (gm + i) + gk * p.sa_k) : 0.f;
+        }
+    } else {
+        // 128 m-rows x 2 groups of 4 consecutive k.
+        int m = t >> 1, kq = (t & 1) * 4;
+        int64_t gm = m0 + m, gk = k0 + kq;
+        if (LA == kLdKContigVec && gm < p.M && gk + 3 < p.K) {
+            float4 x = ldg4(A + gm * p.sa_m + gk);
+            v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                v[i] = (gm < p.M && gk + i < p.K) ? __ldg(A + gm * p.sa_m + (gk + i) * p.sa_k) : 0.f;
+        }
+    }
+}
+
+template <int LA>
+__device__ __forceinline__ void store_a(float (*As)[BM], int t, const float (&v)[4]) {
+    if (LA == kLdMNContigVec) {
+        int k = t >> 5, mq = (t & 31) * 4;
+        *reinterpret_cast<float4*>(&As[k][mq]) = make_float4(v[0], v[1], v[2], v[3]);
+    } else {
+        int m = t >> 1, kq = (t & 1) * 4;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) As[kq + i][m] = v[i];
+    }
+}
+
+// B loaders: kLdMNContigVec = contiguous along n (row-major B), kLdKContigVec =
+// contiguous along k (a transposed view).
+template <int LB>
+__device__ __forceinline__ void load_b(const GemmProblem& p, const float* B, int64_t k0, int64_t n0, int t,
+                                       float (&v)[4]) {
+    if (LB == kLdKContigVec) {
+        int n = t >> 1, kq = (t & 1) * 4;
+        int64_t gn = n0 + n, gk = k0 + kq;
+        if (gn < p.N && gk + 3 < p.K) {
+            float4 x = ldg4(B + gn * p.sb_n + gk);
+            v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                v[i] = (gn < p.N && gk + i < p.K) ? __ldg(B + gn * p.sb_n + (gk + i) * p.sb_k) : 0.f;
+        }
+    } else {
+        int k = t >> 5, nq = (t & 31) * 4;
+        int64_t gk = k0 + k, gn = n0 + nq;
+        if (LB == kLdMNContigVec && gk < p.K && gn + 3 < p.N) {
+            float4 x = ldg4(B + gk * p.sb_k + gn);
+            v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                v[i] = (gk < p.K && gn + i < p.N) ? __ldg(B + gk * p.sb_k + (gn + i) * p.sb_n) : 0.f;
+        }
+    }
+}
+
+template <int LB>
+__device__ __forceinline__ void store_b(float (*Bs)[BN], int t, const float (&v)[4]) {
+    if (LB == kLdKContigVec) {
+        int n = t >> 1, kq = (t & 1) * 4;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) Bs[kq + i][n] = v[i];
+    } else {
+        int k = t >> 5, nq = (t & 31) * 4;
+        *reinterpret_cast<float4*>(&Bs[k][nq]) = make_float4(v[0], v[1], v[2], v[3]);
+    }
+}
+
+__device__ __forceinline__ float epilogue(float acc, const GemmProblem& p, int64_t m, int64_t n) {
+    if (p.epi & kEpiBiasCol) acc = acc + __ldg(p.bias + n);
+    if (p.epi & kEpiBiasRow) acc = acc + __ldg(p.bias + m);
+    if (p.epi & kEpiRelu) acc = acc > 0.f ? acc : 0.f;
+    return acc;
+}
+
+template <int LA, int LB>
+__global__ void __launch_bounds__(THREADS) gemm_kernel(GemmProblem p) {
+    __shared__ __align__(16) float As[2][BK][BM];
+    __shared__ __align__(16) float Bs[2][BK][BN];
+
+    const int t = threadIdx.x;
+    const int tx = t & 15, ty = t >> 4;
+    const int64_t b = blockIdx.z;
+    const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;
+    const float* A = p.A + b * p.sa_b;
+    const float* B = p.B + b * p.sb_b;
+    float* C = p.C + b * p.sc_b;
+
+    float acc[8][8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+
+    float ra[4], rb[4];
+    const int64_t ktiles = (p.K + BK - 1) / BK;
+    if (ktiles > 0) {
+        load_a<LA>(p, A, m0, 0, t, ra);
+        load_b<LB>(p, B, 0, n0, t, rb);
+        store_a<LA>(As[0], t, ra);
+        store_b<LB>(Bs[0], t, rb);
+    }
+    __syncthreads();
+
+    for (int64_t kt = 0; kt < ktiles; ++kt) {
+        const int cur = (int)(kt & 1);
+        const bool more = kt + 1 < ktiles;
+        if (more) {
+            load_a<LA>(p, A, m0, (kt + 1) * BK, t, ra);
+            load_b<LB>(p, B, (kt + 1) * BK, n0, t, rb);
+        }
+#pragma unroll
+        for (int k = 0; k < BK; ++k) {
+            float4 a0 = *reinterpret_cast<const float4*>(&As[cur][k][ty * 4]);
+            float4 a1 = *reinterpret_cast<const float4*>(&As[cur][k][ty * 4 + 64]);
+            float4 b0 = *reinterpret_cast<const float4*>(&Bs[cur][k][tx * 4]);
+            float4 b1 = *reinterpret_cast<const float4*>(&Bs[cur][k][tx * 4 + 64]);
+            const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[i][j] = __fmaf_rn(av[i], bv[j], acc[i][j]);
+        }
+        if (more) {
+            store_a<LA>(As[cur ^ 1], t, ra);
+            store_b<LB>(Bs[cur ^ 1], t, rb);
+        }
+        __syncthreads();
+    }
+
+    const bool vec = (p.sc_n == 1) && ((p.sc_m & 3) == 0) && ((reinterpret_cast<uintptr_t>(C) & 15) == 0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int64_t m = m0 + ty * 4 + (i & 3) + (i >> 2) * 64;
+        if (m >= p.M) continue;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int64_t n = n0 + tx * 4 + h * 64;
+            float o[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) o[j] = (n + j < p.N) ? epilogue(acc[i][h * 4 + j], p, m, n + j) : 0.f;
+            if (vec && n + 3 < p.N) {
+                *reinterpret_cast<float4*>(C + m * p.sc_m + n) = make_float4(o[0], o[1], o[2], o[3]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (n + j < p.N) C[m * p.sc_m + (n + j) * p.sc_n] = o[j];
+            }
+        }
+    }
+}
+
+// K == 0: the sum is empty, C = epi(0).
+__global__ void fill_epilogue_kernel(GemmProblem p) {
+    const int64_t total = p.batch * p.M * p.N;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        int64_t b = i / (p.M * p.N), r = i % (p.M * p.N);
+        int64_t m = r / p.N, n = r % p.N;
+        p.C[b * p.sc_b + m * p.sc_m + n * p.sc_n] = epilogue(0.f, p, m, n);
+    }
+}
+
+}  // namespace simt
+}  // namespace mt

@@ -1,0 +1,297 @@
+// umma_gemm.cuh -- the tensor-core fp32-input GEMM for sm_100a (tcgen05 + TMA + TMEM).
+//
+// C[b,m,n] = epi( sum_k A[b,m,k] * B[b,k,n] ) in two precisions:
+//   TF32   -- one kind::tf32 MMA per k-step on the raw fp32 tiles.
+//   TF32X3 -- the split-precision method of Ootomo & Yokota (2022): x = hi + lo with
+//             hi = rna_tf32(x), lo = x - hi; C += Ahi*Bhi + Ahi*Blo + Alo*Bhi, all three
+//             products accumulated in the same fp32 TMEM accumulator.
+//
+// Layout of work. One persistent CTA per SM walks output tiles of 128 x BN. Warp roles:
+//   warp 0      TMA producer: 128-byte- (or 64-byte-) swizzled tiles into a STAGES-deep
+//               shared-memory ring, completion counted on mbarriers (no multicast).
+//   warp 1      TMEM owner and single-thread MMA issuer (tcgen05.mma.cta_group::1).
+//   warps 2-5   epilogue: TMEM -> registers (tcgen05.ld 32x32b) -> bias/ReLU -> global.
+//   warps 6-9   (TF32X3 only) converter: splits each landed stage into hi (in place) and
+//               lo (a parallel ring), then hands the stage to the MMA issuer.
+// The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue of tile i
+// overlaps the main loop of tile i+1.
+//
+// Operand layouts come straight from the views: A is K-major (row-major A) or M-major (a
+// transposed view), B is K-major (a transposed view, e.g. W^T) or N-major (row-major B).
+// The instruction descriptor's major bits select the smem layout, so NN, NT and TN need
+// no copies. Ragged M/N/K edges are zero-filled by TMA and clipped in the epilogue.
+#pragma once
+
+#include "mt_common.cuh"
+
+namespace mt {
+namespace umma {
+
+constexpr int BM = 128;
+
+struct Params {
+    int M, N, K, batch;
+    int a_batched, b_batched;   // operand has a batch dimension in its tensor map
+    float* C;
+    int64_t sc_b, sc_m;         // C element strides (n stride is 1)
+    const float* bias;
+    int epi;
+    int vec_store;              // rows 16-byte aligned and N % 4 == 0
+    int tiles_m, tiles_n;
+    long long num_tiles;
+};
+
+template <int BN, int SWB, bool X3, int STAGES>
+struct Cfg {
+    static constexpr int BKE = SWB / 4;                        // k elements per stage
+    static constexpr uint32_t A_BYTES = BM * BKE * 4;
+    static constexpr uint32_t B_BYTES = BN * BKE * 4;
+    static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int KSTEPS = BKE / 8;                     // tf32 MMA K = 8
+    static constexpr uint32_t TMEM_COLS = 2 * BN;
+    static constexpr int NUM_WARPS = X3 ? 10 : 6;
+    static constexpr int THREADS = NUM_WARPS * 32;
+    static constexpr uint32_t RING_BYTES = STAGE_BYTES * STAGES * (X3 ? 2 : 1);
+    static constexpr uint32_t BAR_BYTES = 8 * (3 * STAGES + 4) + 16;
+    static constexpr uint32_t SMEM_BYTES = 1024 + RING_BYTES + BAR_BYTES;
+    static constexpr uint32_t CHUNK = SWB / 4;                 // MN elements per swizzle atom row
+    // MN-major: one atom column = BKE k-rows x SWB bytes.
+    static constexpr uint32_t MN_CHUNK_BYTES = BKE * SWB;
+};
+
+// Tile t -> (batch, m block, n block); m blocks are grouped by 8 so that consecutive CTAs
+// share B tiles in L2.
+__device__ __forceinline__ void tile_coords(const Params& p, long long t, int& b, int& mb, int& nb) {
+    const long long per_batch = (long long)p.tiles_m * p.tiles_n;
+    b = (int)(t / per_batch);
+    long long r = t % per_batch;
+    constexpr int G = 8;
+    long long group = r / ((long long)G * p.tiles_n);
+    int first_m = (int)(group * G);
+    int gsize = min(p.tiles_m - first_m, G);
+    long long in_group = r % ((long long)G * p.tiles_n);
+    mb = first_m + (int)(in_group % gsize);
+    nb = (int)(in_group / gsize);
+}
+
+template <bool MN_MAJOR, int SWB>
+__device__ __forceinline__ uint64_t operand_desc(uint32_t base, int kstep, uint32_t mn_chunk_bytes) {
+    if (MN_MAJOR) {
+        // k-step of 8 rows = 8 * SWB bytes; LBO = next MN chunk, SBO = next 8-row K group.
+        uint64_t d = umma_desc_sw128(base + kstep * 8 * SWB, mn_chunk_bytes, 8 * SWB);
+        if (SWB == 64) d = (d & ~((uint64_t)7 << 61)) | ((uint64_t)4 << 61);
+        return d;
+    } else {
+        // k-step of 8 tf32 = 32 bytes inside the swizzled row; SBO = 8 rows.
+        uint64_t d = umma_desc_sw128(base + kstep * 32, 16, 8 * SWB);
+        if (SWB == 64) d = (d & ~((uint64_t)7 << 61)) | ((uint64_t)4 << 61);
+        return d;
+    }
+}
+
+template <int BN, int SWB, bool A_MN, bool B_MN, bool X3, int STAGES>
+__global__ void __launch_bounds__(Cfg<BN, SWB, X3, STAGES>::THREADS, 1)
+gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
+    using G = Cfg<BN, SWB, X3, STAGES>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* ring = smem;                                      // [STAGES][A|B]
+    uint8_t* ring_lo = smem + G::STAGE_BYTES * STAGES;         // X3: [STAGES][Alo|Blo]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + G::RING_BYTES);
+    uint64_t* full = bars;                                     // TMA landed
+    uint64_t* empty = bars + STAGES;                           // MMA done with stage
+    uint64_t* conv = bars + 2 * STAGES;                        // X3: split done
+    uint64_t* acc_full = bars + 3 * STAGES;                    // [2]
+    uint64_t* acc_empty = bars + 3 * STAGES + 2;               // [2]
+    volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(bars + 3 * STAGES + 4);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 3 * STAGES + 4) + 1;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long first_tile = blockIdx.x, tile_step = gridDim.x;
+    const int kblocks = (p.K + G::BKE - 1) / G::BKE;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(smem_u32(&full[s]), 1);
+            mbar_init(smem_u32(&empty[s]), 1);
+            mbar_init(smem_u32(&conv[s]), 128);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(smem_u32(&acc_full[a]), 1);
+            mbar_init(smem_u32(&acc_empty[a]), 128);
+        }
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32((const void*)tmem_slot), G::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------ TMA producer ------------------------------
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            for (long long t = first_tile; t < p.num_tiles; t += tile_step) {
+                int b, mb, nb;
+                tile_coords(p, t, b, mb, nb);
+                const int m0 = mb * BM, n0 = nb * BN;
+                const int ab = p.a_batched ? b : 0, bb = p.b_batched ? b : 0;
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!mbar_wait(smem_u32(&empty[s]), ph ^ 1, abort_flag, kDevTimeoutEmpty)) goto done;
+                    const uint32_t bar = smem_u32(&full[s]);
+                    mbar_arrive_expect_tx(bar, G::STAGE_BYTES);
+                    const uint32_t sa = smem_u32(ring + s * G::STAGE_BYTES);
+                    const uint32_t sb = sa + G::A_BYTES;
+                    const int k0 = kb * G::BKE;
+                    if (A_MN) {
+#pragma unroll
+                        for (int c = 0; c < BM / (int)G::CHUNK; ++c)
+                            tma_load_3d(sa + c * G::MN_CHUNK_BYTES, &tmA, bar, m0 + c * G::CHUNK, k0, ab);
+                    } else {
+                        tma_load_3d(sa, &tmA, bar, k0, m0, ab);
+                    }
+                    if (B_MN) {
+#pragma unroll
+                        for (int c = 0; c < BN / (int)G::CHUNK; ++c)
+                            tma_load_3d(sb + c * G::MN_CHUNK_BYTES, &tmB, bar, n0 + c * G::CHUNK, k0, bb);
+                    } else {
+                        tma_load_3d(sb, &tmB, bar, k0, n0, bb);
+                    }
+                    if (++s == STAGES) { s = 0; ph ^= 1; }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------ MMA issuer --------------------------------
+        if (lane == 0) {
+            constexpr uint32_t idesc = umma_idesc_tf32(BM, BN, A_MN ? 1 : 0, B_MN ? 1 : 0);
+            int s = 0;
+            uint32_t ph = 0;
+            int it = 0;
+            for (long long t = first_tile; t < p.num_tiles; t += tile_step, ++it) {
+                const int a = it & 1;
+                const uint32_t aph = (it >> 1) & 1;
+                if (!mbar_wait(smem_u32(&acc_empty[a]), aph ^ 1, abort_flag, kDevTimeoutAccEmpty)) goto done;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + a * BN;
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    uint32_t wbar = X3 ? smem_u32(&conv[s]) : smem_u32(&full[s]);
+                    if (!mbar_wait(wbar, ph, abort_flag, kDevTimeoutFull)) goto done;
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(ring + s * G::STAGE_BYTES);
+                    const uint32_t sb = sa + G::A_BYTES;
+#pragma unroll
+                    for (int k = 0; k < G::KSTEPS; ++k) {
+                        const uint64_t ad = operand_desc<A_MN, SWB>(sa, k, G::MN_CHUNK_BYTES);
+                        const uint64_t bd = operand_desc<B_MN, SWB>(sb, k, G::MN_CHUNK_BYTES);
+                        const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+                        if (X3) {
+                            const uint32_t la = smem_u32(ring_lo + s * G::STAGE_BYTES);
+                            const uint32_t lb = la + G::A_BYTES;
+                            const uint64_t ald = operand_desc<A_MN, SWB>(la, k, G::MN_CHUNK_BYTES);
+                            const uint64_t bld = operand_desc<B_MN, SWB>(lb, k, G::MN_CHUNK_BYTES);
+                            umma_tf32(d_tmem, ald, bd, idesc, acc);   // Alo * Bhi
+                            umma_tf32(d_tmem, ad, bld, idesc, 1u);    // Ahi * Blo
+                            umma_tf32(d_tmem, ad, bd, idesc, 1u);     // Ahi * Bhi
+                        } else {
+                            umma_tf32(d_tmem, ad, bd, idesc, acc);
+                        }
+                    }
+                    umma_commit(smem_u32(&empty[s]));
+                    if (++s == STAGES) { s = 0; ph ^= 1; }
+                }
+                umma_commit(smem_u32(&acc_full[a]));
+            }
+        }
+    } else if (warp < 6) {
+        // ------------------------------ epilogue ----------------------------------
+        const int q = warp & 3;   // TMEM lane quarter this warp may access
+        int it = 0;
+        for (long long t = first_tile; t < p.num_tiles; t += tile_step, ++it) {
+            int b, mb, nb;
+            tile_coords(p, t, b, mb, nb);
+            const int a = it & 1;
+            const uint32_t aph = (it >> 1) & 1;
+            if (!mbar_wait(smem_u32(&acc_full[a]), aph, abort_flag, kDevTimeoutAccFull)) goto done;
+            __syncwarp();   // tcgen05.ld below is .sync.aligned: reconverge after the spin
+            tc_fence_after();
+            const int m = mb * BM + q * 32 + lane;
+            float* crow = p.C + (int64_t)b * p.sc_b + (int64_t)m * p.sc_m;
+            const float bias_row = (p.epi & 1) && m < p.M ? __ldg(p.bias + m) : 0.f;
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + a * BN + c * 32, r);
+                tmem_ld_wait();
+                if (c == BN / 32 - 1) {
+                    tc_fence_before();
+                    mbar_arrive(smem_u32(&acc_empty[a]));
+                }
+                const int n0 = nb * BN + c * 32;
+                float v[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    float x = __uint_as_float(r[j]) + bias_row;
+                    if (p.epi & 2) x = x + ((n0 + j < p.N) ? __ldg(p.bias + n0 + j) : 0.f);
+                    if (p.epi & 4) x = x > 0.f ? x : 0.f;
+                    v[j] = x;
+                }
+                if (m < p.M) {
+                    if (p.vec_store && n0 + 32 <= p.N) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4)
+                            *reinterpret_cast<float4*>(crow + n0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (n0 + j < p.N) crow[n0 + j] = v[j];
+                    }
+                }
+            }
+        }
+    } else if (X3) {
+        // ------------------------------ 3xTF32 splitter ---------------------------
+        const int ct = threadIdx.x - 6 * 32;   // 0..127
+        int s = 0;
+        uint32_t ph = 0;
+        for (long long t = first_tile; t < p.num_tiles; t += tile_step) {
+            for (int kb = 0; kb < kblocks; ++kb) {
+                if (!mbar_wait(smem_u32(&full[s]), ph, abort_flag, kDevTimeoutMisc)) goto done;
+                float4* hi = reinterpret_cast<float4*>(ring + s * G::STAGE_BYTES);
+                float4* lo = reinterpret_cast<float4*>(ring_lo + s * G::STAGE_BYTES);
+#pragma unroll 4
+                for (uint32_t i = ct; i < G::STAGE_BYTES / 16; i += 128) {
+                    float4 x = hi[i];
+                    float4 h = make_float4(tf32_round(x.x), tf32_round(x.y), tf32_round(x.z), tf32_round(x.w));
+                    hi[i] = h;
+                    lo[i] = make_float4(x.x - h.x, x.y - h.y, x.z - h.z, x.w - h.w);
+                }
+                fence_proxy_async_smem();
+                mbar_arrive(smem_u32(&conv[s]));
+                if (++s == STAGES) { s = 0; ph ^= 1; }
+            }
+        }
+    }
+
+done:
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem_base, G::TMEM_COLS);
+    }
+}
+
+}  // namespace umma
+}  // namespace mt

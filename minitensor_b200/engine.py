@@ -1,0 +1,239 @@
+"""Python front of libmtgemm.so -- the reference's GPU GEMM interface, mirrored.
+
+The names, argument meaning and error behaviour follow the reference's C++ entry points
+(include/TensorOps.hpp:703-712 and the dispatchers at :933-1149):
+
+* ``matmul_gpu(A, B, C)`` & co. write into a caller-allocated ``C``; shape errors raise
+  ``ValueError`` (the reference throws ``std::invalid_argument``), CUDA failures raise
+  ``RuntimeError`` (``GPU_CHECK`` throws ``std::runtime_error``).
+* ``matmul(A, B)``, ``bmm(A, B)``, ``linear_forward`` ... allocate the output like the
+  reference dispatchers do.
+
+Tensors are torch CUDA tensors used purely as device memory: each is passed to the C ABI
+as (storage base, view offset, shape, strides) -- the fields of the reference's
+TensorImpl -- so transposed, sliced and expanded (stride-0) views are consumed in place.
+There is no CPU or library fallback: if libmtgemm.so is missing this module raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "libmtgemm.so")
+
+MAX_DIMS = 8
+MT_OK, MT_EINVAL, MT_EUNSUPPORTED, MT_ECUDA, MT_ETIMEOUT, MT_ENOMEM = range(6)
+MODE_DEFAULT, STRICT_FP32, TF32, TF32X3 = -1, 0, 1, 2
+MODES = {"default": MODE_DEFAULT, "strict": STRICT_FP32, "tf32": TF32, "tf32x3": TF32X3}
+EPI_NONE, EPI_BIAS_ROW, EPI_BIAS_COL, EPI_RELU = 0, 1, 2, 4
+
+
+class MtTensor(ctypes.Structure):
+    _fields_ = [
+        ("data", ctypes.c_void_p),
+        ("offset", ctypes.c_uint64),
+        ("ndim", ctypes.c_uint32),
+        ("shape", ctypes.c_uint64 * MAX_DIMS),
+        ("strides", ctypes.c_uint64 * MAX_DIMS),
+    ]
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """Loads libmtgemm.so (built in-tree by ``python -m minitensor_b200.build``)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(f"{LIB_PATH} is missing: build it with `python -m minitensor_b200.build`")
+    L = ctypes.CDLL(LIB_PATH)
+    P = ctypes.POINTER(MtTensor)
+    vp = ctypes.c_void_p
+    for name in ("mt_matmul_gpu", "mt_matmul_gpu_strided", "mt_matmul_gpu_v2", "mt_matmul_gpu_bk16",
+                 "mt_bmm_gpu"):
+        fn = getattr(L, name)
+        fn.argtypes = [P, P, P, vp]
+        fn.restype = ctypes.c_int
+    L.mt_linear_fwd_gpu.argtypes = [P, P, P, P, ctypes.c_int, vp]
+    L.mt_linear_fwd_gpu.restype = ctypes.c_int
+    L.mt_gemm.argtypes = [P, P, P, vp, ctypes.c_int, ctypes.c_int, vp]
+    L.mt_gemm.restype = ctypes.c_int
+    L.mt_set_default_mode.argtypes = [ctypes.c_int]
+    L.mt_set_default_mode.restype = ctypes.c_int
+    L.mt_get_default_mode.restype = ctypes.c_int
+    L.mt_last_error.restype = ctypes.c_char_p
+    L.mt_last_path.restype = ctypes.c_char_p
+    L.mt_launch_count.restype = ctypes.c_uint64
+    L.mt_device_status.argtypes = [ctypes.c_int]
+    L.mt_device_status.restype = ctypes.c_int
+    L.mt_version.restype = ctypes.c_char_p
+    _lib = L
+    return L
+
+
+def view(t: torch.Tensor | None) -> MtTensor | None:
+    """A torch tensor as an mt_tensor: storage base + element offset + shape + strides."""
+    if t is None:
+        return None
+    if t.dtype != torch.float32:
+        raise ValueError(f"expected float32, got {t.dtype}")
+    if t.dim() > MAX_DIMS:
+        raise ValueError("Exceeded MAX_DIMS")
+    v = MtTensor()
+    v.data = t.untyped_storage().data_ptr() if t.numel() else 0
+    v.offset = t.storage_offset()
+    v.ndim = t.dim()
+    for i, (s, st) in enumerate(zip(t.shape, t.stride())):
+        v.shape[i] = s
+        v.strides[i] = st
+    return v
+
+
+def _stream(stream) -> int | None:
+    if stream is None:
+        # torch's current stream (the role of the reference's active_stream()).
+        return torch.cuda.current_stream().cuda_stream if torch.cuda.is_available() else None
+    if isinstance(stream, torch.cuda.Stream):
+        return stream.cuda_stream
+    return int(stream)
+
+
+def _check(rc: int) -> None:
+    if rc == MT_OK:
+        return
+    msg = lib().mt_last_error().decode()
+    if rc == MT_EINVAL:
+        raise ValueError(msg)
+    raise RuntimeError(f"mtgemm status {rc}: {msg}")
+
+
+def _ref(v):
+    return ctypes.byref(v) if v is not None else None
+
+
+def _call3(name, A, B, C, stream):
+    a, b, c = view(A), view(B), view(C)
+    _check(getattr(lib(), name)(_ref(a), _ref(b), _ref(c), _stream(stream)))
+
+
+# ---- the reference's *_gpu entry points (caller-allocated output) --------------------
+
+def matmul_gpu(A, B, C, stream=None):
+    """include/TensorOps.hpp:703."""
+    _call3("mt_matmul_gpu", A, B, C, stream)
+
+
+def matmul_gpu_strided(A, B, C, stream=None):
+    """include/TensorOps.hpp:704."""
+    _call3("mt_matmul_gpu_strided", A, B, C, stream)
+
+
+def matmul_gpu_v2(A, B, C, stream=None):
+    """include/TensorOps.hpp:705."""
+    _call3("mt_matmul_gpu_v2", A, B, C, stream)
+
+
+def matmul_gpu_bk16(A, B, C, stream=None):
+    """include/TensorOps.hpp:706."""
+    _call3("mt_matmul_gpu_bk16", A, B, C, stream)
+
+
+def bmm_gpu(A, B, C, stream=None):
+    """One launch for bmm (include/TensorOps.hpp:933-991); stride-0 batch = broadcast."""
+    _call3("mt_bmm_gpu", A, B, C, stream)
+
+
+def linear_fwd_gpu(X, W, bias, Y, relu=False, stream=None):
+    """Linear<float>::forward (include/Module.hpp:112-114) with the bias add fused."""
+    x, w, b, y = view(X), view(W), view(bias), view(Y)
+    _check(lib().mt_linear_fwd_gpu(_ref(x), _ref(w), _ref(b), _ref(y), int(bool(relu)), _stream(stream)))
+
+
+def gemm(A, B, C, bias=None, epi=EPI_NONE, mode=MODE_DEFAULT, stream=None):
+    """C = epi(A @ B) for 2-D or 3-D views with an explicit precision mode."""
+    if isinstance(mode, str):
+        mode = MODES[mode]
+    a, b, c = view(A), view(B), view(C)
+    bp = bias.data_ptr() if bias is not None else None
+    _check(lib().mt_gemm(_ref(a), _ref(b), _ref(c), bp, int(epi), int(mode), _stream(stream)))
+
+
+# ---- allocating dispatchers (include/TensorOps.hpp:933-1045, include/Module.hpp) ------
+
+def matmul(A, B, mode=MODE_DEFAULT, stream=None):
+    """matmul(A, B) -> C (include/TensorOps.hpp:993-1045)."""
+    if A.device != B.device:
+        raise ValueError("Tensors must be on the same device for matmul.")
+    if A.dim() != 2 or B.dim() != 2:
+        raise ValueError("matmul currently only supports 2D tensors.")
+    if A.shape[1] != B.shape[0]:
+        raise ValueError("Dimension mismatch: A columns must match B rows.")
+    C = torch.empty((A.shape[0], B.shape[1]), dtype=torch.float32, device=A.device)
+    gemm(A, B, C, mode=mode, stream=stream)
+    return C
+
+
+def bmm(A, B, mode=MODE_DEFAULT, stream=None):
+    """bmm(A, B) -> C (include/TensorOps.hpp:933-991), broadcast operands read in place."""
+    if A.device != B.device:
+        raise ValueError("Tensors must be on the same device for bmm.")
+    if A.dim() != 3 or B.dim() != 3:
+        raise ValueError("bmm requires 3D tensors.")
+    if A.shape[0] != B.shape[0]:
+        raise ValueError("bmm: batch dimension mismatch.")
+    if A.shape[2] != B.shape[1]:
+        raise ValueError("bmm: inner dimension mismatch (A.K != B.K).")
+    C = torch.empty((A.shape[0], A.shape[1], B.shape[2]), dtype=torch.float32, device=A.device)
+    gemm(A, B, C, mode=mode, stream=stream)
+    return C
+
+
+def linear_forward(x, W, bias=None, relu=False, mode=MODE_DEFAULT, stream=None):
+    """Linear<float>::forward: x [M,in] @ W [in,out] + bias [1,out] (optional ReLU fused)."""
+    Y = torch.empty((x.shape[0], W.shape[1]), dtype=torch.float32, device=x.device)
+    epi = (EPI_BIAS_COL if bias is not None else 0) | (EPI_RELU if relu else 0)
+    gemm(x, W, Y, bias=bias.reshape(-1) if bias is not None else None, epi=epi, mode=mode, stream=stream)
+    return Y
+
+
+def linear_backward(x, W, dY, mode=MODE_DEFAULT, stream=None):
+    """MatmulBackward for Linear (include/Autograd.hpp:124-141): dX = dY @ W^T and
+    dW = x^T @ dY, both read through transposed views (no copies), plus the bias gradient
+    db = ones[1,M] @ dY (the reference's unbroadcast sum over rows) as a GEMM."""
+    dX = torch.empty_like(x)
+    dW = torch.empty_like(W)
+    gemm(dY, W.t(), dX, mode=mode, stream=stream)
+    gemm(x.t(), dY, dW, mode=mode, stream=stream)
+    ones = torch.ones((1, dY.shape[0]), dtype=torch.float32, device=dY.device)
+    db = torch.empty((1, dY.shape[1]), dtype=torch.float32, device=dY.device)
+    gemm(ones, dY, db, mode=STRICT_FP32, stream=stream)
+    return dX, dW, db
+
+
+# ---- settings and diagnostics ---------------------------------------------------------
+
+def set_default_mode(mode) -> int:
+    if isinstance(mode, str):
+        mode = MODES[mode]
+    return lib().mt_set_default_mode(int(mode))
+
+
+def last_path() -> str:
+    return lib().mt_last_path().decode()
+
+
+def launch_count() -> int:
+    return int(lib().mt_launch_count())
+
+
+def device_status(reset: bool = True) -> int:
+    return int(lib().mt_device_status(1 if reset else 0))
+
+
+def version() -> str:
+    return lib().mt_version().decode()

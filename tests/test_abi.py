@@ -1,0 +1,93 @@
+"""CPU tests of the C ABI boundary: the library loads, exports every function that
+include/*.h declares, and rejects bad arguments with the reference's error semantics
+before touching the device."""
+import ctypes
+import glob
+import os
+import re
+
+import pytest
+import torch
+
+from minitensor_b200 import engine
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    names = []
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        src = open(h).read()
+        names += re.findall(r"MT_API\s+[\w\s\*]+?\b(mt_\w+)\s*\(", src)
+    return sorted(set(names))
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    for n in ("mt_matmul_gpu", "mt_matmul_gpu_strided", "mt_bmm_gpu", "mt_linear_fwd_gpu", "mt_gemm"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = engine.lib()
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_version_and_default_mode():
+    assert "sm_100a" in engine.version()
+    assert engine.lib().mt_get_default_mode() in (0, 1, 2)
+
+
+def _t(*shape):
+    return torch.zeros(shape, dtype=torch.float32)
+
+
+@pytest.mark.parametrize("fn", ["matmul_gpu", "matmul_gpu_strided", "matmul_gpu_v2", "matmul_gpu_bk16"])
+def test_matmul_shape_errors_raise_value_error(fn):
+    # include/TensorOps.hpp:995-1005: std::invalid_argument on mismatched inner dims.
+    with pytest.raises(ValueError, match="Dimension mismatch"):
+        getattr(engine, fn)(_t(2, 3), _t(4, 2), _t(2, 2))
+    with pytest.raises(ValueError, match="2-D"):
+        getattr(engine, fn)(_t(2, 3, 1), _t(3, 2), _t(2, 2))
+    with pytest.raises(ValueError, match="C must be"):
+        getattr(engine, fn)(_t(2, 3), _t(3, 2), _t(3, 3))
+
+
+def test_bmm_shape_errors():
+    # include/TensorOps.hpp:937-943.
+    with pytest.raises(ValueError, match="batch dimension mismatch"):
+        engine.bmm_gpu(_t(2, 3, 4), _t(3, 4, 5), _t(2, 3, 5))
+    with pytest.raises(ValueError, match="inner dimension mismatch"):
+        engine.bmm_gpu(_t(2, 3, 4), _t(2, 5, 5), _t(2, 3, 5))
+    with pytest.raises(ValueError, match="3-D"):
+        engine.bmm_gpu(_t(3, 4), _t(4, 5), _t(3, 5))
+
+
+def test_dispatcher_errors():
+    with pytest.raises(ValueError, match="Dimension mismatch"):
+        engine.matmul(_t(2, 3), _t(2, 3))
+    with pytest.raises(ValueError, match="bmm requires 3D"):
+        engine.bmm(_t(2, 3), _t(3, 2))
+    with pytest.raises(ValueError, match="float32"):
+        engine.view(torch.zeros(2, 2, dtype=torch.float64))
+
+
+def test_gemm_argument_errors():
+    lib = engine.lib()
+    a, b, c = engine.view(_t(2, 3)), engine.view(_t(3, 2)), engine.view(_t(2, 2))
+    rc = lib.mt_gemm(ctypes.byref(a), ctypes.byref(b), ctypes.byref(c), None, 0, 7, None)
+    assert rc == engine.MT_EINVAL and b"bad mode" in lib.mt_last_error()
+    rc = lib.mt_gemm(ctypes.byref(a), ctypes.byref(b), ctypes.byref(c), None, 64, 0, None)
+    assert rc == engine.MT_EINVAL
+    rc = lib.mt_gemm(None, ctypes.byref(b), ctypes.byref(c), None, 0, 0, None)
+    assert rc == engine.MT_EINVAL
+
+
+def test_view_carries_offset_and_strides():
+    base = torch.arange(48, dtype=torch.float32).reshape(6, 8)
+    v = engine.view(base[2:5, 1:7].t())
+    assert v.offset == 2 * 8 + 1 and v.ndim == 2
+    assert list(v.shape)[:2] == [6, 3] and list(v.strides)[:2] == [1, 8]
+    e = engine.view(torch.zeros(1, 4, 5).expand(3, 4, 5))
+    assert list(e.strides)[:3] == [0, 5, 1]

@@ -1,0 +1,228 @@
+"""GPU parity tests for the GEMM family (matmul / strided views / bmm / Linear) through
+the C ABI, against the CPU oracle (oracle/, pinned to the reference) and the golden
+vectors made by the reference's own code."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from minitensor_b200 import inputs
+from parity import absmm, check, dev, host
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "golden_v1.npz")
+MODES = ["strict", "tf32", "tf32x3"]
+THREADS = max(1, min(16, os.cpu_count() or 1))
+
+
+@pytest.fixture(scope="module")
+def gold():
+    return np.load(GOLDEN)
+
+
+def run(eng, A, B, mode, C=None):
+    if C is None:
+        C = torch.empty((A.shape[0], B.shape[1]), dtype=torch.float32, device="cuda")
+    eng.gemm(A, B, C, mode=mode)
+    return C
+
+
+# ------------------------------------------------------------------ golden vectors ---
+
+@pytest.mark.parametrize("mode", MODES)
+def test_golden_matmul(eng, gold, mode):
+    keys = [k[:-2] for k in gold.files if k.endswith("_C") and (k.startswith("mm") or k.startswith("bench"))
+            and not k.startswith("mmt")]
+    for key in keys:
+        A, B, Cr = gold[key + "_A"], gold[key + "_B"], gold[key + "_C"]
+        C = host(run(eng, dev(A), dev(B), mode))
+        check(mode, C, Cr, absmm(A, B), A.shape[1], key)
+    # The reference's own GPU known answer (test/tensor_test.cpp:285-317) via matmul_gpu.
+    A, B = dev(gold["mm_known_A"]), dev(gold["mm_known_B"])
+    C = torch.empty(2, 2, device="cuda")
+    eng.matmul_gpu(A, B, C)
+    assert host(C).ravel().tolist() == [58.0, 64.0, 139.0, 154.0]
+
+
+@pytest.mark.parametrize("mode", MODES)
+def test_golden_views(eng, gold, mode):
+    for i in range(3):
+        M, K, N, ta, tb = gold[f"mmt{i}_meta"].tolist()
+        As, Bs = dev(gold[f"mmt{i}_As"]), dev(gold[f"mmt{i}_Bs"])
+        A = As.t() if ta else As
+        B = Bs.t() if tb else Bs
+        An, Bn = (gold[f"mmt{i}_As"].T if ta else gold[f"mmt{i}_As"]), (gold[f"mmt{i}_Bs"].T if tb else gold[f"mmt{i}_Bs"])
+        C = host(run(eng, A, B, mode))
+        check(mode, C, gold[f"mmt{i}_C"], absmm(An, Bn), K, f"mmt{i}")
+    r0, r1 = gold["rows_meta"].tolist()
+    A = dev(gold["rows_A"])[r0:r1]
+    C = torch.empty((r1 - r0, gold["rows_B"].shape[1]), device="cuda")
+    eng.matmul_gpu(A, dev(gold["rows_B"]), C)  # contiguous view with an offset
+    check("tf32x3" if mode != "strict" else mode, host(C), gold["rows_C"],
+          absmm(gold["rows_A"][r0:r1], gold["rows_B"]), A.shape[1], "row slice")
+
+
+@pytest.mark.parametrize("mode", MODES)
+def test_golden_bmm_and_linear(eng, gold, mode):
+    A, B0 = gold["bmmb_A"], gold["bmmb_B0"]
+    Bx = dev(B0).expand(A.shape[0], -1, -1)
+    assert Bx.stride(0) == 0
+    C = torch.empty((A.shape[0], A.shape[1], B0.shape[2]), device="cuda")
+    eng.gemm(dev(A), Bx, C, mode=mode)
+    check(mode, host(C), gold["bmmb_C"], absmm(A, B0), A.shape[2], "bmm broadcast")
+    eng.gemm(dev(gold["bmm_A"]), dev(gold["bmm_B"]), C, mode=mode)
+    check(mode, host(C), gold["bmm_C"], absmm(gold["bmm_A"], gold["bmm_B"]), A.shape[2], "bmm")
+
+    X, W, b, dY = (gold[k] for k in ("lin_X", "lin_W", "lin_b", "lin_dY"))
+    Y = eng.linear_forward(dev(X), dev(W), dev(b), mode=mode)
+    check(mode, host(Y), gold["lin_Y"], absmm(X, W) + np.abs(b), X.shape[1], "linear fwd")
+    dX, dW, db = eng.linear_backward(dev(X), dev(W), dev(dY), mode=mode)
+    check(mode, host(dX), gold["lin_dX"], absmm(dY, W.T), W.shape[1], "linear dX")
+    check(mode, host(dW), gold["lin_dW"], absmm(X.T, dY), X.shape[0], "linear dW")
+    assert np.allclose(host(db).ravel(), dY.sum(0, dtype=np.float64), rtol=1e-5, atol=1e-4)
+
+
+# ------------------------------------------------------------------ configurations ---
+
+@pytest.mark.parametrize("mode", MODES)
+def test_config1_512(eng, port, mode):
+    A, B = inputs.config1()
+    C = host(run(eng, dev(A), dev(B), mode))
+    if mode != "strict":
+        assert eng.last_path().startswith("umma_" + mode), eng.last_path()
+    check(mode, C, port.matmul(A, B), absmm(A, B), 512, "config1")
+
+
+@pytest.mark.parametrize("mode", ["tf32", "tf32x3"])
+def test_config2_linear(eng, port, mode):
+    X, W, b, dY = inputs.config2()
+    Xd, Wd, bd, dYd = dev(X), dev(W), dev(b), dev(dY)
+    Y = host(eng.linear_forward(Xd, Wd, bd, mode=mode))
+    Yr = port.matmul_rows(X, W, 0, X.shape[0], THREADS) + b
+    check(mode, Y, Yr, absmm(X, W), 1024, "config2 fwd")
+    dX, dW, _ = eng.linear_backward(Xd, Wd, dYd, mode=mode)
+    # dX = dY.W^T and dW = X^T.dY: same per-element k order as matmul_cpu_strided.
+    dXr = port.matmul_rows(dY, np.ascontiguousarray(W.T), 0, 256, THREADS)
+    check(mode, host(dX), dXr, absmm(dY, W.T), 4096, "config2 dX (NT)")
+    XT = np.ascontiguousarray(X.T)
+    dWr = port.matmul_rows(XT, dY, 0, 1024, THREADS)
+    check(mode, host(dW), dWr, absmm(XT, dY), 256, "config2 dW (TN)")
+
+
+@pytest.mark.parametrize("mode", MODES)
+def test_config3_bmm_broadcast(eng, port, mode):
+    A, B0 = inputs.config3()
+    Bx = dev(B0).expand(64, 64, 512)
+    C = torch.empty(64, 512, 512, device="cuda")
+    eng.bmm_gpu(dev(A), Bx, C) if mode == "tf32x3" else eng.gemm(dev(A), Bx, C, mode=mode)
+    Cr = port.bmm(A, np.broadcast_to(B0, (64, 64, 512)))
+    check(mode, host(C), Cr, absmm(A, B0), 64, "config3")
+
+
+@pytest.mark.parametrize("mode", ["tf32", "tf32x3", "strict"])
+def test_config5_8192_sampled_rows(eng, port, mode):
+    A, B = inputs.config5()
+    Ad, Bd = dev(A), dev(B)
+    C = torch.empty(8192, 8192, device="cuda")
+    eng.gemm(Ad, Bd, C, mode=mode)
+    rows = [0, 1, 127, 128, 4095, 8191]
+    rng = np.random.RandomState(5)
+    rows += sorted(rng.choice(8192, 10, replace=False).tolist())
+    Ch = host(C)
+    for r in rows:
+        Cr = port.matmul_rows(A, B, r, r + 1, 1)
+        check(mode, Ch[r:r + 1], Cr, absmm(A[r:r + 1], B), 8192, f"config5 row {r}")
+    # Size-independent property: the column sums of C equal (1^T A) B.
+    colsum = np.abs(Ch.astype(np.float64).sum(0) - A.astype(np.float64).sum(0) @ B.astype(np.float64))
+    bound = np.abs(A).astype(np.float64).sum(0) @ np.abs(B).astype(np.float64)
+    assert np.max(colsum / bound) < 1e-3
+
+
+# ------------------------------------------------------------------ layouts & edges ---
+
+def padded(shape, seed, pad=4):
+    """A float32 matrix stored with a leading dimension rounded up to `pad` elements:
+    returns (numpy view, the same view on the GPU)."""
+    r, c = shape
+    ld = (c + pad - 1) // pad * pad
+    base = inputs.uniform((r, ld), -1, 1, seed)
+    return base[:, :c], dev(base)[:, :c]
+
+
+@pytest.mark.parametrize("mode", ["tf32", "tf32x3", "strict"])
+@pytest.mark.parametrize("layout", ["NN", "NT", "TN", "TT"])
+def test_layouts_ragged(eng, port, mode, layout):
+    shapes = [(257, 383, 511), (129, 65, 1), (1, 7, 300), (63, 127, 129), (300, 200, 33), (128, 256, 96)]
+    for i, (M, N, K) in enumerate(shapes):
+        a_np, a_t = padded((K, M) if layout[0] == "T" else (M, K), 10 * i + 1)
+        b_np, b_t = padded((N, K) if layout[1] == "T" else (K, N), 10 * i + 2)
+        A = a_t.t() if layout[0] == "T" else a_t
+        B = b_t.t() if layout[1] == "T" else b_t
+        An = a_np.T if layout[0] == "T" else a_np
+        Bn = b_np.T if layout[1] == "T" else b_np
+        C = host(run(eng, A, B, mode))
+        if mode != "strict":
+            assert eng.last_path().startswith("umma_" + mode), (layout, M, N, K, eng.last_path())
+        check(mode, C, port.matmul_strided(An, Bn), absmm(An, Bn), K, f"{layout} {M}x{N}x{K}")
+
+
+@pytest.mark.parametrize("mode", ["tf32", "tf32x3"])
+def test_unaligned_views_use_simt_and_stay_correct(eng, port, mode):
+    # Row stride 383 floats is not 16-byte aligned: the tensor-core kernel cannot take it.
+    A = inputs.uniform((200, 383), -1, 1, 31)
+    B = inputs.uniform((383, 150), -1, 1, 32)
+    C = host(run(eng, dev(A), dev(B), mode))
+    assert eng.last_path().startswith("simt"), eng.last_path()
+    check(mode, C, port.matmul(A, B), absmm(A, B), 383, "unaligned")
+
+
+@pytest.mark.parametrize("mode", MODES)
+def test_epilogues_and_k0(eng, port, mode):
+    M, N, K = 200, 264, 96
+    A = inputs.uniform((M, K), -1, 1, 41)
+    B = inputs.uniform((K, N), -1, 1, 42)
+    bn = inputs.uniform((N,), -1, 1, 43)
+    bm = inputs.uniform((M,), -1, 1, 44)
+    base = port.matmul(A, B)
+    D = absmm(A, B)
+    C = torch.empty(M, N, device="cuda")
+    eng.gemm(dev(A), dev(B), C, bias=dev(bn), epi=eng.EPI_BIAS_COL | eng.EPI_RELU, mode=mode)
+    check(mode, host(C), np.maximum(base + bn, 0), D + np.abs(bn), K, "bias col + relu")
+    eng.gemm(dev(A), dev(B), C, bias=dev(bm), epi=eng.EPI_BIAS_ROW, mode=mode)
+    check(mode, host(C), base + bm[:, None], D + np.abs(bm)[:, None], K, "bias row")
+    # K == 0: the empty sum; C = epi(0).
+    A0 = torch.empty(M, 0, device="cuda")
+    B0 = torch.empty(0, N, device="cuda")
+    eng.gemm(A0, B0, C, bias=dev(bn), epi=eng.EPI_BIAS_COL, mode=mode)
+    assert np.array_equal(host(C), np.broadcast_to(bn, (M, N)))
+
+
+@pytest.mark.parametrize("mode", ["tf32", "tf32x3", "strict"])
+def test_output_guard_bands(eng, port, mode):
+    # C is a window of a larger buffer; everything outside the window must be untouched.
+    M, N, K = 300, 260, 128
+    A = inputs.uniform((M, K), -1, 1, 51)
+    B = inputs.uniform((K, N), -1, 1, 52)
+    big = torch.full((M + 16, N + 20), 12345.0, device="cuda")
+    C = big[8:8 + M, 4:4 + N]
+    eng.gemm(dev(A), dev(B), C, mode=mode)
+    h = host(big)
+    mask = np.ones_like(h, dtype=bool)
+    mask[8:8 + M, 4:4 + N] = False
+    assert np.all(h[mask] == 12345.0)
+    check(mode, h[8:8 + M, 4:4 + N], port.matmul(A, B), absmm(A, B), K, "guarded")
+
+
+def test_column_major_output(eng, port):
+    M, N, K = 160, 96, 64
+    A = inputs.uniform((M, K), -1, 1, 61)
+    B = inputs.uniform((K, N), -1, 1, 62)
+    Ct = torch.empty(N, M, device="cuda")
+    eng.gemm(dev(A), dev(B), Ct.t(), mode="tf32x3")
+    check("tf32x3", host(Ct).T, port.matmul(A, B), absmm(A, B), K, "column-major C")
+
+
+def test_device_status_clean(eng):
+    assert eng.device_status(reset=True) == 0
