@@ -104,8 +104,11 @@ bool encode_3d(CUtensorMap* m, const float* base, uint64_t d0, uint64_t d1, uint
     cuuint64_t strides[2] = {s1, s2};
     cuuint32_t box[3] = {b0, b1, 1};
     cuuint32_t es[3] = {1, 1, 1};
+    // swizzle_bytes: 128 / 64 = 16-byte granules (K-major operands); 32 = the 128-byte
+    // span with 32-byte granules that MN-major tf32 operands require.
     CUtensorMapSwizzle sw = swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
                           : swizzle_bytes == 64  ? CU_TENSOR_MAP_SWIZZLE_64B
+                          : swizzle_bytes == 32  ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
                                                  : CU_TENSOR_MAP_SWIZZLE_NONE;
     CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, es,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -173,11 +176,11 @@ int launch_simt(const GemmProblem& p, cudaStream_t st) {
     return MT_OK;
 }
 
-template <int BN, int SWB, bool AMN, bool BMN, bool X3, int STAGES>
+template <int BN, int BKE, bool AMN, bool BMN, bool X3, int STAGES>
 int launch_umma_inst(const CUtensorMap& ta, const CUtensorMap& tb, const mt::umma::Params& up, int grid,
                      cudaStream_t st) {
-    using G = mt::umma::Cfg<BN, SWB, X3, STAGES>;
-    auto kern = mt::umma::gemm_kernel<BN, SWB, AMN, BMN, X3, STAGES>;
+    using G = mt::umma::Cfg<BN, BKE, X3, STAGES>;
+    auto kern = mt::umma::gemm_kernel<BN, BKE, AMN, BMN, X3, STAGES>;
     static std::atomic<uint64_t> attr_set_mask{0};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -217,8 +220,9 @@ int launch_umma(const GemmProblem& p, bool x3, cudaStream_t st) {
     else if ((p.sb_k == 1 || p.K == 1) && (p.N == 1 || mult4(p.sb_n))) b_mn = 0;
     if (a_mn < 0 || b_mn < 0) return fail(MT_EUNSUPPORTED, "umma: operand strides not TMA-expressible");
 
-    const int swb = x3 ? 64 : 128;
-    const uint32_t bke = swb / 4, chunk = swb / 4;
+    const uint32_t bke = x3 ? 16 : 32;        // k elements per stage
+    const int kswz = (int)bke * 4;             // K-major swizzle span (bytes)
+    const uint32_t chunk = 32;                 // MN-major box width (elements)
     const int64_t tiles_m = (p.M + 127) / 128;
     const bool small = tiles_m * ((p.N + 255) / 256) * p.batch < (int64_t)di.sms || p.N <= 128;
     const int bn = small ? 128 : 256;
@@ -232,21 +236,21 @@ int launch_umma(const GemmProblem& p, bool x3, cudaStream_t st) {
     if (a_mn == 0) {   // dims {K, M, batch}
         uint64_t s1 = st_or(p.M, p.sa_m, round16(p.K * 4));
         uint64_t s2 = a_batched ? (uint64_t)p.sa_b * 4 : round16(s1 * p.M);
-        ok = encode_3d(&ta, p.A, p.K, p.M, a_batched ? p.batch : 1, s1, s2, bke, 128, swb);
+        ok = encode_3d(&ta, p.A, p.K, p.M, a_batched ? p.batch : 1, s1, s2, bke, 128, kswz);
     } else {           // dims {M, K, batch}
         uint64_t s1 = st_or(p.K, p.sa_k, round16(p.M * 4));
         uint64_t s2 = a_batched ? (uint64_t)p.sa_b * 4 : round16(s1 * p.K);
-        ok = encode_3d(&ta, p.A, p.M, p.K, a_batched ? p.batch : 1, s1, s2, chunk, bke, swb);
+        ok = encode_3d(&ta, p.A, p.M, p.K, a_batched ? p.batch : 1, s1, s2, chunk, bke, 32);
     }
     if (!ok) return fail(MT_EUNSUPPORTED, "umma: A tensor map rejected");
     if (b_mn == 0) {   // dims {K, N, batch}
         uint64_t s1 = st_or(p.N, p.sb_n, round16(p.K * 4));
         uint64_t s2 = b_batched ? (uint64_t)p.sb_b * 4 : round16(s1 * p.N);
-        ok = encode_3d(&tb, p.B, p.K, p.N, b_batched ? p.batch : 1, s1, s2, bke, bn, swb);
+        ok = encode_3d(&tb, p.B, p.K, p.N, b_batched ? p.batch : 1, s1, s2, bke, bn, kswz);
     } else {           // dims {N, K, batch}
         uint64_t s1 = st_or(p.K, p.sb_k, round16(p.N * 4));
         uint64_t s2 = b_batched ? (uint64_t)p.sb_b * 4 : round16(s1 * p.K);
-        ok = encode_3d(&tb, p.B, p.N, p.K, b_batched ? p.batch : 1, s1, s2, chunk, bke, swb);
+        ok = encode_3d(&tb, p.B, p.N, p.K, b_batched ? p.batch : 1, s1, s2, chunk, bke, 32);
     }
     if (!ok) return fail(MT_EUNSUPPORTED, "umma: B tensor map rejected");
 
@@ -262,17 +266,17 @@ int launch_umma(const GemmProblem& p, bool x3, cudaStream_t st) {
     const int grid = (int)std::min<long long>(up.num_tiles, (long long)di.sms);
 
     int rc;
-#define MT_UMMA_DISPATCH(BN_, SWB_, X3_, ST_)                                                       \
-    if (a_mn == 0 && b_mn == 0) rc = launch_umma_inst<BN_, SWB_, false, false, X3_, ST_>(ta, tb, up, grid, st); \
-    else if (a_mn == 0 && b_mn == 1) rc = launch_umma_inst<BN_, SWB_, false, true, X3_, ST_>(ta, tb, up, grid, st); \
-    else if (a_mn == 1 && b_mn == 0) rc = launch_umma_inst<BN_, SWB_, true, false, X3_, ST_>(ta, tb, up, grid, st); \
-    else rc = launch_umma_inst<BN_, SWB_, true, true, X3_, ST_>(ta, tb, up, grid, st);
+#define MT_UMMA_DISPATCH(BN_, BKE_, X3_, ST_)                                                       \
+    if (a_mn == 0 && b_mn == 0) rc = launch_umma_inst<BN_, BKE_, false, false, X3_, ST_>(ta, tb, up, grid, st); \
+    else if (a_mn == 0 && b_mn == 1) rc = launch_umma_inst<BN_, BKE_, false, true, X3_, ST_>(ta, tb, up, grid, st); \
+    else if (a_mn == 1 && b_mn == 0) rc = launch_umma_inst<BN_, BKE_, true, false, X3_, ST_>(ta, tb, up, grid, st); \
+    else rc = launch_umma_inst<BN_, BKE_, true, true, X3_, ST_>(ta, tb, up, grid, st);
     if (!x3) {
-        if (bn == 256) { MT_UMMA_DISPATCH(256, 128, false, 4) }
-        else { MT_UMMA_DISPATCH(128, 128, false, 6) }
+        if (bn == 256) { MT_UMMA_DISPATCH(256, 32, false, 4) }
+        else { MT_UMMA_DISPATCH(128, 32, false, 6) }
     } else {
-        if (bn == 256) { MT_UMMA_DISPATCH(256, 64, true, 4) }
-        else { MT_UMMA_DISPATCH(128, 64, true, 6) }
+        if (bn == 256) { MT_UMMA_DISPATCH(256, 16, true, 4) }
+        else { MT_UMMA_DISPATCH(128, 16, true, 6) }
     }
 #undef MT_UMMA_DISPATCH
     if (rc == MT_OK) {

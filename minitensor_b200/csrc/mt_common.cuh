@@ -181,20 +181,25 @@ __device__ __forceinline__ void tmem_ld_wait() {
 // UMMA shared-memory matrix descriptor (sm_100 "version 1" format).
 //   bits  0-13 start address >> 4      bits 16-29 leading byte offset >> 4
 //   bits 32-45 stride byte offset >> 4 bits 46-47 version = 1
-//   bits 49-51 base offset (0: tiles are 1024-byte aligned)
-//   bits 61-63 layout: 2 = 128-byte swizzle
-// K-major SW128: 8 rows of 128 B form one swizzle atom; SBO = 1024 (next 8 rows),
-//   LBO unused (1). Stepping K by 8 tf32 = +32 B on the start address.
-// MN-major SW128: an atom is 8 K-rows x 128 B (32 elements) of M/N; LBO = byte
-//   distance between 32-element M/N chunks, SBO = distance between 8-row K groups.
+//   bits 49-51 base offset (0: atoms start on their natural alignment)
+//   bits 61-63 layout: 1 = 128-byte swizzle of 32-byte granules, 2 = 128-byte
+//                      swizzle (16-byte granules), 4 = 64-byte swizzle
+// K-major (layouts 2 / 4): 8 rows of 128 B (64 B) form one swizzle atom; SBO = 8 rows,
+//   LBO unused (16). Stepping K by 8 tf32 = +32 B on the start address.
+// MN-major tf32: 32-bit operands have exactly one MN-major form, layout 1, whose atom
+//   is 4 K-rows x 128 B (32 elements of M/N) with 32-byte granules XOR-ed by the row
+//   index (TMA writes it with CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B). LBO = byte distance
+//   between 32-element M/N chunks, SBO = distance between 4-row K groups (512 B).
 // ---------------------------------------------------------------------------------
-__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+enum : uint32_t { kLayoutSw128Base32 = 1, kLayoutSw128 = 2, kLayoutSw64 = 4 };
+
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
     uint64_t d = 0;
     d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
     d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
     d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
     d |= (uint64_t)1 << 46;
-    d |= (uint64_t)2 << 61;
+    d |= (uint64_t)layout << 61;
     return d;
 }
 

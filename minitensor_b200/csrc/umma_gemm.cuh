@@ -6,9 +6,10 @@
 //             hi = rna_tf32(x), lo = x - hi; C += Ahi*Bhi + Ahi*Blo + Alo*Bhi, all three
 //             products accumulated in the same fp32 TMEM accumulator.
 //
-// Layout of work. One persistent CTA per SM walks output tiles of 128 x BN. Warp roles:
-//   warp 0      TMA producer: 128-byte- (or 64-byte-) swizzled tiles into a STAGES-deep
-//               shared-memory ring, completion counted on mbarriers (no multicast).
+// Layout of work. One persistent CTA per SM walks output tiles of 128 x BN, BKE (32 for
+// TF32, 16 for TF32X3) k-elements per pipeline stage. Warp roles:
+//   warp 0      TMA producer: swizzled tiles into a STAGES-deep shared-memory ring,
+//               completion counted on mbarriers (no multicast).
 //   warp 1      TMEM owner and single-thread MMA issuer (tcgen05.mma.cta_group::1).
 //   warps 2-5   epilogue: TMEM -> registers (tcgen05.ld 32x32b) -> bias/ReLU -> global.
 //   warps 6-9   (TF32X3 only) converter: splits each landed stage into hi (in place) and
@@ -41,9 +42,10 @@ struct Params {
     long long num_tiles;
 };
 
-template <int BN, int SWB, bool X3, int STAGES>
+template <int BN, int BKE_, bool X3, int STAGES>
 struct Cfg {
-    static constexpr int BKE = SWB / 4;                        // k elements per stage
+    static constexpr int BKE = BKE_;                           // k elements per stage (16 or 32)
+    static constexpr int KSWB = BKE * 4;                       // K-major swizzle span, bytes
     static constexpr uint32_t A_BYTES = BM * BKE * 4;
     static constexpr uint32_t B_BYTES = BN * BKE * 4;
     static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
@@ -54,9 +56,9 @@ struct Cfg {
     static constexpr uint32_t RING_BYTES = STAGE_BYTES * STAGES * (X3 ? 2 : 1);
     static constexpr uint32_t BAR_BYTES = 8 * (3 * STAGES + 4) + 16;
     static constexpr uint32_t SMEM_BYTES = 1024 + RING_BYTES + BAR_BYTES;
-    static constexpr uint32_t CHUNK = SWB / 4;                 // MN elements per swizzle atom row
-    // MN-major: one atom column = BKE k-rows x SWB bytes.
-    static constexpr uint32_t MN_CHUNK_BYTES = BKE * SWB;
+    static constexpr uint32_t CHUNK = 32;                      // MN-major: 32 elements (128 B) per row
+    // MN-major: one chunk = BKE k-rows x 128 bytes.
+    static constexpr uint32_t MN_CHUNK_BYTES = BKE * 128;
 };
 
 // Tile t -> (batch, m block, n block); m blocks are grouped by 8 so that consecutive CTAs
@@ -74,25 +76,22 @@ __device__ __forceinline__ void tile_coords(const Params& p, long long t, int& b
     nb = (int)(in_group / gsize);
 }
 
-template <bool MN_MAJOR, int SWB>
-__device__ __forceinline__ uint64_t operand_desc(uint32_t base, int kstep, uint32_t mn_chunk_bytes) {
+template <bool MN_MAJOR, int BKE>
+__device__ __forceinline__ uint64_t operand_desc(uint32_t base, int kstep) {
     if (MN_MAJOR) {
-        // k-step of 8 rows = 8 * SWB bytes; LBO = next MN chunk, SBO = next 8-row K group.
-        uint64_t d = umma_desc_sw128(base + kstep * 8 * SWB, mn_chunk_bytes, 8 * SWB);
-        if (SWB == 64) d = (d & ~((uint64_t)7 << 61)) | ((uint64_t)4 << 61);
-        return d;
+        // k-step of 8 rows = 1024 bytes; LBO = next 32-element MN chunk, SBO = next
+        // 4-row K group.
+        return umma_desc(base + kstep * 8 * 128, BKE * 128, 4 * 128, kLayoutSw128Base32);
     } else {
         // k-step of 8 tf32 = 32 bytes inside the swizzled row; SBO = 8 rows.
-        uint64_t d = umma_desc_sw128(base + kstep * 32, 16, 8 * SWB);
-        if (SWB == 64) d = (d & ~((uint64_t)7 << 61)) | ((uint64_t)4 << 61);
-        return d;
+        return umma_desc(base + kstep * 32, 16, 8 * BKE * 4, BKE == 32 ? kLayoutSw128 : kLayoutSw64);
     }
 }
 
-template <int BN, int SWB, bool A_MN, bool B_MN, bool X3, int STAGES>
-__global__ void __launch_bounds__(Cfg<BN, SWB, X3, STAGES>::THREADS, 1)
+template <int BN, int BKE, bool A_MN, bool B_MN, bool X3, int STAGES>
+__global__ void __launch_bounds__(Cfg<BN, BKE, X3, STAGES>::THREADS, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
-    using G = Cfg<BN, SWB, X3, STAGES>;
+    using G = Cfg<BN, BKE, X3, STAGES>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* ring = smem;                                      // [STAGES][A|B]
@@ -192,14 +191,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                     const uint32_t sb = sa + G::A_BYTES;
 #pragma unroll
                     for (int k = 0; k < G::KSTEPS; ++k) {
-                        const uint64_t ad = operand_desc<A_MN, SWB>(sa, k, G::MN_CHUNK_BYTES);
-                        const uint64_t bd = operand_desc<B_MN, SWB>(sb, k, G::MN_CHUNK_BYTES);
+                        const uint64_t ad = operand_desc<A_MN, BKE>(sa, k);
+                        const uint64_t bd = operand_desc<B_MN, BKE>(sb, k);
                         const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
                         if (X3) {
                             const uint32_t la = smem_u32(ring_lo + s * G::STAGE_BYTES);
                             const uint32_t lb = la + G::A_BYTES;
-                            const uint64_t ald = operand_desc<A_MN, SWB>(la, k, G::MN_CHUNK_BYTES);
-                            const uint64_t bld = operand_desc<B_MN, SWB>(lb, k, G::MN_CHUNK_BYTES);
+                            const uint64_t ald = operand_desc<A_MN, BKE>(la, k);
+                            const uint64_t bld = operand_desc<B_MN, BKE>(lb, k);
                             umma_tf32(d_tmem, ald, bd, idesc, acc);   // Alo * Bhi
                             umma_tf32(d_tmem, ad, bld, idesc, 1u);    // Ahi * Blo
                             umma_tf32(d_tmem, ad, bd, idesc, 1u);     // Ahi * Bhi

@@ -21,6 +21,7 @@ from __future__ import annotations
 import ctypes
 import os
 import subprocess
+import time
 
 import numpy as np
 
@@ -91,12 +92,14 @@ class Port:
         self.lib.orc_matmul_strided(pa, sa[0], sa[1], pb, sb[0], sb[1], _p(C), N, 1, M, K, N)
         return C
 
-    def matmul_rows(self, A, B, r0, r1, threads=1):
+    def matmul_rows(self, A, B, r0, r1, threads=1, timing=False):
         M, K = A.shape
         N = B.shape[1]
         C = np.zeros((M, N), np.float32)
+        t0 = time.perf_counter()
         self.lib.orc_matmul_rows_mt(_p(A), _p(B), _p(C), M, K, N, r0, r1, threads)
-        return C[r0:r1]
+        dt = time.perf_counter() - t0
+        return (C[r0:r1], dt) if timing else C[r0:r1]
 
     def bmm(self, A, B):
         """A [b,M,K], B [b,K,N]; a numpy broadcast view (stride 0) is honoured."""
@@ -161,7 +164,8 @@ class Ref:
         L.ref_linear.argtypes = [_f, _f, _f, _f, _f, _f, _f, _i64, _i64, _i64]
         L.ref_conv2d.argtypes = [_f, _f, _f, _f] + [_i64] * 9
         L.ref_conv2d_backward.argtypes = [_f, _f, _f, _f, _f, _f] + [_i64] * 9
-        L.ref_matmul_rows_mt.argtypes = [_f, _f, _f, _i64, _i64, _i64, _i64, _i64, ctypes.c_int]
+        L.ref_matmul_rows_mt.argtypes = [_f, _f, _f, _i64, _i64, _i64, _i64, _i64, ctypes.c_int,
+                                         ctypes.POINTER(ctypes.c_double)]
 
     @staticmethod
     def _ok(rc):
@@ -187,12 +191,15 @@ class Ref:
         self._ok(self.lib.ref_matmul_rowslice(_p(A), _p(B), _p(C), M, K, N, r0, r1))
         return C
 
-    def matmul_rows(self, A, B, r0, r1, threads=1):
+    def matmul_rows(self, A, B, r0, r1, threads=1, timing=False):
+        """C rows [r0, r1) by the reference's matmul_cpu on row slices; with timing=True
+        also returns the seconds spent in matmul_cpu (excluding input copies)."""
         M, K = A.shape
         N = B.shape[1]
         C = np.empty((r1 - r0, N), np.float32)
-        self._ok(self.lib.ref_matmul_rows_mt(_p(A), _p(B), _p(C), M, K, N, r0, r1, threads))
-        return C
+        sec = ctypes.c_double(0.0)
+        self._ok(self.lib.ref_matmul_rows_mt(_p(A), _p(B), _p(C), M, K, N, r0, r1, threads, ctypes.byref(sec)))
+        return (C, sec.value) if timing else C
 
     def bmm(self, A, B, b_bcast):
         bt, M, K = A.shape

@@ -8,6 +8,7 @@
 //
 // Only tests/ (golden-vector generation and oracle pinning) and bench.py's reference
 // arm load the result.
+#include <chrono>
 #include <cstdint>
 #include <cstring>
 #include <exception>
@@ -173,8 +174,11 @@ int ref_conv2d_backward(const float* dy, const float* x, const float* w,
 // rows. Each thread calls the reference's matmul_cpu on a row slice of A
 // (include/Tensor.hpp:52-74 slice keeps the storage and advances the offset), which
 // gives per-element results identical to one matmul_cpu call over all rows.
+// *seconds (optional) receives the wall time of the threaded matmul_cpu calls alone,
+// without the copies of A and B into reference Tensors.
 int ref_matmul_rows_mt(const float* A, const float* B, float* C,
-                       int64_t M, int64_t K, int64_t N, int64_t r0, int64_t r1, int threads) {
+                       int64_t M, int64_t K, int64_t N, int64_t r0, int64_t r1, int threads,
+                       double* seconds) {
     try {
         Tensor<float> a = from_host(A, {(size_t)M, (size_t)K});
         Tensor<float> b = from_host(B, {(size_t)K, (size_t)N});
@@ -184,6 +188,7 @@ int ref_matmul_rows_mt(const float* A, const float* B, float* C,
         if (threads > rows) threads = (int)rows;
         std::vector<Tensor<float>> outs((size_t)threads);
         std::vector<std::thread> pool;
+        auto t0 = std::chrono::steady_clock::now();
         for (int t = 0; t < threads; ++t) {
             size_t s = (size_t)(r0 + rows * t / threads), e = (size_t)(r0 + rows * (t + 1) / threads);
             outs[(size_t)t] = Tensor<float>({e - s, (size_t)N});
@@ -193,6 +198,7 @@ int ref_matmul_rows_mt(const float* A, const float* B, float* C,
             });
         }
         for (auto& th : pool) th.join();
+        if (seconds) *seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
         size_t row = 0;
         for (int t = 0; t < threads; ++t) {
             to_host(outs[(size_t)t], C + row * (size_t)N);
