@@ -37,6 +37,8 @@ def parse():
     ap.add_argument("--impl", default="mt", choices=["mt", "reference"])
     ap.add_argument("--mode", default="tf32x3", choices=["tf32x3", "tf32", "strict"])
     ap.add_argument("--no-extras", action="store_true", help="skip the other modes, e2e and CPU legs")
+    ap.add_argument("--size", type=int, default=8192,
+                    help="square problem size; 8192 is the benchmark, smaller sizes are profiling cases")
     return ap.parse_args()
 
 
@@ -170,6 +172,12 @@ def time_steps(fn, steps, stream):
 def run_gpu(args, rank, world, local_rank):
     import torch
     from minitensor_b200 import engine, inputs
+
+    global N_DIM, FLOP, WORKLOAD
+    if args.size != N_DIM:
+        N_DIM = args.size
+        FLOP = 2.0 * N_DIM ** 3
+        WORKLOAD = f"profiling case: config5 generator at {N_DIM}^3 (not the benchmark shape)"
 
     torch.cuda.set_device(local_rank)
     dist = None

@@ -100,6 +100,49 @@ MT_API int mt_bmm_gpu(const mt_tensor* A, const mt_tensor* B, const mt_tensor* C
 MT_API int mt_linear_fwd_gpu(const mt_tensor* X, const mt_tensor* W, const mt_tensor* bias,
                              const mt_tensor* Y, int relu, void* stream);
 
+/* ---- Conv2D (NCHW) as implicit GEMM --------------------------------------------------
+ * x [N,C,H,W], w [C_out,C,kh,kw], y / dY [N,C_out,H_out,W_out] with
+ * H_out = (H + 2*padding - kh) / stride + 1 (0 when H + 2*padding < kh), as
+ * safe_out_size (include/TensorOps.hpp:17-20). Inputs may be strided views; outputs must be
+ * contiguous (as the reference allocates them). */
+
+/* include/TensorOps.hpp:708 conv2d_gpu(input, weight, bias, output, stride, padding);
+ * bias may be NULL or empty. Called by conv2d() (include/TensorOps.hpp:1096). */
+MT_API int mt_conv2d_gpu(const mt_tensor* in, const mt_tensor* w, const mt_tensor* bias, const mt_tensor* out,
+                         uint64_t stride, uint64_t padding, void* stream);
+
+/* include/TensorOps.hpp:709 conv2d_gpu_strided: same contract for non-contiguous inputs
+ * (the reference's conv2d() picks it when a view is not contiguous, :1097). */
+MT_API int mt_conv2d_gpu_strided(const mt_tensor* in, const mt_tensor* w, const mt_tensor* bias,
+                                 const mt_tensor* out, uint64_t stride, uint64_t padding, void* stream);
+
+/* include/TensorOps.hpp:710 conv2d_backward_input_gpu(grad_output, weight, grad_input, ...). */
+MT_API int mt_conv2d_backward_input_gpu(const mt_tensor* dY, const mt_tensor* w, const mt_tensor* dX,
+                                        uint64_t stride, uint64_t padding, void* stream);
+
+/* include/TensorOps.hpp:711 conv2d_backward_weight_gpu(grad_output, input, grad_weight, ...).
+ * The tensor-core path splits the reduction over output pixels; its fp32 partials live in a
+ * stream-ordered allocation (cudaMallocAsync on `stream`, freed on the same stream), summed
+ * in a fixed order. mt_conv2d_wgrad takes a caller workspace instead. */
+MT_API int mt_conv2d_backward_weight_gpu(const mt_tensor* dY, const mt_tensor* x, const mt_tensor* dW,
+                                         uint64_t stride, uint64_t padding, void* stream);
+
+/* include/TensorOps.hpp:712 conv2d_backward_bias_gpu(grad_output, grad_bias): db[co] is the
+ * sum over n (ascending) of the spatial sum of dY[n,co], the order of :398-418. */
+MT_API int mt_conv2d_backward_bias_gpu(const mt_tensor* dY, const mt_tensor* db, void* stream);
+
+/* Explicit-mode variants of the three convolution products. */
+MT_API int mt_conv2d_fwd(const mt_tensor* x, const mt_tensor* w, const mt_tensor* bias, const mt_tensor* y,
+                         uint64_t stride, uint64_t padding, int mode, void* stream);
+MT_API int mt_conv2d_dgrad(const mt_tensor* dy, const mt_tensor* w, const mt_tensor* dx, uint64_t stride,
+                           uint64_t padding, int mode, void* stream);
+/* workspace == NULL: stream-ordered allocation as above; else at least
+ * mt_conv2d_wgrad_workspace_bytes(...) bytes of device memory, used only by this call. */
+MT_API int mt_conv2d_wgrad(const mt_tensor* dy, const mt_tensor* x, const mt_tensor* dw, uint64_t stride,
+                           uint64_t padding, int mode, void* workspace, size_t ws_bytes, void* stream);
+MT_API size_t mt_conv2d_wgrad_workspace_bytes(const mt_tensor* dy, const mt_tensor* x, const mt_tensor* dw,
+                                              uint64_t stride, uint64_t padding, int mode);
+
 /* ---- general entry point ----------------------------------------------------------- */
 
 /* C = epi(A * B) for 2-D or 3-D (batched) views with an explicit mode. `bias` is a device

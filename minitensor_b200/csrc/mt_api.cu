@@ -13,6 +13,7 @@
 #include "mt_common.cuh"
 #include "simt_gemm.cuh"
 #include "umma_gemm.cuh"
+#include "conv_gemm.cuh"
 
 namespace {
 
@@ -345,6 +346,309 @@ int matmul_2d(const mt_tensor* A, const mt_tensor* B, const mt_tensor* C, void* 
     return gemm_from_views(a, b, c, nullptr, MT_EPI_NONE, MT_MODE_DEFAULT, stream);
 }
 
+
+// ------------------------------- Conv2D -------------------------------------------
+// include/TensorOps.hpp:17-20 safe_out_size.
+int64_t out_size(int64_t in, int64_t pad, int64_t k, int64_t stride) {
+    if (in + 2 * pad < k) return 0;
+    return (in + 2 * pad - k) / stride + 1;
+}
+
+bool is_contig(const mt_tensor* t) {
+    for (uint32_t i = 0; i < t->ndim; ++i)
+        if (t->shape[i] == 0) return true;   // empty: nothing to address
+    uint64_t expect = 1;
+    for (int i = (int)t->ndim - 1; i >= 0; --i) {
+        if (t->shape[i] != 1 && t->strides[i] != expect) return false;
+        expect *= t->shape[i];
+    }
+    return true;
+}
+
+uint64_t numel(const mt_tensor* t) {
+    if (!t) return 0;
+    uint64_t n = 1;
+    for (uint32_t i = 0; i < t->ndim; ++i) n *= t->shape[i];
+    return t->ndim ? n : 0;
+}
+
+int check4(const mt_tensor* t, const char* who, const char* name) {
+    if (!t) return fail(MT_EINVAL, "%s: %s is null", who, name);
+    if (t->ndim != 4) return fail(MT_EINVAL, "%s: %s must be 4-D (NCHW), got %u-D", who, name, t->ndim);
+    if (numel(t) && !t->data) return fail(MT_EINVAL, "%s: %s has no data", who, name);
+    return MT_OK;
+}
+
+void fill_strides(int64_t (&d)[4], const mt_tensor* t) {
+    for (int i = 0; i < 4; ++i) d[i] = (int64_t)t->strides[i];
+}
+
+template <int KIND, int BN, bool X3, int STAGES>
+int launch_conv_inst(const mt::conv::Params& cp, int grid, cudaStream_t st) {
+    using G = mt::conv::Cfg<BN, X3, STAGES>;
+    auto kern = mt::conv::conv_kernel<KIND, BN, X3, STAGES>;
+    static std::atomic<uint64_t> attr_set_mask{0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(attr_set_mask.load() & bit)) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)G::SMEM_BYTES);
+        if (e != cudaSuccess) return cuda_fail(e, "conv: set smem attribute");
+        attr_set_mask.fetch_or(bit);
+    }
+    kern<<<grid, G::THREADS, G::SMEM_BYTES, st>>>(cp);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess && e != cudaErrorStreamCaptureUnsupported) return cuda_fail(e, "conv launch");
+    g_launches.fetch_add(1);
+    return MT_OK;
+}
+
+template <int KIND, bool X3>
+int launch_conv_bn(const mt::conv::Params& cp, int bn, int grid, cudaStream_t st) {
+    // Stages: the ring (x2 for the lo copy) stays within ~192 KB of shared memory.
+    switch (bn) {
+        case 32:  return launch_conv_inst<KIND, 32, X3, X3 ? 4 : 8>(cp, grid, st);
+        case 64:  return launch_conv_inst<KIND, 64, X3, X3 ? 4 : 8>(cp, grid, st);
+        case 128: return launch_conv_inst<KIND, 128, X3, X3 ? 3 : 6>(cp, grid, st);
+        default:  return launch_conv_inst<KIND, 256, X3, X3 ? 2 : 4>(cp, grid, st);
+    }
+}
+
+int pick_bn(int ncol) { return ncol <= 32 ? 32 : ncol <= 64 ? 64 : ncol <= 128 ? 128 : 256; }
+
+struct ConvShape {
+    int64_t N, C, H, W, Co, kh, kw, Ho, Wo, stride, pad;
+};
+
+// Shared shape checks (include/TensorOps.hpp:1076-1110 conv2d and the backward
+// dispatchers :1112-1149): x [N,C,H,W], w [Co,C,kh,kw], y/dy [N,Co,Ho,Wo].
+int conv_shape(const mt_tensor* x, const mt_tensor* w, const mt_tensor* y, uint64_t stride, uint64_t pad,
+               const char* who, ConvShape& s) {
+    if (stride == 0) return fail(MT_EINVAL, "%s: stride must be >= 1", who);
+    s.N = (int64_t)x->shape[0]; s.C = (int64_t)x->shape[1]; s.H = (int64_t)x->shape[2]; s.W = (int64_t)x->shape[3];
+    s.Co = (int64_t)w->shape[0]; s.kh = (int64_t)w->shape[2]; s.kw = (int64_t)w->shape[3];
+    s.stride = (int64_t)stride; s.pad = (int64_t)pad;
+    if ((int64_t)w->shape[1] != s.C)
+        return fail(MT_EINVAL, "%s: weight C_in (%llu) != input C (%lld)", who, (unsigned long long)w->shape[1], (long long)s.C);
+    s.Ho = out_size(s.H, s.pad, s.kh, s.stride);
+    s.Wo = out_size(s.W, s.pad, s.kw, s.stride);
+    if ((int64_t)y->shape[0] != s.N || (int64_t)y->shape[1] != s.Co || (int64_t)y->shape[2] != s.Ho ||
+        (int64_t)y->shape[3] != s.Wo)
+        return fail(MT_EINVAL, "%s: output must be [%lld,%lld,%lld,%lld]", who, (long long)s.N, (long long)s.Co,
+                    (long long)s.Ho, (long long)s.Wo);
+    const int64_t big = (int64_t)1 << 31;
+    if (s.N * s.C * s.H * s.W >= big || s.N * s.Co * s.Ho * s.Wo >= big || s.C * s.kh * s.kw >= big)
+        return fail(MT_EUNSUPPORTED, "%s: tensors beyond 2^31 elements", who);
+    return MT_OK;
+}
+
+mt::conv::Params conv_params(const ConvShape& s) {
+    mt::conv::Params cp;
+    memset(&cp, 0, sizeof cp);
+    cp.N = (int)s.N; cp.C = (int)s.C; cp.H = (int)s.H; cp.W = (int)s.W; cp.Co = (int)s.Co;
+    cp.kh = (int)s.kh; cp.kw = (int)s.kw; cp.stride = (int)s.stride; cp.pad = (int)s.pad;
+    cp.Ho = (int)s.Ho; cp.Wo = (int)s.Wo;
+    cp.splits = 1;
+    return cp;
+}
+
+int direct_launch(void (*kern)(const mt::conv::Params), const mt::conv::Params& cp, int64_t total, cudaStream_t st,
+                  const char* name) {
+    if (total == 0) return MT_OK;
+    int blocks = (int)std::min<int64_t>((total + 127) / 128, 1 << 20);
+    kern<<<blocks, 128, 0, st>>>(cp);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess && e != cudaErrorStreamCaptureUnsupported) return cuda_fail(e, name);
+    g_launches.fetch_add(1);
+    return MT_OK;
+}
+
+int conv_fwd(const mt_tensor* x, const mt_tensor* w, const mt_tensor* bias, const mt_tensor* y, uint64_t stride,
+             uint64_t pad, int mode, cudaStream_t st, const char* who) {
+    int rc;
+    if ((rc = check4(x, who, "input")) || (rc = check4(w, who, "weight")) || (rc = check4(y, who, "output"))) return rc;
+    ConvShape s;
+    if ((rc = conv_shape(x, w, y, stride, pad, who, s))) return rc;
+    if (!is_contig(y)) return fail(MT_EINVAL, "%s: output must be contiguous", who);
+    const float* bp = nullptr;
+    if (bias && numel(bias)) {
+        if ((int64_t)numel(bias) != s.Co) return fail(MT_EINVAL, "%s: bias must hold C_out elements", who);
+        if (!is_contig(bias)) return fail(MT_EINVAL, "%s: bias must be contiguous", who);
+        bp = bias->data + bias->offset;
+    }
+    mt::conv::Params cp = conv_params(s);
+    cp.x = x->data + x->offset; fill_strides(cp.sx, x);
+    cp.w = w->data + w->offset; fill_strides(cp.sw, w);
+    cp.out = y->data + y->offset;
+    cp.bias = bp;
+    const int64_t total = s.N * s.Co * s.Ho * s.Wo;
+    if (total == 0) { t_path = "empty"; return MT_OK; }
+    mode = resolve_mode(mode);
+    DevInfo di = dev_info();
+    if (mode == MT_STRICT_FP32 || di.cc != 100) {
+        if (mode != MT_STRICT_FP32) return fail(MT_EUNSUPPORTED, "%s: tensor-core conv needs sm_100a", who);
+        t_path = "conv_direct_fwd_fp32";
+        return direct_launch(mt::conv::direct_fwd_kernel, cp, total, st, who);
+    }
+    cp.M = (int)(s.N * s.Ho * s.Wo); cp.Ncol = (int)s.Co; cp.K = (int)(s.C * s.kh * s.kw);
+    cp.tiles_m = (cp.M + 127) / 128;
+    const int bn = pick_bn(cp.Ncol);
+    cp.tiles_n = (cp.Ncol + bn - 1) / bn;
+    cp.kb_total = (cp.K + 31) / 32;
+    cp.num_units = (long long)cp.tiles_m * cp.tiles_n;
+    if (cp.K == 0) return fail(MT_EUNSUPPORTED, "%s: empty reduction", who);
+    const int grid = (int)std::min<long long>(cp.num_units, di.sms);
+    const bool x3 = mode == MT_TF32X3;
+    rc = x3 ? launch_conv_bn<mt::conv::kFwd, true>(cp, bn, grid, st) : launch_conv_bn<mt::conv::kFwd, false>(cp, bn, grid, st);
+    if (rc == MT_OK) t_path = std::string("conv_umma_fwd_") + (x3 ? "tf32x3" : "tf32") + " bn=" + std::to_string(bn);
+    return rc;
+}
+
+int conv_dgrad(const mt_tensor* dy, const mt_tensor* w, const mt_tensor* dx, uint64_t stride, uint64_t pad, int mode,
+               cudaStream_t st, const char* who) {
+    int rc;
+    if ((rc = check4(dy, who, "grad_output")) || (rc = check4(w, who, "weight")) || (rc = check4(dx, who, "grad_input")))
+        return rc;
+    ConvShape s;
+    if ((rc = conv_shape(dx, w, dy, stride, pad, who, s))) return rc;
+    if (!is_contig(dx)) return fail(MT_EINVAL, "%s: grad_input must be contiguous", who);
+    mt::conv::Params cp = conv_params(s);
+    cp.dy = dy->data + dy->offset; fill_strides(cp.sdy, dy);
+    cp.w = w->data + w->offset; fill_strides(cp.sw, w);
+    cp.out = dx->data + dx->offset;
+    const int64_t total = s.N * s.C * s.H * s.W;
+    if (total == 0) { t_path = "empty"; return MT_OK; }
+    mode = resolve_mode(mode);
+    DevInfo di = dev_info();
+    if (mode == MT_STRICT_FP32 || di.cc != 100) {
+        if (mode != MT_STRICT_FP32) return fail(MT_EUNSUPPORTED, "%s: tensor-core conv needs sm_100a", who);
+        t_path = "conv_direct_dgrad_fp32";
+        return direct_launch(mt::conv::direct_dgrad_kernel, cp, total, st, who);
+    }
+    cp.M = (int)total / (int)s.C; cp.Ncol = (int)s.C; cp.K = (int)(s.Co * s.kh * s.kw);
+    cp.tiles_m = (cp.M + 127) / 128;
+    const int bn = pick_bn(cp.Ncol);
+    cp.tiles_n = (cp.Ncol + bn - 1) / bn;
+    cp.kb_total = (cp.K + 31) / 32;
+    cp.num_units = (long long)cp.tiles_m * cp.tiles_n;
+    if (cp.K == 0) {   // no output pixels: the gradient is zero
+        cudaError_t e = cudaMemsetAsync(cp.out, 0, total * sizeof(float), st);
+        return e == cudaSuccess ? MT_OK : cuda_fail(e, who);
+    }
+    const int grid = (int)std::min<long long>(cp.num_units, di.sms);
+    const bool x3 = mode == MT_TF32X3;
+    rc = x3 ? launch_conv_bn<mt::conv::kDgrad, true>(cp, bn, grid, st) : launch_conv_bn<mt::conv::kDgrad, false>(cp, bn, grid, st);
+    if (rc == MT_OK) t_path = std::string("conv_umma_dgrad_") + (x3 ? "tf32x3" : "tf32") + " bn=" + std::to_string(bn);
+    return rc;
+}
+
+// Split-K plan of the weight gradient: one wave of (m tile, split) units.
+struct WgradPlan {
+    int tiles_m, tiles_n, kb_per_img, kb_total, splits;
+    size_t ws_bytes;
+};
+
+WgradPlan wgrad_plan(const ConvShape& s, int sms) {
+    WgradPlan w;
+    const int M = (int)(s.C * s.kh * s.kw);
+    const int bn = pick_bn((int)s.Co);
+    w.tiles_m = (M + 127) / 128;
+    w.tiles_n = ((int)s.Co + bn - 1) / bn;
+    w.kb_per_img = (int)((s.Ho * s.Wo + 31) / 32);
+    w.kb_total = (int)s.N * w.kb_per_img;
+    const int tiles = w.tiles_m * w.tiles_n;
+    int splits = tiles >= sms ? 1 : sms / tiles;
+    splits = std::max(1, std::min(splits, w.kb_total));
+    w.splits = splits;
+    w.ws_bytes = splits > 1 ? (size_t)splits * (size_t)s.Co * (size_t)M * sizeof(float) : 0;
+    return w;
+}
+
+int conv_wgrad(const mt_tensor* dy, const mt_tensor* x, const mt_tensor* dw, uint64_t stride, uint64_t pad, int mode,
+               void* workspace, size_t ws_bytes, cudaStream_t st, const char* who) {
+    int rc;
+    if ((rc = check4(dy, who, "grad_output")) || (rc = check4(x, who, "input")) || (rc = check4(dw, who, "grad_weight")))
+        return rc;
+    ConvShape s;
+    if ((rc = conv_shape(x, dw, dy, stride, pad, who, s))) return rc;
+    if (!is_contig(dw)) return fail(MT_EINVAL, "%s: grad_weight must be contiguous", who);
+    mt::conv::Params cp = conv_params(s);
+    cp.x = x->data + x->offset; fill_strides(cp.sx, x);
+    cp.dy = dy->data + dy->offset; fill_strides(cp.sdy, dy);
+    float* dwp = dw->data + dw->offset;
+    const int64_t total = s.Co * s.C * s.kh * s.kw;
+    if (total == 0) { t_path = "empty"; return MT_OK; }
+    mode = resolve_mode(mode);
+    DevInfo di = dev_info();
+    if (s.N * s.Ho * s.Wo == 0) {   // empty reduction: the gradient is zero
+        cudaError_t e = cudaMemsetAsync(dwp, 0, total * sizeof(float), st);
+        t_path = "zero";
+        return e == cudaSuccess ? MT_OK : cuda_fail(e, who);
+    }
+    if (mode == MT_STRICT_FP32 || di.cc != 100) {
+        if (mode != MT_STRICT_FP32) return fail(MT_EUNSUPPORTED, "%s: tensor-core conv needs sm_100a", who);
+        cp.out = dwp;
+        t_path = "conv_direct_wgrad_fp32";
+        return direct_launch(mt::conv::direct_wgrad_kernel, cp, total, st, who);
+    }
+    WgradPlan wp = wgrad_plan(s, di.sms);
+    cp.M = (int)(s.C * s.kh * s.kw); cp.Ncol = (int)s.Co; cp.K = (int)(s.N * s.Ho * s.Wo);
+    cp.tiles_m = wp.tiles_m; cp.tiles_n = wp.tiles_n;
+    cp.kb_per_img = wp.kb_per_img; cp.kb_total = wp.kb_total; cp.splits = wp.splits;
+    cp.num_units = (long long)wp.tiles_m * wp.tiles_n * wp.splits;
+    bool owned = false;
+    float* part = dwp;
+    if (wp.splits > 1) {
+        if (workspace) {
+            if (ws_bytes < wp.ws_bytes)
+                return fail(MT_EINVAL, "%s: workspace of %zu bytes < %zu needed", who, ws_bytes, wp.ws_bytes);
+            part = static_cast<float*>(workspace);
+        } else {
+            // Stream-ordered allocation from the device's default pool (capturable).
+            cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&part), wp.ws_bytes, st);
+            if (e != cudaSuccess) return cuda_fail(e, "conv wgrad workspace");
+            owned = true;
+        }
+    }
+    cp.out = part;
+    const int grid = (int)std::min<long long>(cp.num_units, di.sms);
+    const bool x3 = mode == MT_TF32X3;
+    const int bn = pick_bn(cp.Ncol);
+    rc = x3 ? launch_conv_bn<mt::conv::kWgrad, true>(cp, bn, grid, st) : launch_conv_bn<mt::conv::kWgrad, false>(cp, bn, grid, st);
+    if (rc == MT_OK && wp.splits > 1) {
+        const int blocks = (int)std::min<int64_t>((total + 255) / 256, 4 * di.sms);
+        mt::conv::splitk_reduce_kernel<<<blocks, 256, 0, st>>>(part, dwp, wp.splits, total);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess && e != cudaErrorStreamCaptureUnsupported) rc = cuda_fail(e, "splitk reduce");
+        else g_launches.fetch_add(1);
+    }
+    if (owned) cudaFreeAsync(part, st);
+    if (rc == MT_OK)
+        t_path = std::string("conv_umma_wgrad_") + (x3 ? "tf32x3" : "tf32") + " bn=" + std::to_string(bn) +
+                 " splits=" + std::to_string(wp.splits);
+    return rc;
+}
+
+int conv_bgrad(const mt_tensor* dy, const mt_tensor* db, cudaStream_t st, const char* who) {
+    int rc;
+    if ((rc = check4(dy, who, "grad_output"))) return rc;
+    if (!db || numel(db) != dy->shape[1]) return fail(MT_EINVAL, "%s: grad_bias must hold C_out elements", who);
+    if (!is_contig(db) || !db->data) return fail(MT_EINVAL, "%s: grad_bias must be contiguous", who);
+    const int N = (int)dy->shape[0], Co = (int)dy->shape[1];
+    const int64_t HW = (int64_t)dy->shape[2] * (int64_t)dy->shape[3];
+    if (Co == 0) return MT_OK;
+    // Spatial dims must be flat (stride W = 1, stride H = W) for the per-channel sweep.
+    if (HW > 1 && !(dy->strides[3] == 1 && dy->strides[2] == dy->shape[3]))
+        return fail(MT_EUNSUPPORTED, "%s: grad_output needs contiguous spatial dims", who);
+    mt::conv::bias_grad_kernel<<<Co, 256, 0, st>>>(dy->data + dy->offset, db->data + db->offset, N, Co, (int)HW,
+                                                   (int64_t)dy->strides[0], (int64_t)dy->strides[1]);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess && e != cudaErrorStreamCaptureUnsupported) return cuda_fail(e, "bias grad launch");
+    g_launches.fetch_add(1);
+    t_path = "conv_bias_grad";
+    return MT_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -411,6 +715,57 @@ MT_API int mt_gemm(const mt_tensor* A, const mt_tensor* B, const mt_tensor* C, c
     if (c.d[1] != a.d[1] || c.d[2] != b.d[2]) return fail(MT_EINVAL, "gemm: C shape mismatch");
     if (c.d[0] == 1) { a.s[0] = 0; b.s[0] = 0; c.s[0] = 0; }
     return gemm_from_views(a, b, c, bias, epi, mode, stream);
+}
+
+
+// ---- Conv2D: mirrors of include/TensorOps.hpp:708-712 and explicit-mode variants ----
+MT_API int mt_conv2d_gpu(const mt_tensor* in, const mt_tensor* w, const mt_tensor* bias, const mt_tensor* out,
+                         uint64_t stride, uint64_t padding, void* stream) {
+    return conv_fwd(in, w, bias, out, stride, padding, MT_MODE_DEFAULT, static_cast<cudaStream_t>(stream), "conv2d_gpu");
+}
+MT_API int mt_conv2d_gpu_strided(const mt_tensor* in, const mt_tensor* w, const mt_tensor* bias, const mt_tensor* out,
+                                 uint64_t stride, uint64_t padding, void* stream) {
+    return conv_fwd(in, w, bias, out, stride, padding, MT_MODE_DEFAULT, static_cast<cudaStream_t>(stream),
+                    "conv2d_gpu_strided");
+}
+MT_API int mt_conv2d_backward_input_gpu(const mt_tensor* dY, const mt_tensor* w, const mt_tensor* dX, uint64_t stride,
+                                        uint64_t padding, void* stream) {
+    return conv_dgrad(dY, w, dX, stride, padding, MT_MODE_DEFAULT, static_cast<cudaStream_t>(stream),
+                      "conv2d_backward_input_gpu");
+}
+MT_API int mt_conv2d_backward_weight_gpu(const mt_tensor* dY, const mt_tensor* x, const mt_tensor* dW, uint64_t stride,
+                                         uint64_t padding, void* stream) {
+    return conv_wgrad(dY, x, dW, stride, padding, MT_MODE_DEFAULT, nullptr, 0, static_cast<cudaStream_t>(stream),
+                      "conv2d_backward_weight_gpu");
+}
+MT_API int mt_conv2d_backward_bias_gpu(const mt_tensor* dY, const mt_tensor* db, void* stream) {
+    return conv_bgrad(dY, db, static_cast<cudaStream_t>(stream), "conv2d_backward_bias_gpu");
+}
+
+MT_API int mt_conv2d_fwd(const mt_tensor* x, const mt_tensor* w, const mt_tensor* bias, const mt_tensor* y,
+                         uint64_t stride, uint64_t padding, int mode, void* stream) {
+    if (mode < MT_MODE_DEFAULT || mode > MT_TF32X3) return fail(MT_EINVAL, "conv2d_fwd: bad mode %d", mode);
+    return conv_fwd(x, w, bias, y, stride, padding, mode, static_cast<cudaStream_t>(stream), "conv2d_fwd");
+}
+MT_API int mt_conv2d_dgrad(const mt_tensor* dy, const mt_tensor* w, const mt_tensor* dx, uint64_t stride,
+                           uint64_t padding, int mode, void* stream) {
+    if (mode < MT_MODE_DEFAULT || mode > MT_TF32X3) return fail(MT_EINVAL, "conv2d_dgrad: bad mode %d", mode);
+    return conv_dgrad(dy, w, dx, stride, padding, mode, static_cast<cudaStream_t>(stream), "conv2d_dgrad");
+}
+MT_API int mt_conv2d_wgrad(const mt_tensor* dy, const mt_tensor* x, const mt_tensor* dw, uint64_t stride,
+                           uint64_t padding, int mode, void* workspace, size_t ws_bytes, void* stream) {
+    if (mode < MT_MODE_DEFAULT || mode > MT_TF32X3) return fail(MT_EINVAL, "conv2d_wgrad: bad mode %d", mode);
+    return conv_wgrad(dy, x, dw, stride, padding, mode, workspace, ws_bytes, static_cast<cudaStream_t>(stream),
+                      "conv2d_wgrad");
+}
+MT_API size_t mt_conv2d_wgrad_workspace_bytes(const mt_tensor* dy, const mt_tensor* x, const mt_tensor* dw,
+                                              uint64_t stride, uint64_t padding, int mode) {
+    if (check4(dy, "wgrad_ws", "grad_output") || check4(x, "wgrad_ws", "input") || check4(dw, "wgrad_ws", "grad_weight"))
+        return 0;
+    ConvShape s;
+    if (conv_shape(x, dw, dy, stride, padding, "wgrad_ws", s)) return 0;
+    if (resolve_mode(mode) == MT_STRICT_FP32 || s.N * s.Ho * s.Wo == 0) return 0;
+    return wgrad_plan(s, dev_info().sms).ws_bytes;
 }
 
 MT_API int mt_set_default_mode(int mode) {

@@ -63,6 +63,25 @@ def lib() -> ctypes.CDLL:
     L.mt_linear_fwd_gpu.restype = ctypes.c_int
     L.mt_gemm.argtypes = [P, P, P, vp, ctypes.c_int, ctypes.c_int, vp]
     L.mt_gemm.restype = ctypes.c_int
+    u64 = ctypes.c_uint64
+    for name in ("mt_conv2d_gpu", "mt_conv2d_gpu_strided"):
+        fn = getattr(L, name)
+        fn.argtypes = [P, P, P, P, u64, u64, vp]
+        fn.restype = ctypes.c_int
+    for name in ("mt_conv2d_backward_input_gpu", "mt_conv2d_backward_weight_gpu"):
+        fn = getattr(L, name)
+        fn.argtypes = [P, P, P, u64, u64, vp]
+        fn.restype = ctypes.c_int
+    L.mt_conv2d_backward_bias_gpu.argtypes = [P, P, vp]
+    L.mt_conv2d_backward_bias_gpu.restype = ctypes.c_int
+    L.mt_conv2d_fwd.argtypes = [P, P, P, P, u64, u64, ctypes.c_int, vp]
+    L.mt_conv2d_fwd.restype = ctypes.c_int
+    L.mt_conv2d_dgrad.argtypes = [P, P, P, u64, u64, ctypes.c_int, vp]
+    L.mt_conv2d_dgrad.restype = ctypes.c_int
+    L.mt_conv2d_wgrad.argtypes = [P, P, P, u64, u64, ctypes.c_int, vp, ctypes.c_size_t, vp]
+    L.mt_conv2d_wgrad.restype = ctypes.c_int
+    L.mt_conv2d_wgrad_workspace_bytes.argtypes = [P, P, P, u64, u64, ctypes.c_int]
+    L.mt_conv2d_wgrad_workspace_bytes.restype = ctypes.c_size_t
     L.mt_set_default_mode.argtypes = [ctypes.c_int]
     L.mt_set_default_mode.restype = ctypes.c_int
     L.mt_get_default_mode.restype = ctypes.c_int
@@ -213,6 +232,89 @@ def linear_backward(x, W, dY, mode=MODE_DEFAULT, stream=None):
     db = torch.empty((1, dY.shape[1]), dtype=torch.float32, device=dY.device)
     gemm(ones, dY, db, mode=STRICT_FP32, stream=stream)
     return dX, dW, db
+
+
+# ---- Conv2D (include/TensorOps.hpp:708-712, :1076-1149) --------------------------------
+
+def out_size(n, pad, k, stride):
+    """include/TensorOps.hpp:17-20 safe_out_size."""
+    return 0 if n + 2 * pad < k else (n + 2 * pad - k) // stride + 1
+
+
+def _mode(mode):
+    return MODES[mode] if isinstance(mode, str) else int(mode)
+
+
+def conv2d_gpu(x, w, bias, y, stride, padding, stream=None):
+    """include/TensorOps.hpp:708; y is caller-allocated [N, C_out, H_out, W_out]."""
+    _check(lib().mt_conv2d_gpu(_ref(view(x)), _ref(view(w)), _ref(view(bias)), _ref(view(y)),
+                               stride, padding, _stream(stream)))
+
+
+def conv2d_gpu_strided(x, w, bias, y, stride, padding, stream=None):
+    """include/TensorOps.hpp:709 (non-contiguous input views)."""
+    _check(lib().mt_conv2d_gpu_strided(_ref(view(x)), _ref(view(w)), _ref(view(bias)), _ref(view(y)),
+                                       stride, padding, _stream(stream)))
+
+
+def conv2d_backward_input_gpu(dy, w, dx, stride, padding, stream=None):
+    """include/TensorOps.hpp:710."""
+    _check(lib().mt_conv2d_backward_input_gpu(_ref(view(dy)), _ref(view(w)), _ref(view(dx)), stride, padding,
+                                              _stream(stream)))
+
+
+def conv2d_backward_weight_gpu(dy, x, dw, stride, padding, stream=None):
+    """include/TensorOps.hpp:711."""
+    _check(lib().mt_conv2d_backward_weight_gpu(_ref(view(dy)), _ref(view(x)), _ref(view(dw)), stride, padding,
+                                               _stream(stream)))
+
+
+def conv2d_backward_bias_gpu(dy, db, stream=None):
+    """include/TensorOps.hpp:712."""
+    _check(lib().mt_conv2d_backward_bias_gpu(_ref(view(dy)), _ref(view(db)), _stream(stream)))
+
+
+def conv2d(x, w, bias=None, stride=1, padding=0, mode=MODE_DEFAULT, stream=None):
+    """conv2d(input, weight, bias, stride, padding) -> output (include/TensorOps.hpp:1076-1110)."""
+    if x.dim() != 4 or w.dim() != 4:
+        raise ValueError("conv2d expects 4-D input and weight")
+    N, _, H, W = x.shape
+    Co, _, kh, kw = w.shape
+    y = torch.empty((N, Co, out_size(H, padding, kh, stride), out_size(W, padding, kw, stride)),
+                    dtype=torch.float32, device=x.device)
+    _check(lib().mt_conv2d_fwd(_ref(view(x)), _ref(view(w)), _ref(view(bias)), _ref(view(y)), stride, padding,
+                               _mode(mode), _stream(stream)))
+    return y
+
+
+def conv2d_backward(dy, x, w, stride=1, padding=0, need=("input", "weight", "bias"), mode=MODE_DEFAULT,
+                    workspace=None, stream=None):
+    """Conv2DBackward (include/Autograd.hpp:481-509): (dx, dw, db), each None unless asked for."""
+    dx = dw = db = None
+    s = _stream(stream)
+    if "input" in need:
+        dx = torch.empty_like(x, memory_format=torch.contiguous_format)
+        _check(lib().mt_conv2d_dgrad(_ref(view(dy)), _ref(view(w)), _ref(view(dx)), stride, padding, _mode(mode), s))
+    if "weight" in need:
+        dw = torch.empty(w.shape, dtype=torch.float32, device=w.device)
+        ws_ptr = workspace.data_ptr() if workspace is not None else None
+        ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
+        _check(lib().mt_conv2d_wgrad(_ref(view(dy)), _ref(view(x)), _ref(view(dw)), stride, padding, _mode(mode),
+                                     ws_ptr, ws_bytes, s))
+    if "bias" in need:
+        db = torch.empty((dy.shape[1],), dtype=torch.float32, device=dy.device)
+        _check(lib().mt_conv2d_backward_bias_gpu(_ref(view(dy)), _ref(view(db)), s))
+    return dx, dw, db
+
+
+def conv2d_wgrad_workspace_bytes(dy, x, w_shape, stride, padding, mode=MODE_DEFAULT):
+    dw = torch.empty(0)
+    v = view(dw)
+    v.ndim = 4
+    for i, d in enumerate(w_shape):
+        v.shape[i] = d
+    return int(lib().mt_conv2d_wgrad_workspace_bytes(_ref(view(dy)), _ref(view(x)), _ref(v), stride, padding,
+                                                     _mode(mode)))
 
 
 # ---- settings and diagnostics ---------------------------------------------------------

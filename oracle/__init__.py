@@ -69,7 +69,7 @@ class Port:
         L.orc_bmm.argtypes = [_f, _i64, _i64, _i64, _f, _i64, _i64, _i64, _f, _i64, _i64, _i64, _i64]
         L.orc_linear_fwd.argtypes = [_f, _f, _f, _f, _i64, _i64, _i64]
         L.orc_conv2d_fwd.argtypes = [_f, _f, _f, _f] + [_i64] * 9 + [ctypes.c_int]
-        L.orc_conv2d_bwd_input.argtypes = [_f, _f, _f] + [_i64] * 9
+        L.orc_conv2d_bwd_input.argtypes = [_f, _f, _f] + [_i64] * 9 + [ctypes.c_int]
         L.orc_conv2d_bwd_weight.argtypes = [_f, _f, _f] + [_i64] * 9 + [ctypes.c_int]
         L.orc_conv2d_bwd_bias.argtypes = [_f, _f, _i64, _i64, _i64, _i64]
 
@@ -128,11 +128,11 @@ class Port:
                                 N, C, H, W, Co, kh, kw, stride, pad, threads)
         return y
 
-    def conv2d_bwd_input(self, dy, w, x_shape, stride, pad):
+    def conv2d_bwd_input(self, dy, w, x_shape, stride, pad, threads=1):
         N, C, H, W = x_shape
         Co, _, kh, kw = w.shape
         dx = np.empty((N, C, H, W), np.float32)
-        self.lib.orc_conv2d_bwd_input(_p(dy), _p(w), _p(dx), N, C, H, W, Co, kh, kw, stride, pad)
+        self.lib.orc_conv2d_bwd_input(_p(dy), _p(w), _p(dx), N, C, H, W, Co, kh, kw, stride, pad, threads)
         return dx
 
     def conv2d_bwd_weight(self, dy, x, w_shape, stride, pad, threads=1):

@@ -198,15 +198,15 @@ void orc_conv2d_fwd(const float* x, const float* w, const float* bias, float* y,
 }
 
 /* include/TensorOps.hpp:319-356 -- gi zero-filled, then scatter-add in the order
- * n, c_out, y, x, c_in, r, s. */
-void orc_conv2d_bwd_input(const float* dy, const float* w, float* dx,
-                          int64_t N, int64_t C, int64_t H, int64_t W,
-                          int64_t Cout, int64_t kH, int64_t kW,
-                          int64_t stride, int64_t pad) {
-    int64_t Ho = orc_conv_out_size(H, pad, kH, stride);
-    int64_t Wo = orc_conv_out_size(W, pad, kW, stride);
-    memset(dx, 0, (size_t)(N * C * H * W) * sizeof(float));
-    for (int64_t n = 0; n < N; ++n)
+ * n, c_out, y, x, c_in, r, s. Images are independent, so threads split n without
+ * changing the order of additions into any element. */
+static void conv_dgrad_range(const conv_job* j) {
+    const float* dy = j->x;   /* dy stored in the x slot for this job type */
+    const float* w = j->w;
+    float* dx = j->y;
+    int64_t C = j->C, H = j->H, W = j->W, Cout = j->Cout, kH = j->kH, kW = j->kW;
+    int64_t stride = j->stride, pad = j->pad, Ho = j->Ho, Wo = j->Wo;
+    for (int64_t n = j->n0; n < j->n1; ++n)
         for (int64_t co = 0; co < Cout; ++co)
             for (int64_t y = 0; y < Ho; ++y)
                 for (int64_t x = 0; x < Wo; ++x) {
@@ -224,6 +224,8 @@ void orc_conv2d_bwd_input(const float* dy, const float* w, float* dx,
                             }
                 }
 }
+
+static void* conv_dgrad_worker(void* p) { conv_dgrad_range((conv_job*)p); return NULL; }
 
 void orc_conv2d_bwd_weight(const float* dy, const float* x, float* dw,
                            int64_t N, int64_t C, int64_t H, int64_t W,
@@ -252,4 +254,19 @@ void orc_conv2d_bwd_bias(const float* dy, float* db,
                     sum += dy[n * (Cout * Hout * Wout) + c * (Hout * Wout) + y * Wout + x];
             db[c] += sum;
         }
+}
+
+void orc_conv2d_bwd_input(const float* dy, const float* w, float* dx,
+                          int64_t N, int64_t C, int64_t H, int64_t W,
+                          int64_t Cout, int64_t kH, int64_t kW,
+                          int64_t stride, int64_t pad, int threads) {
+    conv_job j;
+    memset(&j, 0, sizeof j);
+    j.x = dy; j.w = w; j.y = dx;
+    j.N = N; j.C = C; j.H = H; j.W = W; j.Cout = Cout; j.kH = kH; j.kW = kW;
+    j.stride = stride; j.pad = pad;
+    j.Ho = orc_conv_out_size(H, pad, kH, stride);
+    j.Wo = orc_conv_out_size(W, pad, kW, stride);
+    memset(dx, 0, (size_t)(N * C * H * W) * sizeof(float));
+    run_split(j, N, threads, conv_dgrad_worker);
 }

@@ -68,7 +68,7 @@ void orc_conv2d_fwd(const float* x, const float* w, const float* bias, float* y,
 void orc_conv2d_bwd_input(const float* dy, const float* w, float* dx,
                           int64_t N, int64_t C, int64_t H, int64_t W,
                           int64_t Cout, int64_t kH, int64_t kW,
-                          int64_t stride, int64_t pad);
+                          int64_t stride, int64_t pad, int threads);
 
 /* include/TensorOps.hpp:358-396 conv2d_backward_weight_cpu. */
 void orc_conv2d_bwd_weight(const float* dy, const float* x, float* dw,

@@ -1,0 +1,162 @@
+"""GPU parity tests for Conv2D as implicit GEMM (forward, input-grad, weight-grad,
+bias-grad) through the C ABI, against the CPU oracle and the reference's golden vectors."""
+import os
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from minitensor_b200 import inputs
+from parity import check, dev, host
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "golden_v1.npz")
+MODES = ["strict", "tf32", "tf32x3"]
+THREADS = max(1, min(32, os.cpu_count() or 1))
+
+
+@pytest.fixture(scope="module")
+def gold():
+    return np.load(GOLDEN)
+
+
+# Error denominators |x|*|w| for each product (float64; they only scale the error).
+def d_fwd(x, w, s, p):
+    return F.conv2d(torch.from_numpy(np.abs(x)).double(), torch.from_numpy(np.abs(w)).double(),
+                    stride=s, padding=p).numpy()
+
+
+def d_dgrad(dy, w, x_shape, s, p):
+    return torch.nn.grad.conv2d_input(x_shape, torch.from_numpy(np.abs(w)).double(),
+                                      torch.from_numpy(np.abs(dy)).double(), stride=s, padding=p).numpy()
+
+
+def d_wgrad(dy, x, w_shape, s, p):
+    return torch.nn.grad.conv2d_weight(torch.from_numpy(np.abs(x)).double(), w_shape,
+                                       torch.from_numpy(np.abs(dy)).double(), stride=s, padding=p).numpy()
+
+
+def run_all(eng, x, w, b, dy, s, p, mode):
+    xd, wd = dev(x), dev(w)
+    bd = dev(b) if b is not None else None
+    y = eng.conv2d(xd, wd, bd, s, p, mode=mode)
+    dx, dw, db = eng.conv2d_backward(dev(dy), xd, wd, s, p, mode=mode)
+    return host(y), host(dx), host(dw), host(db)
+
+
+@pytest.mark.parametrize("mode", MODES)
+def test_golden_conv(eng, gold, mode):
+    # spatial_test.cpp:155-185 known answer [12, 16, 24, 28].
+    y = eng.conv2d(dev(gold["convk_x"]), dev(gold["convk_w"]), dev(gold["convk_b"]), 1, 0, mode=mode)
+    assert np.allclose(host(y).ravel(), [12, 16, 24, 28], rtol=1e-6)
+    # spatial_test.cpp:209-230 device equivalence (stride 2, pad 1): rtol 1e-3, atol 1e-4.
+    x, w, b = gold["conveq_x"], gold["conveq_w"], gold["conveq_b"]
+    y = host(eng.conv2d(dev(x), dev(w), dev(b), 2, 1, mode=mode))
+    ref = gold["conveq_y"]
+    assert np.all(np.abs(y - ref) <= 1e-4 + 1e-3 * np.abs(ref))
+    for i in range(4):
+        s, p = gold[f"conv{i}_meta"].tolist()
+        x, w, b, dy = (gold[f"conv{i}_{k}"] for k in ("x", "w", "b", "dy"))
+        y, dx, dw, db = run_all(eng, x, w, b, dy, s, p, mode)
+        K = x.shape[1] * w.shape[2] * w.shape[3]
+        check(mode, y, gold[f"conv{i}_y"], d_fwd(x, w, s, p) + np.abs(b)[None, :, None, None], K, f"conv{i} fwd")
+        check(mode, dx, gold[f"conv{i}_dx"], d_dgrad(dy, w, x.shape, s, p), w.shape[0] * w.shape[2] * w.shape[3],
+              f"conv{i} dgrad")
+        check(mode, dw, gold[f"conv{i}_dw"], d_wgrad(dy, x, w.shape, s, p), dy.shape[0] * dy.shape[2] * dy.shape[3],
+              f"conv{i} wgrad")
+        assert np.allclose(db, gold[f"conv{i}_db"], rtol=1e-5, atol=1e-5), f"conv{i} bias grad"
+
+
+@pytest.mark.parametrize("mode", ["tf32", "tf32x3"])
+def test_config4_resnet_3x3(eng, port, mode):
+    x, w, b, dy = inputs.config4()
+    xd, wd, dyd = dev(x), dev(w), dev(dy)
+    y = host(eng.conv2d(xd, wd, dev(b), 1, 1, mode=mode))
+    assert eng.last_path().startswith("conv_umma_fwd_" + mode), eng.last_path()
+    yr = port.conv2d(x, w, b, 1, 1, threads=THREADS)
+    check(mode, y, yr, d_fwd(x, w, 1, 1), 576, "config4 fwd")
+    _, dw, _ = eng.conv2d_backward(dyd, xd, wd, 1, 1, need=("weight",), mode=mode)
+    path = eng.last_path()
+    dwr = port.conv2d_bwd_weight(dy, x, w.shape, 1, 1, threads=THREADS)
+    check(mode, host(dw), dwr, d_wgrad(dy, x, w.shape, 1, 1), 32 * 56 * 56, f"config4 wgrad ({path})")
+    dx, _, _ = eng.conv2d_backward(dyd, xd, wd, 1, 1, need=("input",), mode=mode)
+    dxr = port.conv2d_bwd_input(dy, w, x.shape, 1, 1, threads=THREADS)
+    check(mode, host(dx), dxr, d_dgrad(dy, w, x.shape, 1, 1), 576, "config4 dgrad")
+
+
+@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("shape", [
+    # N, C, H, W, Co, k, stride, pad
+    (1, 3, 7, 9, 5, 3, 1, 1),
+    (2, 17, 13, 11, 33, 3, 2, 1),
+    (3, 8, 10, 10, 130, 1, 1, 0),
+    (2, 5, 9, 12, 7, 5, 2, 2),
+    (1, 64, 14, 14, 256, 3, 1, 1),
+    (4, 2, 6, 6, 3, 7, 1, 3),
+])
+def test_conv_shapes(eng, port, mode, shape):
+    N, C, H, W, Co, k, s, p = shape
+    x = inputs.normal((N, C, H, W), 1.0, 1000 + C)
+    w = inputs.normal((Co, C, k, k), float(np.sqrt(2.0 / (C * k * k))), 1100 + Co)
+    b = inputs.normal((Co,), 0.1, 1200)
+    Ho, Wo = (H + 2 * p - k) // s + 1, (W + 2 * p - k) // s + 1
+    dy = inputs.normal((N, Co, Ho, Wo), 1.0, 1300)
+    y, dx, dw, db = run_all(eng, x, w, b, dy, s, p, mode)
+    K = C * k * k
+    check(mode, y, port.conv2d(x, w, b, s, p), d_fwd(x, w, s, p) + np.abs(b)[None, :, None, None], K, f"{shape} fwd")
+    check(mode, dx, port.conv2d_bwd_input(dy, w, x.shape, s, p), d_dgrad(dy, w, x.shape, s, p), Co * k * k,
+          f"{shape} dgrad")
+    check(mode, dw, port.conv2d_bwd_weight(dy, x, w.shape, s, p), d_wgrad(dy, x, w.shape, s, p), N * Ho * Wo,
+          f"{shape} wgrad")
+    assert np.allclose(db, port.conv2d_bwd_bias(dy), rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("mode", ["tf32x3", "strict"])
+def test_strided_input_view(eng, port, mode):
+    # spatial_test.cpp:259-281: an NHWC buffer viewed as NCHW via transposes (non-contiguous).
+    nhwc = (np.arange(2 * 16 * 16 * 3, dtype=np.float32) * np.float32(0.1)).reshape(2, 16, 16, 3)
+    xv = dev(nhwc).transpose(1, 3).transpose(2, 3)
+    assert not xv.is_contiguous()
+    w = np.full((8, 3, 3, 3), 0.5, np.float32)
+    b = np.zeros(8, np.float32)
+    y = torch.empty(2, 8, 16, 16, device="cuda")
+    eng.set_default_mode(mode)
+    try:
+        eng.conv2d_gpu_strided(xv, dev(w), dev(b), y, 1, 1)
+    finally:
+        eng.set_default_mode("tf32x3")
+    x = np.ascontiguousarray(nhwc.transpose(0, 3, 1, 2))
+    check(mode, host(y), port.conv2d(x, w, b, 1, 1), d_fwd(x, w, 1, 1), 27, "strided view")
+
+
+def test_explicit_workspace_matches_pool(eng):
+    x, w, _, dy = (a[:4] if a.ndim == 4 and a.shape[0] == 32 else a for a in inputs.config4())
+    xd, wd, dyd = dev(x), dev(w), dev(dy)
+    nbytes = eng.conv2d_wgrad_workspace_bytes(dyd, xd, w.shape, 1, 1, mode="tf32x3")
+    assert nbytes > 0
+    ws = torch.empty(nbytes // 4 + 1, device="cuda")
+    _, dw1, _ = eng.conv2d_backward(dyd, xd, wd, 1, 1, need=("weight",), mode="tf32x3", workspace=ws)
+    _, dw2, _ = eng.conv2d_backward(dyd, xd, wd, 1, 1, need=("weight",), mode="tf32x3")
+    assert torch.equal(dw1, dw2)   # same split plan and reduction order: bit-identical
+    with pytest.raises(ValueError, match="workspace"):
+        eng.conv2d_backward(dyd, xd, wd, 1, 1, need=("weight",), mode="tf32x3", workspace=ws[:8])
+
+
+def test_conv_errors_and_empty(eng):
+    x = torch.zeros(2, 3, 8, 8, device="cuda")
+    w = torch.zeros(4, 5, 3, 3, device="cuda")
+    with pytest.raises(ValueError, match="C_in"):
+        eng.conv2d(x, w, None, 1, 1)
+    w = torch.zeros(4, 3, 3, 3, device="cuda")
+    y = torch.zeros(2, 4, 7, 7, device="cuda")
+    with pytest.raises(ValueError, match="output must be"):
+        eng.conv2d_gpu(x, w, None, y, 1, 1)
+    # Kernel larger than the padded input: safe_out_size gives 0 -> empty output.
+    y = eng.conv2d(torch.zeros(1, 3, 2, 2, device="cuda"), torch.zeros(4, 3, 5, 5, device="cuda"), None, 1, 1)
+    assert tuple(y.shape) == (1, 4, 0, 0)
+
+
+def test_device_status_clean_after_conv(eng):
+    assert eng.device_status(reset=True) == 0
