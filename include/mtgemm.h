@@ -140,6 +140,8 @@ MT_API int mt_conv2d_dgrad(const mt_tensor* dy, const mt_tensor* w, const mt_ten
  * mt_conv2d_wgrad_workspace_bytes(...) bytes of device memory, used only by this call. */
 MT_API int mt_conv2d_wgrad(const mt_tensor* dy, const mt_tensor* x, const mt_tensor* dw, uint64_t stride,
                            uint64_t padding, int mode, void* workspace, size_t ws_bytes, void* stream);
+/* Workspace size for mt_conv2d_wgrad (0: none needed or invalid shapes); reads only the
+ * shapes of its arguments, so their data pointers may be NULL. */
 MT_API size_t mt_conv2d_wgrad_workspace_bytes(const mt_tensor* dy, const mt_tensor* x, const mt_tensor* dw,
                                               uint64_t stride, uint64_t padding, int mode);
 
@@ -149,6 +151,29 @@ MT_API size_t mt_conv2d_wgrad_workspace_bytes(const mt_tensor* dy, const mt_tens
  * pointer of M (BIAS_ROW) or N (BIAS_COL) floats, shared by all batches. */
 MT_API int mt_gemm(const mt_tensor* A, const mt_tensor* B, const mt_tensor* C,
                    const float* bias, int epi, int mode, void* stream);
+
+/* ---- multi-GPU: a column-sharded GEMM whose epilogue all-gathers C ------------------
+ * The reference is single-GPU (README.md:273); these entry points have no counterpart
+ * there. One process per GPU: rank r holds A and the column shard B[:, n0:n1], computes
+ * C[:, n0:n1] and its epilogue stores every tile into its own C and into each peer's C
+ * (CUDA IPC peer pointers over NVLink), then mt_peer_barrier makes the writes visible. */
+
+/* IPC handle (64 bytes) of the allocation containing dptr, plus dptr's byte offset in it. */
+MT_API int mt_ipc_get_handle(const void* dptr, void* handle_out, uint64_t* offset_out);
+/* Maps a peer's handle into this process; *dptr_out = mapped base + offset. */
+MT_API int mt_ipc_open(const void* handle, uint64_t offset, void** dptr_out);
+MT_API int mt_ipc_close(void* dptr, uint64_t offset);
+
+/* C = epi(A * B) written to C and to extra_dst[0..nextra) (nextra < 8), each a device
+ * pointer (peer-mapped allowed) laid out with C's row stride. */
+MT_API int mt_gemm_multi(const mt_tensor* A, const mt_tensor* B, const mt_tensor* C, float* const* extra_dst,
+                         int nextra, const float* bias, int epi, int mode, void* stream);
+
+/* Stream-ordered cross-GPU barrier: flags[d] is rank d's array of `world` ints (peer-mapped,
+ * zero-initialised). Rank `rank` stores `epoch` into flags[d][rank] for every d, then waits
+ * until flags[rank][*] == epoch. The wait gives up after timeout_ns and records status 6 in
+ * the device status word (mt_device_status) instead of hanging. */
+MT_API int mt_peer_barrier(int* const* flags, int rank, int world, int epoch, uint64_t timeout_ns, void* stream);
 
 /* ---- process settings and diagnostics ---------------------------------------------- */
 

@@ -200,7 +200,7 @@ int launch_umma_inst(const CUtensorMap& ta, const CUtensorMap& tb, const mt::umm
 
 // Returns MT_OK when launched, MT_EUNSUPPORTED when the views do not fit the tensor-core
 // kernel (the caller then uses the SIMT kernel).
-int launch_umma(const GemmProblem& p, bool x3, cudaStream_t st) {
+int launch_umma(const GemmProblem& p, bool x3, cudaStream_t st, float* const* extra_dst = nullptr, int nextra = 0) {
     DevInfo di = dev_info();
     if (di.cc != 100) return fail(MT_EUNSUPPORTED, "umma: device is sm_%d, kernel built for sm_100a", di.cc);
     if (p.M > INT32_MAX || p.N > INT32_MAX || p.K > INT32_MAX || p.batch > INT32_MAX)
@@ -258,9 +258,17 @@ int launch_umma(const GemmProblem& p, bool x3, cudaStream_t st) {
     mt::umma::Params up;
     up.M = (int)p.M; up.N = (int)p.N; up.K = (int)p.K; up.batch = (int)p.batch;
     up.a_batched = a_batched; up.b_batched = b_batched;
-    up.C = p.C; up.sc_b = p.sc_b; up.sc_m = p.sc_m;
+    up.ndst = 1 + nextra;
+    up.dst[0] = p.C;
+    bool dst_aligned = aligned16(p.C);
+    for (int d = 0; d < nextra; ++d) {
+        up.dst[1 + d] = extra_dst[d];
+        dst_aligned = dst_aligned && aligned16(extra_dst[d]);
+    }
+    for (int d = up.ndst; d < mt::umma::kMaxDst; ++d) up.dst[d] = nullptr;
+    up.sc_b = p.sc_b; up.sc_m = p.sc_m;
     up.bias = p.bias; up.epi = p.epi;
-    up.vec_store = aligned16(p.C) && p.sc_m % 4 == 0 && (p.batch == 1 || p.sc_b % 4 == 0) && p.N % 4 == 0;
+    up.vec_store = dst_aligned && p.sc_m % 4 == 0 && (p.batch == 1 || p.sc_b % 4 == 0) && p.N % 4 == 0;
     up.tiles_m = (int)tiles_m;
     up.tiles_n = (int)((p.N + bn - 1) / bn);
     up.num_tiles = (long long)up.tiles_m * up.tiles_n * p.batch;
@@ -649,6 +657,55 @@ int conv_bgrad(const mt_tensor* dy, const mt_tensor* db, cudaStream_t st, const 
     return MT_OK;
 }
 
+
+// ------------------------------- multi-GPU ----------------------------------------
+namespace peer {
+struct Flags {
+    int* f[mt::umma::kMaxDst];   // f[d] = rank d's flag array (world ints), peer-mapped
+};
+
+// Rank `rank` raises its flag in every rank's array, then waits (bounded) until every
+// rank has raised its flag in the local array. Stream order puts this after the GEMM
+// kernel whose epilogue wrote into the peers' C buffers; the system-scope fence and
+// release/acquire make those writes visible before anyone reads C.
+__global__ void barrier_kernel(Flags fl, int rank, int world, int epoch, unsigned long long timeout_ns) {
+    const int d = threadIdx.x;
+    if (d < world) {
+        __threadfence_system();
+        asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(fl.f[d] + rank), "r"(epoch) : "memory");
+    }
+    __syncwarp();
+    if (d < world) {
+        const int* mine = fl.f[rank] + d;
+        const unsigned long long t0 = mt::globaltimer_ns();
+        for (;;) {
+            int v;
+            asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+            if (v == epoch) break;
+            if (mt::globaltimer_ns() - t0 > timeout_ns) {
+                atomicCAS(&mt::g_dev_status, 0, mt::kDevTimeoutPeer);
+                break;
+            }
+        }
+    }
+}
+}  // namespace peer
+
+typedef CUresult (*GetAddressRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+GetAddressRangeFn addr_range_fn() {
+    static GetAddressRangeFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<GetAddressRangeFn>(p);
+    });
+    return fn;
+}
+
 }  // namespace
 
 extern "C" {
@@ -760,12 +817,105 @@ MT_API int mt_conv2d_wgrad(const mt_tensor* dy, const mt_tensor* x, const mt_ten
 }
 MT_API size_t mt_conv2d_wgrad_workspace_bytes(const mt_tensor* dy, const mt_tensor* x, const mt_tensor* dw,
                                               uint64_t stride, uint64_t padding, int mode) {
-    if (check4(dy, "wgrad_ws", "grad_output") || check4(x, "wgrad_ws", "input") || check4(dw, "wgrad_ws", "grad_weight"))
-        return 0;
+    // Shapes only: no pointer is dereferenced, so data may be NULL here.
+    if (!dy || !x || !dw || dy->ndim != 4 || x->ndim != 4 || dw->ndim != 4) return 0;
     ConvShape s;
     if (conv_shape(x, dw, dy, stride, padding, "wgrad_ws", s)) return 0;
     if (resolve_mode(mode) == MT_STRICT_FP32 || s.N * s.Ho * s.Wo == 0) return 0;
     return wgrad_plan(s, dev_info().sms).ws_bytes;
+}
+
+
+// ---- multi-GPU: peer memory and the GEMM that writes every rank's output -------------
+
+MT_API int mt_ipc_get_handle(const void* dptr, void* handle_out, uint64_t* offset_out) {
+    if (!dptr || !handle_out || !offset_out) return fail(MT_EINVAL, "ipc_get_handle: null argument");
+    GetAddressRangeFn range = addr_range_fn();
+    if (!range) return fail(MT_EUNSUPPORTED, "ipc_get_handle: cuMemGetAddressRange unavailable");
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (range(&base, &size, reinterpret_cast<CUdeviceptr>(dptr)) != CUDA_SUCCESS)
+        return fail(MT_EINVAL, "ipc_get_handle: not a device allocation");
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+    memcpy(handle_out, &h, sizeof h);
+    *offset_out = reinterpret_cast<uint64_t>(dptr) - static_cast<uint64_t>(base);
+    return MT_OK;
+}
+
+MT_API int mt_ipc_open(const void* handle, uint64_t offset, void** dptr_out) {
+    if (!handle || !dptr_out) return fail(MT_EINVAL, "ipc_open: null argument");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof h);
+    void* base = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+    *dptr_out = static_cast<char*>(base) + offset;
+    return MT_OK;
+}
+
+MT_API int mt_ipc_close(void* dptr, uint64_t offset) {
+    cudaError_t e = cudaIpcCloseMemHandle(static_cast<char*>(dptr) - offset);
+    return e == cudaSuccess ? MT_OK : cuda_fail(e, "cudaIpcCloseMemHandle");
+}
+
+MT_API int mt_gemm_multi(const mt_tensor* A, const mt_tensor* B, const mt_tensor* C, float* const* extra_dst,
+                         int nextra, const float* bias, int epi, int mode, void* stream) {
+    if (nextra < 0 || nextra >= mt::umma::kMaxDst) return fail(MT_EINVAL, "gemm_multi: 0 <= nextra < %d", mt::umma::kMaxDst);
+    if (nextra && !extra_dst) return fail(MT_EINVAL, "gemm_multi: extra_dst is null");
+    for (int i = 0; i < nextra; ++i)
+        if (!extra_dst[i]) return fail(MT_EINVAL, "gemm_multi: extra_dst[%d] is null", i);
+    if (mode < MT_MODE_DEFAULT || mode > MT_TF32X3) return fail(MT_EINVAL, "gemm_multi: bad mode %d", mode);
+    if (epi & ~7) return fail(MT_EINVAL, "gemm_multi: bad epilogue flags %d", epi);
+    View a, b, c;
+    int rc;
+    if ((rc = to_view(A, 2, "gemm_multi A", a)) || (rc = to_view(B, 2, "gemm_multi B", b)) ||
+        (rc = to_view(C, 2, "gemm_multi C", c)))
+        return rc;
+    if (a.d[2] != b.d[1]) return fail(MT_EINVAL, "gemm_multi: inner dimension mismatch (A.K != B.K)");
+    if (c.d[1] != a.d[1] || c.d[2] != b.d[2]) return fail(MT_EINVAL, "gemm_multi: C shape mismatch");
+    if (c.s[2] != 1 && c.d[2] > 1) return fail(MT_EINVAL, "gemm_multi: C rows must be contiguous");
+    GemmProblem p;
+    p.A = a.ptr; p.sa_b = 0; p.sa_m = a.s[1]; p.sa_k = a.s[2];
+    p.B = b.ptr; p.sb_b = 0; p.sb_k = b.s[1]; p.sb_n = b.s[2];
+    p.C = const_cast<float*>(c.ptr); p.sc_b = 0; p.sc_m = c.s[1]; p.sc_n = 1;
+    p.M = a.d[1]; p.K = a.d[2]; p.N = b.d[2]; p.batch = 1;
+    p.bias = bias; p.epi = epi;
+    if (p.M == 0 || p.N == 0) return MT_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int m = resolve_mode(mode);
+    if (m != MT_STRICT_FP32 && p.K > 0) {
+        std::string saved = t_err;
+        rc = launch_umma(p, m == MT_TF32X3, st, extra_dst, nextra);
+        if (rc == MT_OK) { t_path += " +" + std::to_string(nextra) + " peers"; return MT_OK; }
+        if (rc != MT_EUNSUPPORTED) return rc;
+        t_err = saved;
+    }
+    // Local product, then one 2-D copy per peer (stream-ordered, over NVLink).
+    if ((rc = run_gemm(p, m, st))) return rc;
+    for (int i = 0; i < nextra; ++i) {
+        cudaError_t e = cudaMemcpy2DAsync(extra_dst[i], p.sc_m * 4, p.C, p.sc_m * 4, p.N * 4, p.M,
+                                          cudaMemcpyDeviceToDevice, st);
+        if (e != cudaSuccess) return cuda_fail(e, "gemm_multi peer copy");
+    }
+    t_path += " +" + std::to_string(nextra) + " peer copies";
+    return MT_OK;
+}
+
+MT_API int mt_peer_barrier(int* const* flags, int rank, int world, int epoch, uint64_t timeout_ns, void* stream) {
+    if (world < 1 || world > mt::umma::kMaxDst || rank < 0 || rank >= world || !flags)
+        return fail(MT_EINVAL, "peer_barrier: bad rank/world");
+    peer::Flags fl;
+    for (int d = 0; d < mt::umma::kMaxDst; ++d) fl.f[d] = d < world ? flags[d] : nullptr;
+    for (int d = 0; d < world; ++d)
+        if (!fl.f[d]) return fail(MT_EINVAL, "peer_barrier: flags[%d] is null", d);
+    peer::barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(fl, rank, world, epoch,
+                                                                          (unsigned long long)timeout_ns);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess && e != cudaErrorStreamCaptureUnsupported) return cuda_fail(e, "peer barrier launch");
+    g_launches.fetch_add(1);
+    return MT_OK;
 }
 
 MT_API int mt_set_default_mode(int mode) {

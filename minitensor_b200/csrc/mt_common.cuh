@@ -21,6 +21,7 @@ enum DevStatus : int {
     kDevTimeoutAccFull = 3,   // epilogue waited too long for an accumulator
     kDevTimeoutAccEmpty = 4,  // MMA issuer waited too long for a drained accumulator
     kDevTimeoutMisc = 5,
+    kDevTimeoutPeer = 6,      // a peer GPU never raised its flag in mt_peer_barrier
 };
 
 // Defined here: every kernel of the library is compiled in the single translation unit

@@ -29,12 +29,18 @@ namespace mt {
 namespace umma {
 
 constexpr int BM = 128;
+constexpr int kMaxDst = 8;      // output copies (one per GPU of a sharded GEMM)
 
 struct Params {
     int M, N, K, batch;
     int a_batched, b_batched;   // operand has a batch dimension in its tensor map
-    float* C;
-    int64_t sc_b, sc_m;         // C element strides (n stride is 1)
+    // The epilogue writes every tile to each of the ndst outputs: dst[0] is the local C;
+    // for a column-sharded GEMM over several GPUs, dst[1..] are the same shard columns
+    // of the other GPUs' C buffers (peer pointers), so the all-gather of C happens in
+    // the epilogue, tile by tile, while the next tile's main loop runs.
+    float* dst[kMaxDst];
+    int ndst;
+    int64_t sc_b, sc_m;         // C element strides (n stride is 1), same for every dst
     const float* bias;
     int epi;
     int vec_store;              // rows 16-byte aligned and N % 4 == 0
@@ -225,7 +231,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             __syncwarp();   // tcgen05.ld below is .sync.aligned: reconverge after the spin
             tc_fence_after();
             const int m = mb * BM + q * 32 + lane;
-            float* crow = p.C + (int64_t)b * p.sc_b + (int64_t)m * p.sc_m;
+            const int64_t row_off = (int64_t)b * p.sc_b + (int64_t)m * p.sc_m;
             const float bias_row = (p.epi & 1) && m < p.M ? __ldg(p.bias + m) : 0.f;
 #pragma unroll 1
             for (int c = 0; c < BN / 32; ++c) {
@@ -246,14 +252,20 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                     v[j] = x;
                 }
                 if (m < p.M) {
-                    if (p.vec_store && n0 + 32 <= p.N) {
 #pragma unroll
-                        for (int j = 0; j < 32; j += 4)
-                            *reinterpret_cast<float4*>(crow + n0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-                    } else {
+                    for (int d = 0; d < kMaxDst; ++d) {
+                        if (d >= p.ndst) break;
+                        float* crow = p.dst[d] + row_off;
+                        if (p.vec_store && n0 + 32 <= p.N) {
 #pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            if (n0 + j < p.N) crow[n0 + j] = v[j];
+                            for (int j = 0; j < 32; j += 4)
+                                *reinterpret_cast<float4*>(crow + n0 + j) =
+                                    make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j)
+                                if (n0 + j < p.N) crow[n0 + j] = v[j];
+                        }
                     }
                 }
             }

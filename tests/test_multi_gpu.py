@@ -1,0 +1,123 @@
+"""GPU tests of the sharded GEMM path.
+
+On one GPU: the multi-destination epilogue (every tile stored to several buffers) and the
+bounded cross-GPU flag barrier (a wait that runs out records status 6 and returns; the
+context stays usable). On two or more GPUs (skipped otherwise): the fused column-sharded
+GEMM + all-gather across real processes, checked against the CPU oracle.
+"""
+import ctypes
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+from minitensor_b200 import engine, inputs
+from parity import absmm, check, dev, host
+
+pytestmark = pytest.mark.gpu
+
+
+def _multi(A, B, C, extras, mode):
+    L = engine.lib()
+    P = ctypes.POINTER(engine.MtTensor)
+    L.mt_gemm_multi.argtypes = [P, P, P, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
+                                ctypes.c_void_p]
+    arr = (ctypes.c_void_p * max(1, len(extras)))(*[e.data_ptr() for e in extras])
+    engine._check(L.mt_gemm_multi(ctypes.byref(engine.view(A)), ctypes.byref(engine.view(B)),
+                                  ctypes.byref(engine.view(C)), arr, len(extras), None, 0, engine._mode(mode),
+                                  engine._stream(None)))
+
+
+@pytest.mark.parametrize("mode", ["tf32", "tf32x3", "strict"])
+def test_multi_destination_epilogue(eng, port, mode):
+    M, K, N = 384, 256, 640
+    A = inputs.uniform((M, K), -1, 1, 71)
+    B = inputs.uniform((K, N), -1, 1, 72)
+    C = torch.empty(M, N, device="cuda")
+    extras = [torch.full((M, N), -7.0, device="cuda") for _ in range(3)]
+    _multi(dev(A), dev(B), C, extras, mode)
+    ref = port.matmul(A, B)
+    c = host(C)
+    check(mode, c, ref, absmm(A, B), K, "local")
+    for e in extras:
+        assert np.array_equal(host(e), c)
+
+
+def test_column_shard_into_wide_buffers(eng, port):
+    # The sharded layout on one GPU: 4 "ranks" write their column blocks into 4 full-width Cs.
+    M, K, N, world = 256, 192, 512, 4
+    A = inputs.uniform((M, K), -1, 1, 73)
+    B = inputs.uniform((K, N), -1, 1, 74)
+    Cs = [torch.zeros(M, N, device="cuda") for _ in range(world)]
+    Ad = dev(A)
+    for r in range(world):
+        n0, n1 = N * r // world, N * (r + 1) // world
+        Bs = dev(np.ascontiguousarray(B[:, n0:n1]))
+        others = [Cs[d][:, n0:] for d in range(world) if d != r]   # element (0, n0) of each peer C
+        _multi(Ad, Bs, Cs[r][:, n0:n1], others, "tf32x3")
+    ref = port.matmul(A, B)
+    for C in Cs:
+        check("tf32x3", host(C), ref, absmm(A, B), K, "sharded layout")
+
+
+def test_peer_barrier_timeout_reports_status(eng):
+    L = engine.lib()
+    L.mt_peer_barrier.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_uint64,
+                                  ctypes.c_void_p]
+    assert engine.device_status(reset=True) == 0
+    mine = torch.zeros(2, dtype=torch.int32, device="cuda")
+    other = torch.zeros(2, dtype=torch.int32, device="cuda")    # "rank 1" never raises its flag
+    arr = (ctypes.c_void_p * 2)(mine.data_ptr(), other.data_ptr())
+    engine._check(L.mt_peer_barrier(arr, 0, 2, 1, int(0.2e9), engine._stream(None)))
+    assert engine.device_status(reset=True) == 6
+    assert host(other).tolist() == [1, 0]                       # our flag reached the peer array
+    # The context is still usable.
+    A = torch.ones(64, 64, device="cuda")
+    C = torch.empty(64, 64, device="cuda")
+    engine.gemm(A, A, C, mode="tf32x3")
+    assert float(host(C)[0, 0]) == 64.0
+    assert engine.device_status(reset=True) == 0
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _sharded_worker(rank, world, port, out, mode):
+    import torch.distributed as dist
+    from minitensor_b200 import sharded
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    M, N, K = 1024, 1536, 512
+    A = inputs.uniform((M, K), -1, 1, 81)
+    B = inputs.uniform((K, N), -1, 1, 82)
+    plan = sharded.ShardedGemm(M, N, K, rank, world, timeout_s=5.0)
+    C = torch.zeros(M, N, device="cuda")
+    for _ in range(2):   # twice: the second call reuses the IPC mappings and a new epoch
+        plan.run(dev(A), dev(np.ascontiguousarray(B[:, plan.n0:plan.n1])), C, mode=mode)
+    torch.cuda.synchronize()
+    np.save(os.path.join(out, f"c{rank}.npy"), C.cpu().numpy())
+    status = engine.device_status(reset=True)
+    dist.barrier()
+    plan.close()
+    dist.destroy_process_group()
+    assert status == 0, status
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("mode", ["tf32x3", "strict"])
+def test_sharded_gemm_two_gpus(eng, port, tmp_path, mode):
+    import torch.multiprocessing as mp
+    world = 2
+    mp.spawn(_sharded_worker, args=(world, _free_port(), str(tmp_path), mode), nprocs=world, join=True)
+    A = inputs.uniform((1024, 512), -1, 1, 81)
+    B = inputs.uniform((512, 1536), -1, 1, 82)
+    ref = port.matmul(A, B)
+    for r in range(world):
+        check(mode, np.load(tmp_path / f"c{r}.npy"), ref, absmm(A, B), 512, f"rank {r}")

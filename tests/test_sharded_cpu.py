@@ -1,0 +1,89 @@
+"""CPU tests of the multi-GPU host logic with world_size-2 gloo process groups: the column
+shard plan, the baseline all-gather reassembly, and failure detection (a rank that dies
+before the collective makes the survivor's collective fail within its timeout, never hang).
+"""
+import datetime
+import os
+import socket
+import time
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from minitensor_b200.sharded import allgather_shards, shard_columns
+
+
+def free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_shard_plan_covers_columns():
+    for N in (1, 7, 8, 8192, 1000):
+        for world in (1, 2, 3, 4, 8):
+            cols = []
+            for r in range(world):
+                n0, n1 = shard_columns(N, world, r)
+                assert 0 <= n0 <= n1 <= N
+                cols.extend(range(n0, n1))
+            assert cols == list(range(N))
+
+
+def _gather_worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    rs = np.random.RandomState(0)
+    A = rs.standard_normal((12, 5)).astype(np.float32)
+    B = rs.standard_normal((5, 8)).astype(np.float32)
+    n0, n1 = shard_columns(8, world, rank)
+    C_shard = torch.from_numpy(A @ B[:, n0:n1])
+    C = allgather_shards(C_shard, world)
+    np.save(os.path.join(out, f"c{rank}.npy"), C.numpy())
+    np.save(os.path.join(out, "ref.npy"), A @ B)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_allgather_reassembly_gloo(tmp_path):
+    mp.spawn(_gather_worker, args=(2, free_port(), str(tmp_path)), nprocs=2, join=True)
+    ref = np.load(tmp_path / "ref.npy")
+    for r in range(2):
+        assert np.array_equal(np.load(tmp_path / f"c{r}.npy"), ref)
+
+
+def _dying_worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=3))
+    if rank == 1:
+        # This rank fails on the host before its collective (between steps).
+        os._exit(3)
+    t0 = time.time()
+    try:
+        allgather_shards(torch.ones(4, 2), world)
+        status = "completed"
+    except Exception as e:  # gloo reports the lost peer / timeout as an error
+        status = f"error:{type(e).__name__}"
+    with open(os.path.join(out, "survivor.txt"), "w") as f:
+        f.write(f"{status} {time.time() - t0:.2f}")
+    os._exit(0)
+
+
+def test_dead_rank_is_detected_not_hung(tmp_path):
+    ctx = mp.get_context("spawn")
+    port = free_port()
+    procs = [ctx.Process(target=_dying_worker, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=60)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    assert not alive, "a rank hung past the process-group timeout"
+    status, secs = open(tmp_path / "survivor.txt").read().split()
+    assert status.startswith("error"), status
+    assert float(secs) < 30
