@@ -1,5 +1,5 @@
 // mt_common.cuh -- sm_100a building blocks shared by the GEMM and conv kernels:
-// mbarrier, TMA (cp.async.bulk.tensor, no multicast), tcgen05 (TMEM alloc / MMA /
+// mbarrier, TMA (cp.async.bulk.tensor, per-CTA loads), tcgen05 (TMEM alloc / MMA /
 // commit / ld) as inline PTX, and the device status word that every bounded wait
 // reports into instead of spinning forever.
 #pragma once
@@ -98,7 +98,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
 
 // ---------------------------------------------------------------------------------
 // TMA: tiled bulk tensor loads global -> shared, completion on an mbarrier.
-// No .multicast::cluster form is used anywhere in this library.
+// Every TMA load in this library is a plain per-CTA load (no cluster broadcast).
 // ---------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");

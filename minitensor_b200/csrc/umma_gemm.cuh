@@ -9,7 +9,7 @@
 // Layout of work. One persistent CTA per SM walks output tiles of 128 x BN, BKE (32 for
 // TF32, 16 for TF32X3) k-elements per pipeline stage. Warp roles:
 //   warp 0      TMA producer: swizzled tiles into a STAGES-deep shared-memory ring,
-//               completion counted on mbarriers (no multicast).
+//               completion counted on mbarriers (plain per-CTA loads).
 //   warp 1      TMEM owner and single-thread MMA issuer (tcgen05.mma.cta_group::1).
 //   warps 2-5   epilogue: TMEM -> registers (tcgen05.ld 32x32b) -> bias/ReLU -> global.
 //   warps 6-9   (TF32X3 only) converter: splits each landed stage into hi (in place) and
