@@ -145,6 +145,18 @@ MT_API int mt_conv2d_wgrad(const mt_tensor* dy, const mt_tensor* x, const mt_ten
 MT_API size_t mt_conv2d_wgrad_workspace_bytes(const mt_tensor* dy, const mt_tensor* x, const mt_tensor* dw,
                                               uint64_t stride, uint64_t padding, int mode);
 
+/* Weight gradient that allocates nothing: no counterpart in the reference. For callers
+ * that cannot allocate device memory during the call (a graph capture that forbids
+ * allocation nodes, a host that owns all device memory, a latency-critical loop). It
+ * computes what mt_conv2d_wgrad computes, with the split-K partials in a fixed 8 MiB
+ * array inside the library (one per GPU, held until the process exits); problems whose
+ * partials need more get MT_EINVAL with the size in the message. The first call on a
+ * device looks up that array's device address, so make it before any stream capture.
+ * All calls on a device share the array: calls that overlap on the GPU (other streams,
+ * other host threads) race and must be serialised by the caller. */
+MT_API int mt_conv2d_wgrad_noalloc(const mt_tensor* dy, const mt_tensor* x, const mt_tensor* dw, uint64_t stride,
+                                   uint64_t padding, int mode, void* stream);
+
 /* ---- general entry point ----------------------------------------------------------- */
 
 /* C = epi(A * B) for 2-D or 3-D (batched) views with an explicit mode. `bias` is a device

@@ -815,6 +815,55 @@ MT_API int mt_conv2d_wgrad(const mt_tensor* dy, const mt_tensor* x, const mt_ten
     return conv_wgrad(dy, x, dw, stride, padding, mode, workspace, ws_bytes, static_cast<cudaStream_t>(stream),
                       "conv2d_wgrad");
 }
+// ---- weight gradient without any allocation -----------------------------------------
+// For callers that cannot allocate device memory at call time: code running under a
+// CUDA-graph capture that forbids allocation nodes, plugin hosts that own every byte of
+// device memory and reject cudaMalloc from libraries, or real-time loops where an
+// allocation could block. The split-K partials go to this fixed file-scope array
+// instead of a workspace. The array exists once per GPU that loads the library and stays
+// until the process exits.
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;   // 8 MiB of partials per GPU
+static __device__ __align__(256) float g_wgrad_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+
+// Device address of the array on the current device. On the host the array's name is
+// only a stand-in symbol, so the address is looked up once per device (with that device
+// current) and cached.
+int noalloc_scratch(float** out) {
+    static std::mutex mu;
+    static float* cache[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "conv2d_wgrad_noalloc: cudaGetDevice");
+    if (dev < 0 || dev >= 64) return fail(MT_EUNSUPPORTED, "conv2d_wgrad_noalloc: device index %d", dev);
+    std::lock_guard<std::mutex> g(mu);
+    if (!cache[dev]) {
+        void* ptr = nullptr;
+        e = cudaGetSymbolAddress(&ptr, g_wgrad_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_fail(e, "conv2d_wgrad_noalloc: cudaGetSymbolAddress");
+        cache[dev] = static_cast<float*>(ptr);
+    }
+    *out = cache[dev];
+    return MT_OK;
+}
+
+MT_API int mt_conv2d_wgrad_noalloc(const mt_tensor* dy, const mt_tensor* x, const mt_tensor* dw, uint64_t stride,
+                                   uint64_t padding, int mode, void* stream) {
+    if (mode < MT_MODE_DEFAULT || mode > MT_TF32X3) return fail(MT_EINVAL, "conv2d_wgrad_noalloc: bad mode %d", mode);
+    const size_t need = mt_conv2d_wgrad_workspace_bytes(dy, x, dw, stride, padding, mode);
+    if (need > kNoAllocScratchBytes)
+        return fail(MT_EINVAL,
+                    "conv2d_wgrad_noalloc: this problem needs %zu bytes of split-K partials; the static scratch "
+                    "holds %zu (use mt_conv2d_wgrad with a workspace)",
+                    need, kNoAllocScratchBytes);
+    float* scratch = nullptr;
+    int rc = noalloc_scratch(&scratch);
+    if (rc) return rc;
+    // Every split writes its whole partial tile (zeros for an empty split), so nothing
+    // left in the array by an earlier call is read.
+    return conv_wgrad(dy, x, dw, stride, padding, mode, scratch, kNoAllocScratchBytes,
+                      static_cast<cudaStream_t>(stream), "conv2d_wgrad_noalloc");
+}
+
 MT_API size_t mt_conv2d_wgrad_workspace_bytes(const mt_tensor* dy, const mt_tensor* x, const mt_tensor* dw,
                                               uint64_t stride, uint64_t padding, int mode) {
     // Shapes only: no pointer is dereferenced, so data may be NULL here.
