@@ -56,5 +56,53 @@ def build(verbose: bool = False, force: bool = False) -> str:
     return LIB
 
 
+OVERLAY = os.path.join(PKG, "overlay")
+DROPIN_OUT = os.path.join(OVERLAY, "_build")
+DROPIN_BIN = os.path.join(DROPIN_OUT, "dropin_test")
+# Symbols defined by gpu_ops_b200.cpp (the reference declares them at
+# include/TensorOps.hpp:703-712); the reference object's own definitions are renamed.
+OVERRIDDEN = ("matmul_gpu", "matmul_gpu_strided", "matmul_gpu_v2", "matmul_gpu_bk16", "conv2d_gpu",
+              "conv2d_gpu_strided", "conv2d_backward_input_gpu", "conv2d_backward_weight_gpu",
+              "conv2d_backward_bias_gpu")
+
+
+def _run(cmd):
+    subprocess.check_call(cmd)
+
+
+def build_dropin(ref_root: str = "/root/reference") -> str | None:
+    """Builds overlay/_build/dropin_test: the reference's own dispatchers, autograd and
+    modules (headers unmodified; src/gpu_ops.cpp compiled from where it lies) with the
+    GEMM/conv entry points served by gpu_ops_b200.cpp + libmtgemm.so. Needs the reference
+    checkout; returns None without it (the built binary travels with the other outputs)."""
+    src = os.path.join(ref_root, "src", "gpu_ops.cpp")
+    if not os.path.exists(src):
+        return None
+    build()
+    os.makedirs(DROPIN_OUT, exist_ok=True)
+    ref_inc = os.path.join(ref_root, "include")
+    cuda_inc = os.path.join(os.path.dirname(os.path.dirname(nvcc())), "include")
+    ref_obj = os.path.join(DROPIN_OUT, "ref_gpu_ops.o")
+    if not os.path.exists(ref_obj) or os.path.getmtime(ref_obj) < os.path.getmtime(src):
+        _run([nvcc(), "-x", "cu", "-std=c++20", "-DUSE_CUDA", *ARCH, "-O3", "-w", "-Xcompiler", "-fPIC",
+              "-I", ref_inc, "-c", src, "-o", ref_obj])
+    cxx = ["g++", "-std=c++20", "-O2", "-fPIC", "-DUSE_CUDA", "-I", ref_inc, "-I", INCLUDE, "-I", cuda_inc]
+    ov_obj = os.path.join(DROPIN_OUT, "gpu_ops_b200.o")
+    test_obj = os.path.join(DROPIN_OUT, "dropin_test.o")
+    _run([*cxx, "-c", os.path.join(OVERLAY, "gpu_ops_b200.cpp"), "-o", ov_obj])
+    _run([*cxx, "-c", os.path.join(OVERLAY, "dropin_test.cpp"), "-o", test_obj])
+    # Rename the reference's definitions of the overridden entry points so that each
+    # symbol has exactly one definition (the overlay's) in the link.
+    defined = subprocess.check_output(["nm", "--defined-only", ov_obj], text=True).split("\n")
+    syms = [ln.split()[-1] for ln in defined if ln.strip() and any(f"{len(n)}{n}I" in ln for n in OVERRIDDEN)]
+    split_obj = os.path.join(DROPIN_OUT, "ref_gpu_ops_split.o")
+    _run(["objcopy", *[f"--redefine-sym={s}={s}__reference_replaced" for s in syms], ref_obj, split_obj])
+    _run([nvcc(), *ARCH, "-o", DROPIN_BIN, test_obj, ov_obj, split_obj, "-L", PKG, "-lmtgemm",
+          "-Xlinker", "-rpath", "-Xlinker", "$ORIGIN/../.."])
+    return DROPIN_BIN
+
+
 if __name__ == "__main__":
     print(build(verbose="--verbose" in sys.argv, force=True))
+    if "--dropin" in sys.argv:
+        print(build_dropin())
