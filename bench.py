@@ -1,16 +1,21 @@
-"""Benchmark: fp32-input GEMM TFLOP/s on B200 (config 5: 8192 x 8192 x 8192).
+"""Benchmark: fp32-input GEMM TFLOP/s on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--mode tf32x3|tf32|strict]
-    python bench.py --impl reference ...     # the reference's CPU matmul on the host cores
+                    [--workload c1|c2|c3|c4|c5]
+    python bench.py --impl reference ...     # the reference's CPU path on the host cores
 
-One step = one C = A.B over the whole 8192^3 problem (inputs resident in HBM; 512 MB of
-operands, larger than the 126 MB L2, so no flush is needed between steps). With N > 1
-GPUs (torchrun, one process per GPU, NCCL) the N columns of C are sharded over the ranks
-and every rank ends with the full C (strong scaling). Prints ONE JSON line on rank 0.
+Default workload c5 (the one the metric's 1/2/4/8-GPU figures are quoted on):
+C[8192,8192] = A[8192,8192] . B[8192,8192], inputs resident in HBM (512 MB of operands,
+larger than the 126 MB L2, so no flush between steps). With N > 1 GPUs (torchrun, one
+process per GPU) the N columns of C are sharded over the ranks and every rank ends with
+the full C (strong scaling). The other workloads (c1 512^3 GEMM, c2 Linear 256x1024->4096
+forward+backward, c3 broadcast bmm, c4 ResNet 3x3 conv forward+weight-grad) are
+single-GPU measurements of the same engine. Prints ONE JSON line on rank 0.
 """
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -23,10 +28,9 @@ sys.path.insert(0, ROOT)
 
 import numpy as np  # noqa: E402
 
-N_DIM = 8192
-FLOP = 2.0 * N_DIM ** 3
 METRIC = "fp32-input GEMM TFLOP/s (TF32 & 3xTF32) at 1/2/4/8 B200, % of roofline"
-WORKLOAD = "config5: C[8192,8192] = A[8192,8192] . B[8192,8192], A,B ~ U[-1,1] seed 1"
+# 148 SMs x 128 FP32 lanes x 2 FLOP x 1.965 GHz, in TFLOP/s (no measured SIMT peak exists).
+FP32_SIMT_NOMINAL = 148 * 128 * 2 * 1.965e9 / 1e12
 
 
 def parse():
@@ -36,9 +40,10 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="mt", choices=["mt", "reference"])
     ap.add_argument("--mode", default="tf32x3", choices=["tf32x3", "tf32", "strict"])
+    ap.add_argument("--workload", default="c5", choices=["c1", "c2", "c3", "c4", "c5"])
     ap.add_argument("--no-extras", action="store_true", help="skip the other modes, e2e and CPU legs")
     ap.add_argument("--size", type=int, default=8192,
-                    help="square problem size; 8192 is the benchmark, smaller sizes are profiling cases")
+                    help="c5 square size; 8192 is the benchmark, smaller sizes are profiling cases")
     return ap.parse_args()
 
 
@@ -48,10 +53,9 @@ def peaks():
     try:
         with open(path) as f:
             p = json.load(f)
-        return float(p["bf16_tflops"]), float(p.get("bf16_tflops_sustained", p["bf16_tflops"])), \
-            float(p["hbm_gbs"]), "measured"
+        return float(p["bf16_tflops"]), float(p["hbm_gbs"]), "measured"
     except Exception:
-        return 1590.0, 1400.0, 6650.0, "fallback"
+        return 1590.0, 6650.0, "fallback"
 
 
 # ------------------------------------------------------------------ clocks ----------
@@ -61,9 +65,7 @@ class ClockSampler:
                0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
     def __init__(self, device_index: int, period: float = 0.02):
-        self.samples = []
-        self.reasons = set()
-        self.max_mhz = None
+        self.samples, self.reasons, self.max_mhz = [], set(), None
         self.period = period
         self._stop = threading.Event()
         self._t = None
@@ -100,13 +102,11 @@ class ClockSampler:
             self._t.join()
 
     def summary(self):
-        if not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": 0}
-        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
-                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+        med = statistics.median(self.samples) if self.samples else None
+        return {"sm_mhz": med, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                "samples": len(self.samples)}
 
 
-# ------------------------------------------------------------------ CPU legs ---------
 def cpu_threads():
     try:
         return len(os.sched_getaffinity(0))
@@ -114,42 +114,292 @@ def cpu_threads():
         return os.cpu_count() or 1
 
 
-def reference_sample(A, B, rows: int, threads: int):
-    """The reference's own matmul_cpu (oracle/_ref) over C rows [0, rows) with `threads`
-    host threads; falls back to the C restatement when the reference build is absent."""
+def _ref():
+    """The reference's own CPU code (oracle/_ref), else the C restatement of it."""
     import oracle
-    if oracle.have_ref():
-        impl, kind = oracle.Ref(), "reference"
-    else:
-        impl, kind = oracle.Port(), "port"
-    _, dt = impl.matmul_rows(A, B, 0, rows, threads, timing=True)
-    return 2.0 * rows * A.shape[1] * B.shape[1] / dt / 1e12, dt, kind
+    return (oracle.Ref(), "reference") if oracle.have_ref() else (oracle.Port(), "port")
 
 
+def _pin(a):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).pin_memory()
+
+
+def _cuda(a):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+# ------------------------------------------------------------------ workloads --------
+class Workload:
+    """One configuration. Host inputs always exist; gpu=True also builds device buffers.
+    flops / bytes are the algorithmic figures per step (2MNK per GEMM; every operand read
+    once and every output written once, fp32)."""
+    name = desc = ""
+    flops = bytes = 0.0
+
+    def __init__(self, gpu=True):
+        self.h2d, self.d2h = [], []
+        if gpu:
+            self.to_gpu()
+
+    def to_gpu(self):
+        pass
+
+    def step(self, mode):
+        raise NotImplementedError
+
+    def cpu_sample(self, threads):
+        """(TFLOP/s, seconds, kind, sample description) of the reference CPU path."""
+        raise NotImplementedError
+
+
+class C5(Workload):
+    name = "c5"
+
+    def __init__(self, gpu=True, n=8192, rank=0, world=1):
+        from minitensor_b200 import inputs
+        self.n, self.rank, self.world = n, rank, world
+        self.desc = (f"config5: C[{n},{n}] = A[{n},{n}] . B[{n},{n}], A,B ~ U[-1,1] seed 1" if n == 8192
+                     else f"profiling case: config5 generator at {n}^3 (not the benchmark shape)")
+        self.flops = 2.0 * n ** 3
+        self.bytes = 3.0 * n * n * 4
+        self.A_h, self.B_h = inputs.config5(n)
+        super().__init__(gpu)
+
+    def to_gpu(self):
+        import torch
+        from minitensor_b200 import engine
+        self.engine = engine
+        n = self.n
+        self.A = _cuda(self.A_h)
+        self.C = torch.empty(n, n, device="cuda")
+        if self.world == 1:
+            Bsrc = self.B_h
+        else:
+            from minitensor_b200 import sharded
+            self.plan = sharded.ShardedGemm(n, n, n, self.rank, self.world)
+            Bsrc = np.ascontiguousarray(self.B_h[:, self.plan.n0:self.plan.n1])
+        self.B = _cuda(Bsrc)
+        self.h2d = [(_pin(self.A_h), self.A), (_pin(Bsrc), self.B)]
+        self.d2h = [(self.C, torch.empty(n, n).pin_memory())]
+
+    def step(self, mode):
+        if self.world == 1:
+            self.engine.gemm(self.A, self.B, self.C, mode=mode)
+        else:
+            self.plan.run(self.A, self.B, self.C, mode=mode)
+
+    def cpu_sample(self, threads):
+        impl, kind = _ref()
+        rows = threads
+        _, dt = impl.matmul_rows(self.A_h, self.B_h, 0, rows, threads, timing=True)
+        return (2.0 * rows * self.n * self.n / dt / 1e12, dt, kind,
+                f"C rows 0..{rows - 1} of config5 ({rows} x {self.n} x {self.n}), {threads} threads")
+
+
+class C1(Workload):
+    name = "c1"
+    desc = "config1: C[512,512] = A[512,512] . B[512,512], A,B ~ U[-1,1] seed 0"
+    flops = 2.0 * 512 ** 3
+    bytes = 3.0 * 512 * 512 * 4
+
+    def __init__(self, gpu=True):
+        from minitensor_b200 import inputs
+        self.A_h, self.B_h = inputs.config1()
+        super().__init__(gpu)
+
+    def to_gpu(self):
+        import torch
+        from minitensor_b200 import engine
+        self.engine = engine
+        self.A, self.B = _cuda(self.A_h), _cuda(self.B_h)
+        self.C = torch.empty(512, 512, device="cuda")
+        self.h2d = [(_pin(self.A_h), self.A), (_pin(self.B_h), self.B)]
+        self.d2h = [(self.C, torch.empty(512, 512).pin_memory())]
+
+    def step(self, mode):
+        self.engine.gemm(self.A, self.B, self.C, mode=mode)
+
+    def cpu_sample(self, threads):
+        impl, kind = _ref()
+        t0 = time.perf_counter()
+        impl.matmul(self.A_h, self.B_h)
+        dt = time.perf_counter() - t0
+        return self.flops / dt / 1e12, dt, kind, "the whole 512^3 matmul, 1 thread (matmul_cpu is serial)"
+
+
+class C2(Workload):
+    name = "c2"
+    desc = ("config2: Linear 1024->4096, batch 256: Y = X.W + b (bias fused), dX = dY.W^T and dW = X^T.dY "
+            "read from transposed views, db = 1^T.dY; W [in,out] He-normal seed 42, X, dY ~ N(0,1)")
+    M, K, N = 256, 1024, 4096
+    flops = 3 * 2.0 * M * K * N + 2.0 * M * N
+    bytes = 3 * 4.0 * (M * K + K * N + M * N) + 4.0 * (M * N + 2 * N)
+
+    def __init__(self, gpu=True):
+        from minitensor_b200 import inputs
+        self.host = inputs.config2()
+        super().__init__(gpu)
+
+    def to_gpu(self):
+        import torch
+        from minitensor_b200 import engine
+        self.engine = engine
+        X, W, b, dY = self.host
+        self.X, self.W, self.b, self.dY = (_cuda(a) for a in (X, W, b, dY))
+        self.Y = torch.empty(256, 4096, device="cuda")
+        self.dX = torch.empty(256, 1024, device="cuda")
+        self.dW = torch.empty(1024, 4096, device="cuda")
+        self.db = torch.empty(1, 4096, device="cuda")
+        self.ones = torch.ones(1, 256, device="cuda")
+        self.h2d = [(_pin(X), self.X), (_pin(dY), self.dY)]
+        self.d2h = [(self.Y, torch.empty(256, 4096).pin_memory()), (self.dW, torch.empty(1024, 4096).pin_memory())]
+
+    def step(self, mode):
+        e = self.engine
+        e.gemm(self.X, self.W, self.Y, bias=self.b.reshape(-1), epi=e.EPI_BIAS_COL, mode=mode)
+        e.gemm(self.dY, self.W.t(), self.dX, mode=mode)
+        e.gemm(self.X.t(), self.dY, self.dW, mode=mode)
+        e.gemm(self.ones, self.dY, self.db, mode="strict")
+
+    def cpu_sample(self, threads):
+        impl, kind = _ref()
+        X, W, b, dY = self.host
+        rows = 8
+        Xs, dYs = np.ascontiguousarray(X[:rows]), np.ascontiguousarray(dY[:rows])
+        t0 = time.perf_counter()
+        if kind == "reference":
+            impl.linear(Xs, W, b, dYs)
+        else:
+            impl.linear_fwd(Xs, W, b)
+            impl.matmul_strided(dYs, W.T)
+            impl.matmul_strided(Xs.T, dYs)
+        dt = time.perf_counter() - t0
+        return (3 * 2.0 * rows * 1024 * 4096 / dt / 1e12, dt, kind,
+                f"Linear fwd+bwd on {rows} of 256 batch rows, 1 thread (the reference CPU path is serial)")
+
+
+class C3(Workload):
+    name = "c3"
+    desc = "config3: C[64,512,512] = A[64,512,64] . expand(B0[1,64,512]) (stride-0 batch), N(0,0.125)"
+    flops = 2.0 * 64 * 512 * 512 * 64
+    bytes = 4.0 * (64 * 512 * 64 + 64 * 512 + 64 * 512 * 512)
+
+    def __init__(self, gpu=True):
+        from minitensor_b200 import inputs
+        self.A_h, self.B0_h = inputs.config3()
+        super().__init__(gpu)
+
+    def to_gpu(self):
+        import torch
+        from minitensor_b200 import engine
+        self.engine = engine
+        self.A, self.B0 = _cuda(self.A_h), _cuda(self.B0_h)
+        self.Bx = self.B0.expand(64, 64, 512)
+        self.C = torch.empty(64, 512, 512, device="cuda")
+        self.h2d = [(_pin(self.A_h), self.A), (_pin(self.B0_h), self.B0)]
+        self.d2h = [(self.C, torch.empty(64, 512, 512).pin_memory())]
+
+    def step(self, mode):
+        self.engine.gemm(self.A, self.Bx, self.C, mode=mode)
+
+    def cpu_sample(self, threads):
+        impl, kind = _ref()
+        nb = 4
+        t0 = time.perf_counter()
+        if kind == "reference":
+            impl.bmm(np.ascontiguousarray(self.A_h[:nb]), self.B0_h, True)
+        else:
+            impl.bmm(self.A_h[:nb], np.broadcast_to(self.B0_h, (nb, 64, 512)))
+        dt = time.perf_counter() - t0
+        return 2.0 * nb * 512 * 512 * 64 / dt / 1e12, dt, kind, f"bmm on {nb} of 64 batches, 1 thread"
+
+
+class C4(Workload):
+    name = "c4"
+    desc = ("config4: Conv2D x[32,64,56,56] * W[64,64,3,3] stride 1 pad 1 (ResNet-50 3x3), forward + "
+            "weight-grad as implicit GEMM on NCHW")
+    flops = 2 * 2.0 * (32 * 56 * 56) * 64 * 576
+    # forward reads x, W and writes y; weight-grad reads dy, x and writes dW
+    bytes = 4.0 * (32 * 64 * 56 * 56 * 2 + 64 * 576) * 2
+
+    def __init__(self, gpu=True):
+        from minitensor_b200 import inputs
+        self.host = inputs.config4()
+        super().__init__(gpu)
+
+    def to_gpu(self):
+        import torch
+        from minitensor_b200 import engine
+        self.engine = engine
+        x, w, b, dy = self.host
+        self.x, self.w, self.b, self.dy = (_cuda(a) for a in (x, w, b, dy))
+        self.y = torch.empty(32, 64, 56, 56, device="cuda")
+        self.dw = torch.empty(64, 64, 3, 3, device="cuda")
+        nbytes = engine.conv2d_wgrad_workspace_bytes(self.dy, self.x, tuple(self.w.shape), 1, 1, mode="tf32x3")
+        self.ws = torch.empty(max(1, nbytes // 4), device="cuda")
+        self.h2d = [(_pin(x), self.x), (_pin(dy), self.dy)]
+        self.d2h = [(self.y, torch.empty(32, 64, 56, 56).pin_memory()), (self.dw, torch.empty(64, 64, 3, 3).pin_memory())]
+
+    def step(self, mode):
+        e = self.engine
+        L = e.lib()
+        m, s = e._mode(mode), e._stream(None)
+        e._check(L.mt_conv2d_fwd(ctypes.byref(e.view(self.x)), ctypes.byref(e.view(self.w)),
+                                 ctypes.byref(e.view(self.b)), ctypes.byref(e.view(self.y)), 1, 1, m, s))
+        e._check(L.mt_conv2d_wgrad(ctypes.byref(e.view(self.dy)), ctypes.byref(e.view(self.x)),
+                                   ctypes.byref(e.view(self.dw)), 1, 1, m, self.ws.data_ptr(),
+                                   self.ws.numel() * 4, s))
+
+    def cpu_sample(self, threads):
+        impl, kind = _ref()
+        x, w, b, dy = self.host
+        n = 1
+        xs, dys = np.ascontiguousarray(x[:n]), np.ascontiguousarray(dy[:n])
+        t0 = time.perf_counter()
+        if kind == "reference":
+            impl.conv2d(xs, w, b, 1, 1)
+            impl.conv2d_backward(dys, xs, w, 1, 1)   # also runs the input- and bias-grad
+        else:
+            impl.conv2d(xs, w, b, 1, 1)
+            impl.conv2d_bwd_weight(dys, xs, w.shape, 1, 1)
+        dt = time.perf_counter() - t0
+        return (2 * 2.0 * n * 56 * 56 * 64 * 576 / dt / 1e12, dt, kind,
+                f"conv forward + backward on {n} of 32 images, 1 thread")
+
+
+def make_workload(args, rank, world, gpu=True):
+    if args.workload == "c5":
+        return C5(gpu, args.size, rank, world)
+    if world > 1 and gpu:
+        raise SystemExit("workloads c1-c4 are single-GPU problems (replicas only)")
+    return {"c1": C1, "c2": C2, "c3": C3, "c4": C4}[args.workload](gpu)
+
+
+# ------------------------------------------------------------------ reference arm ----
 def run_reference(args, rank):
-    """--impl reference: rank 0 times the reference CPU path; other ranks exit."""
+    """--impl reference: rank 0 times the reference CPU path (its own matmul_cpu / Linear /
+    conv routines, compiled from its headers into oracle/_ref) on bounded samples."""
     if rank != 0:
         return
-    from minitensor_b200 import inputs
-    A, B = inputs.config5(N_DIM)
+    wl = make_workload(args, 0, 1, gpu=False)
     threads = cpu_threads()
-    rows = threads
     vals = []
-    kind = "reference"
+    kind = sample = ""
     for i in range(args.warmup + args.steps):
-        v, dt, kind = reference_sample(A, B, rows, threads)
+        v, dt, kind, sample = wl.cpu_sample(threads)
         if i >= args.warmup:
             vals.append((v, dt))
     tflops = statistics.mean(v for v, _ in vals)
     ms = statistics.mean(dt for _, dt in vals) * 1e3
+    cores = threads if wl.name == "c5" else 1
     line = {
         "impl": "reference", "metric": METRIC, "value": tflops, "unit": "TFLOP/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "sample": f"C rows 0..{rows - 1} per step ({rows} x 8192 x 8192)",
-                   "threads": threads},
-        "cpu_baseline": {"value": tflops, "unit": "TFLOP/s", "cores": threads, "kind": kind,
-                         "sample": f"{rows} rows of C per step, reference matmul_cpu on row slices"},
+        "config": {"workload": wl.desc, "sample": sample, "threads": cores},
+        "cpu_baseline": {"value": tflops, "unit": "TFLOP/s", "cores": cores, "kind": kind, "sample": sample},
         "e2e": {"value": tflops, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -171,13 +421,7 @@ def time_steps(fn, steps, stream):
 
 def run_gpu(args, rank, world, local_rank):
     import torch
-    from minitensor_b200 import engine, inputs
-
-    global N_DIM, FLOP, WORKLOAD
-    if args.size != N_DIM:
-        N_DIM = args.size
-        FLOP = 2.0 * N_DIM ** 3
-        WORKLOAD = f"profiling case: config5 generator at {N_DIM}^3 (not the benchmark shape)"
+    from minitensor_b200 import engine
 
     torch.cuda.set_device(local_rank)
     dist = None
@@ -188,128 +432,117 @@ def run_gpu(args, rank, world, local_rank):
                                 device_id=torch.device("cuda", local_rank))
     engine.lib()
     stream = torch.cuda.current_stream()
-    A_h, B_h = inputs.config5(N_DIM)
+    wl = make_workload(args, rank, world)
 
-    if world == 1:
-        A = torch.from_numpy(A_h).cuda()
-        B = torch.from_numpy(B_h).cuda()
-        C = torch.empty(N_DIM, N_DIM, device="cuda")
-
-        def step(mode=args.mode):
-            engine.gemm(A, B, C, mode=mode)
-    else:
-        from minitensor_b200 import sharded
-        plan = sharded.ShardedGemm(N_DIM, N_DIM, N_DIM, rank, world)
-        A = torch.from_numpy(A_h).cuda()
-        B = torch.from_numpy(np.ascontiguousarray(B_h[:, plan.n0:plan.n1])).cuda()
-        C = torch.empty(N_DIM, N_DIM, device="cuda")
-
-        def step(mode=args.mode):
-            plan.run(A, B, C, mode=mode)
+    def max_over_ranks(t):
+        if not dist:
+            return t
+        tt = torch.tensor([t], device="cuda", dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        return float(tt.item())
 
     for _ in range(args.warmup):
-        step()
+        wl.step(args.mode)
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
     n0 = engine.launch_count()
     with ClockSampler(local_rank) as clk:
-        t = time_steps(step, args.steps, stream)
+        t = time_steps(lambda: wl.step(args.mode), args.steps, stream)
     launches = engine.launch_count() - n0
-    if dist:
-        tt = torch.tensor([t], device="cuda", dtype=torch.float64)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        t = float(tt.item())
+    t = max_over_ranks(t)
     path = engine.last_path()
-    tflops = FLOP * args.steps / t / 1e12
+    tflops = wl.flops * args.steps / t / 1e12
     ms = t / args.steps * 1e3
 
-    extras = {}
+    extras, e2e, cpu = {}, None, None
     if not args.no_extras:
-        # The other precisions, same workload (a few steps each).
         for m in ("tf32", "tf32x3", "strict"):
             if m == args.mode:
                 continue
             s = 3 if m == "strict" else max(5, args.steps // 2)
-            step(m)
+            wl.step(m)
             torch.cuda.synchronize()
             if dist:
                 dist.barrier()
-            tm = time_steps(lambda: step(m), s, stream)
-            if dist:
-                tt = torch.tensor([tm], device="cuda", dtype=torch.float64)
-                dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-                tm = float(tt.item())
-            extras[m] = {"value": FLOP * s / tm / 1e12, "ms_per_step": tm / s * 1e3}
+            tm = max_over_ranks(time_steps(lambda: wl.step(m), s, stream))
+            extras[m] = {"value": wl.flops * s / tm / 1e12, "ms_per_step": tm / s * 1e3}
 
-    # End to end through the public API from pinned host buffers: H2D of this rank's
-    # inputs, the GEMM (and the all-gather for N > 1), D2H of the full C.
-    e2e = None
-    if not args.no_extras:
-        Ap = torch.from_numpy(A_h).pin_memory()
-        Bp = torch.from_numpy(B_h if world == 1 else np.ascontiguousarray(B_h[:, plan.n0:plan.n1])).pin_memory()
-        Cp = torch.empty(N_DIM, N_DIM).pin_memory()
-
+        # End to end through the public API from pinned host buffers: H2D of this rank's
+        # inputs, the step, D2H of the results.
         def e2e_step():
-            A.copy_(Ap, non_blocking=True)
-            B.copy_(Bp, non_blocking=True)
-            step()
-            Cp.copy_(C, non_blocking=True)
+            for h, d in wl.h2d:
+                d.copy_(h, non_blocking=True)
+            wl.step(args.mode)
+            for d, h in wl.d2h:
+                h.copy_(d, non_blocking=True)
         e2e_step()
         torch.cuda.synchronize()
         if dist:
             dist.barrier()
         s = max(3, min(args.steps, 10))
-        te = time_steps(e2e_step, s, stream)
-        if dist:
-            tt = torch.tensor([te], device="cuda", dtype=torch.float64)
-            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-            te = float(tt.item())
-        e2e = {"value": FLOP * s / te / 1e12, "unit": "TFLOP/s", "ms_per_step": te / s * 1e3,
-               "h2d_bytes_per_step": int(Ap.numel() * 4 + Bp.numel() * 4), "d2h_bytes_per_step": int(Cp.numel() * 4)}
-
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_extras:
-        threads = cpu_threads()
-        v, dt, kind = reference_sample(A_h, B_h, threads, threads)
-        cpu = {"value": v, "unit": "TFLOP/s", "cores": threads, "kind": kind,
-               "sample": f"C rows 0..{threads - 1} of config5 ({threads} x 8192 x 8192, {dt:.1f} s)"}
+        te = max_over_ranks(time_steps(e2e_step, s, stream))
+        e2e = {"value": wl.flops * s / te / 1e12, "unit": "TFLOP/s", "ms_per_step": te / s * 1e3,
+               "h2d_bytes_per_step": int(sum(h.numel() * h.element_size() for h, _ in wl.h2d)),
+               "d2h_bytes_per_step": int(sum(h.numel() * h.element_size() for _, h in wl.d2h))}
+        if rank == 0 and world == 1:
+            v, dt, kind, sample = wl.cpu_sample(cpu_threads())
+            cpu = {"value": v, "unit": "TFLOP/s", "cores": cpu_threads() if wl.name == "c5" else 1,
+                   "kind": kind, "sample": f"{sample} ({dt:.2f} s)"}
 
     if dist:
         dist.barrier()
+        if hasattr(wl, "plan"):
+            wl.plan.close()
         dist.destroy_process_group()
     if rank != 0:
         return
 
-    bf16_burst, bf16_sust, hbm, src = peaks()
-    tf32_peak = bf16_burst / 2.0   # tcgen05 kind::tf32 runs at half the bf16 rate
-    per_gpu = tflops / world
-    roofline = {"bound": "tensor", "achieved": per_gpu, "peak": tf32_peak, "unit": "TFLOP/s",
-                "frac": per_gpu / tf32_peak, "traffic": traffic_for(args.mode),
-                "peak_source": f"{src}: dense bf16 burst {bf16_burst} / 2 (tf32)",
-                "kernel": path}
+    bf16, hbm, src = peaks()
+    tf32_peak = bf16 / 2.0   # tcgen05 kind::tf32 runs at half the bf16 rate
+    t_step = t / args.steps
+    if args.mode == "strict":
+        p_mode, p_src = FP32_SIMT_NOMINAL, "nominal FP32 SIMT peak (148 SM x 128 lanes x 2 x 1.965 GHz)"
+    else:
+        p_mode, p_src = tf32_peak, f"{src}: dense bf16 burst {bf16} TFLOP/s / 2 (tf32)"
+    flops_rank, bytes_rank = wl.flops / world, wl.bytes / world
+    t_compute, t_mem = flops_rank / (p_mode * 1e12), bytes_rank / (hbm * 1e9)
+    if t_compute >= t_mem:
+        roofline = {"bound": "tensor" if args.mode != "strict" else "fp32_simt",
+                    "achieved": flops_rank / t_step / 1e12, "peak": p_mode, "unit": "TFLOP/s",
+                    "peak_source": p_src}
+    else:
+        roofline = {"bound": "hbm", "achieved": bytes_rank / t_step / 1e9, "peak": hbm, "unit": "GB/s",
+                    "peak_source": f"{src}: STREAM-style copy {hbm} GB/s"}
+    roofline["frac"] = roofline["achieved"] / roofline["peak"]
+    roofline["traffic"] = traffic_for(wl.name, args.mode)
+    roofline["roofline_time_frac"] = max(t_compute, t_mem) / t_step
+    roofline["algorithmic"] = {"flops_per_step": flops_rank, "bytes_per_step": bytes_rank}
+    roofline["kernel"] = path
     if args.mode == "tf32x3":
-        roofline["frac_vs_tf32_over_3"] = per_gpu / (tf32_peak / 3.0)
+        roofline["frac_vs_tf32_over_3"] = (flops_rank / t_step / 1e12) / (tf32_peak / 3.0)
     line = {
         "metric": METRIC, "value": tflops, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": {"tf32x3": "fp32 (3xTF32 split, fp32-accurate)", "tf32": "tf32",
                                        "strict": "fp32"}[args.mode],
-        "data": "synthetic (seeded U[-1,1], no dataset)",
-        "config": {"workload": WORKLOAD, "mode": args.mode, "parallelism": f"N-column shards x{world}"
-                   if world > 1 else "single GPU", "l2": "inputs 512 MB > 126 MB L2, no flush needed"},
+        "data": "synthetic (seeded, no dataset)",
+        "config": {"workload": wl.desc, "mode": args.mode,
+                   "parallelism": f"N-column shards x{world}" if world > 1 else "single GPU",
+                   "l2": "inputs larger than the 126 MB L2, no flush" if wl.name == "c5" else
+                         "steps back to back without an L2 flush (working set fits L2)"},
         "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "modes": extras,
         "clocks": clk.summary(), "gpu_launches": launches,
     }
     print(json.dumps(line), flush=True)
 
 
-def traffic_for(mode):
-    """Per-launch DRAM bytes of the GEMM kernel from the committed ncu summary, if any."""
+def traffic_for(workload, mode):
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary, if any."""
     path = os.path.join(ROOT, "profiles", "traffic.json")
     try:
         with open(path) as f:
-            return json.load(f).get(f"config5_{mode}")
+            return json.load(f).get(f"{workload}_{mode}")
     except Exception:
         return None
 

@@ -10,7 +10,10 @@
 #include <vector>
 
 #include "Dispatch.hpp"
+#include "GraphExecutor.hpp"
+#include "Loss.hpp"
 #include "Module.hpp"
+#include "Optimizer.hpp"
 #include "Tensor.hpp"
 #include "TensorOps.hpp"
 #include "mtgemm.h"
@@ -166,6 +169,46 @@ int main() {
         bool ok;
         double e = compare(C, matmul(A, B), 1e-4, 1e-4, &ok);
         report("OpRegistry<float> Matmul dispatch", ok, e);
+    }
+    {   // include/GraphExecutor.hpp: warm-up, capture (Relaxed, on active_stream()) and replay
+        // of a whole training step; the captured GEMMs are this library's kernels. Compared
+        // step by step with eager training of an identical model.
+        auto make = [] {
+            return std::make_shared<Sequential<float>>(std::initializer_list<std::shared_ptr<Module<float>>>{
+                std::make_shared<Linear<float>>(64, 128), std::make_shared<ReLU<float>>(),
+                std::make_shared<Linear<float>>(128, 16)});
+        };
+        auto eager = make();
+        auto graphed = make();
+        auto pe = eager->parameters(), pg = graphed->parameters();
+        for (size_t i = 0; i < pe.size(); ++i)
+            std::copy(pe[i].data(), pe[i].data() + pe[i].total_elements(), pg[i].data());
+        eager->to(kGpu);
+        graphed->to(kGpu);
+        SGD<float> opt_e(eager->parameters(), 0.05f), opt_g(graphed->parameters(), 0.05f);
+        GraphExecutor<float> exec(graphed, opt_g,
+                                  [](const Tensor<float>& p, const Tensor<float>& t) { return mse_loss(p, t); });
+        Tensor<float> x = filled({32, 64}, 16).to(kGpu), y = filled({32, 16}, 17).to(kGpu);
+        bool ok = true;
+        double worst = 0;
+        for (int step = 0; step < 4; ++step) {
+            opt_e.zero_grad();
+            Tensor<float> le = mse_loss(eager->forward(x), y);
+            le.backward();
+            opt_e.step();
+            Tensor<float> lg = exec.step(x, y);
+            const double a = le.to(kCpu).data()[0], b = lg.to(kCpu).data()[0];
+            const double r = std::fabs(a - b) / (1e-5 + 1e-4 * std::fabs(a));
+            worst = std::max(worst, r);
+            ok = ok && r <= 1.0;
+        }
+        auto fe = eager->parameters(), fg = graphed->parameters();
+        for (size_t i = 0; i < fe.size(); ++i) {
+            bool pok;
+            worst = std::max(worst, compare(fg[i], fe[i].to(kCpu), 1e-4, 1e-5, &pok));
+            ok = ok && pok;
+        }
+        report("GraphExecutor capture/replay of a training step", ok, worst);
     }
     std::printf("%s: %d failure(s)\n", failures ? "FAILED" : "ALL PASSED", failures);
     return failures ? 1 : 0;
