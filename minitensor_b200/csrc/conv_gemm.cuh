@@ -86,113 +86,141 @@ __device__ __forceinline__ uint32_t off_k(int row, int k) {
     return row * 128 + ((((k >> 2) ^ (row & 7)) << 4) | ((k & 3) << 2));
 }
 
-template <bool X3>
-__device__ __forceinline__ void put(uint8_t* hi, uint8_t* lo, uint32_t off, float v) {
-    if (X3) {
-        const float h = tf32_round(v);
-        *reinterpret_cast<float*>(hi + off) = h;
-        *reinterpret_cast<float*>(lo + off) = v - h;
-    } else {
-        *reinterpret_cast<float*>(hi + off) = v;
-    }
-}
-
 // ------------------------------------------------------------------------------------
-// Producers: fill the A (BM x 32) and B (BN x 32) tiles of reduction block kb.
-// t = producer thread 0..127, lane = t & 31, pw = t >> 5.
+// Producers. issue() starts the asynchronous copies (cp.async, 4 bytes each, zero-fill for
+// padding and tile edges) of the A (128 x 32) and B (BN x 32) tiles of reduction block kb
+// straight into their swizzled slots; finish() runs once they have landed: for TF32X3 it
+// splits every element this thread copied into hi (in place) and lo (the parallel ring).
+// t = producer thread 0..127, lane = t & 31, pw = t >> 5. Element offsets are 32-bit: the
+// host checks that every view spans fewer than 2^31 elements.
 // ------------------------------------------------------------------------------------
-template <int KIND, int BN, bool X3>
-__device__ __forceinline__ void produce(const Params& p, int m0, int n0, int kb, int t, uint8_t* a_hi,
-                                        uint8_t* a_lo, uint8_t* b_hi, uint8_t* b_lo) {
+template <int KIND, int BN>
+__device__ __forceinline__ void issue(const Params& p, int m0, int n0, int kb, int t, uint32_t a, uint32_t b) {
     const int lane = t & 31, pw = t >> 5;
     const int khkw = p.kh * p.kw;
     if (KIND == kFwd || KIND == kDgrad) {
-        // ---- A: pixel m = m0 + t, k-rows k0..k0+31 ----
+        // ---- A: pixel m = m0 + t, k-rows k0..k0+31, k = (c, r, s) ----
         const int m = m0 + t;
         const bool mv = m < p.M;
-        const int HWo = (KIND == kFwd) ? p.Ho * p.Wo : p.H * p.W;
+        const int HW = (KIND == kFwd) ? p.Ho * p.Wo : p.H * p.W;
         const int wdim = (KIND == kFwd) ? p.Wo : p.W;
-        const int img = mv ? m / HWo : 0;
-        const int pix = mv ? m - img * HWo : 0;
+        const int img = mv ? m / HW : 0;
+        const int pix = mv ? m - img * HW : 0;
         const int py = pix / wdim, px = pix - py * wdim;
         const int k0 = kb * 32;
-        // incremental (c, r, s) for k = k0
         int c = k0 / khkw, rs = k0 - c * khkw;
         int r = rs / p.kw, s = rs - r * p.kw;
-        float v[32];
-#pragma unroll
-        for (int kk = 0; kk < 32; ++kk) {
-            float val = 0.f;
-            const bool kv = mv && (k0 + kk < p.K);
-            if (KIND == kFwd) {
-                const int iy = py * p.stride - p.pad + r, ix = px * p.stride - p.pad + s;
-                if (kv && iy >= 0 && iy < p.H && ix >= 0 && ix < p.W)
-                    val = __ldg(p.x + img * p.sx[0] + c * p.sx[1] + iy * p.sx[2] + ix * p.sx[3]);
-            } else {
-                // dx[iy,ix] gathers dy[oy,ox] with oy*stride - pad + r == iy.
-                const int ny = py + p.pad - r, nx = px + p.pad - s;
-                if (kv && ny >= 0 && nx >= 0 && ny % p.stride == 0 && nx % p.stride == 0) {
-                    const int oy = ny / p.stride, ox = nx / p.stride;
-                    if (oy < p.Ho && ox < p.Wo)
-                        val = __ldg(p.dy + img * p.sdy[0] + c * p.sdy[1] + oy * p.sdy[2] + ox * p.sdy[3]);
+        if (KIND == kFwd) {
+            const int s1 = (int)p.sx[1], s2 = (int)p.sx[2], s3 = (int)p.sx[3];
+            const float* base = p.x + (int64_t)img * p.sx[0];
+            const int iy0 = py * p.stride - p.pad, ix0 = px * p.stride - p.pad;
+            int off = c * s1 + r * s2 + s * s3;          // x offset of tap (c, r, s), image-relative
+            const int pixoff = iy0 * s2 + ix0 * s3;
+#pragma unroll 8
+            for (int kk = 0; kk < 32; ++kk) {
+                const bool v = mv && (k0 + kk < p.K) && (unsigned)(iy0 + r) < (unsigned)p.H &&
+                               (unsigned)(ix0 + s) < (unsigned)p.W;
+                cp_async4(a + off_mn(t, kk), v ? base + (pixoff + off) : p.x, v);
+                off += s3;
+                if (++s == p.kw) {
+                    s = 0; off += s2 - p.kw * s3;
+                    if (++r == p.kh) { r = 0; off += s1 - p.kh * s2; }
                 }
             }
-            v[kk] = val;
-            if (++s == p.kw) { s = 0; if (++r == p.kh) { r = 0; ++c; } }
+        } else {
+            // dx[iy,ix] gathers dy[oy,ox] with oy*stride - pad + r == iy.
+            const float* base = p.dy + (int64_t)img * p.sdy[0];
+            const int s1 = (int)p.sdy[1], s2 = (int)p.sdy[2], s3 = (int)p.sdy[3];
+#pragma unroll 8
+            for (int kk = 0; kk < 32; ++kk) {
+                const int ny = py + p.pad - r, nx = px + p.pad - s;
+                bool v = mv && (k0 + kk < p.K) && ny >= 0 && nx >= 0;
+                int oy = ny, ox = nx;
+                if (p.stride != 1) {
+                    v = v && (ny % p.stride == 0) && (nx % p.stride == 0);
+                    oy = ny / p.stride;
+                    ox = nx / p.stride;
+                }
+                v = v && oy < p.Ho && ox < p.Wo;
+                cp_async4(a + off_mn(t, kk), v ? base + (c * s1 + oy * s2 + ox * s3) : p.dy, v);
+                if (++s == p.kw) { s = 0; if (++r == p.kh) { r = 0; ++c; } }
+            }
         }
-#pragma unroll
-        for (int kk = 0; kk < 32; ++kk) put<X3>(a_hi, a_lo, off_mn(t, kk), v[kk]);
         // ---- B: rows n (C_out for FWD, C_in for DGRAD), k = lane ----
         const int k = k0 + lane;
         const bool kv = k < p.K;
-        int64_t koff = 0;       // part of the weight offset that depends on k only
-        int64_t nstride;        // weight stride between consecutive rows n
+        int koff = 0;            // weight offset of this k (rows add n * nstride)
         if (kv) {
             const int bc = k / khkw, q = k - bc * khkw, br = q / p.kw, bs = q - br * p.kw;
             // FWD: W[co = n, ci = bc, r, s];  DGRAD: W[co = bc, ci = n, r, s]
-            koff = (KIND == kFwd ? bc * p.sw[1] : bc * p.sw[0]) + br * p.sw[2] + bs * p.sw[3];
+            koff = (int)((KIND == kFwd ? bc * p.sw[1] : bc * p.sw[0]) + br * p.sw[2] + bs * p.sw[3]);
         }
-        nstride = (KIND == kFwd) ? p.sw[0] : p.sw[1];
+        const int nstride = (int)((KIND == kFwd) ? p.sw[0] : p.sw[1]);
 #pragma unroll 4
         for (int row = pw; row < BN; row += 4) {
             const int n = n0 + row;
-            const float val = (kv && n < p.Ncol) ? __ldg(p.w + koff + n * nstride) : 0.f;
-            put<X3>(b_hi, b_lo, off_k(row, lane), val);
+            const bool v = kv && n < p.Ncol;
+            cp_async4(b + off_k(row, lane), v ? p.w + (koff + n * nstride) : p.w, v);
         }
     } else {
         // ---- WGRAD: reduction block kb = 32 output pixels of one image ----
         const int img = kb / p.kb_per_img;
         const int p0 = (kb - img * p.kb_per_img) * 32;
-        const int HWo = p.Ho * p.Wo;
         const int pix = p0 + lane;
-        const bool pv = pix < HWo;
+        const bool pv = pix < p.Ho * p.Wo;
         const int oy = pv ? pix / p.Wo : 0, ox = pv ? pix - (pix / p.Wo) * p.Wo : 0;
         // A rows m = (ci, r, s); warp pw covers rows pw*32 .. pw*32+31.
         const int mrow0 = m0 + pw * 32;
         int c = mrow0 / khkw, rs = mrow0 - c * khkw;
         int r = rs / p.kw, s = rs - r * p.kw;
-        const float* xb = p.x + img * p.sx[0];
-        float v[32];
-#pragma unroll
+        const int s1 = (int)p.sx[1], s2 = (int)p.sx[2], s3 = (int)p.sx[3];
+        const float* xb = p.x + (int64_t)img * p.sx[0];
+        const int iy0 = oy * p.stride - p.pad, ix0 = ox * p.stride - p.pad;
+        const int pixoff = iy0 * s2 + ix0 * s3;
+        int off = c * s1 + r * s2 + s * s3;
+#pragma unroll 8
         for (int i = 0; i < 32; ++i) {
-            float val = 0.f;
-            const int iy = oy * p.stride - p.pad + r, ix = ox * p.stride - p.pad + s;
-            if (pv && mrow0 + i < p.M && iy >= 0 && iy < p.H && ix >= 0 && ix < p.W)
-                val = __ldg(xb + c * p.sx[1] + iy * p.sx[2] + ix * p.sx[3]);
-            v[i] = val;
-            if (++s == p.kw) { s = 0; if (++r == p.kh) { r = 0; ++c; } }
+            const bool v = pv && mrow0 + i < p.M && (unsigned)(iy0 + r) < (unsigned)p.H &&
+                           (unsigned)(ix0 + s) < (unsigned)p.W;
+            cp_async4(a + off_k(pw * 32 + i, lane), v ? xb + (pixoff + off) : p.x, v);
+            off += s3;
+            if (++s == p.kw) {
+                s = 0; off += s2 - p.kw * s3;
+                if (++r == p.kh) { r = 0; off += s1 - p.kh * s2; }
+            }
         }
-#pragma unroll
-        for (int i = 0; i < 32; ++i) put<X3>(a_hi, a_lo, off_k(pw * 32 + i, lane), v[i]);
         // B rows = co, k = pixel (dy[img, co, oy, ox]).
-        const float* db = p.dy + img * p.sdy[0] + oy * p.sdy[2] + ox * p.sdy[3];
+        const float* db = p.dy + (int64_t)img * p.sdy[0] + oy * p.sdy[2] + ox * p.sdy[3];
+        const int cs = (int)p.sdy[1];
 #pragma unroll 4
         for (int row = pw; row < BN; row += 4) {
             const int co = n0 + row;
-            const float val = (pv && co < p.Ncol) ? __ldg(db + co * p.sdy[1]) : 0.f;
-            put<X3>(b_hi, b_lo, off_k(row, lane), val);
+            const bool v = pv && co < p.Ncol;
+            cp_async4(b + off_k(row, lane), v ? db + co * cs : p.dy, v);
         }
     }
+}
+
+// 3xTF32: hi = rna_tf32(x) in place, lo = x - hi into the lo ring, for exactly the slots
+// this thread's issue() filled.
+template <int KIND, int BN>
+__device__ __forceinline__ void split_slots(int t, uint8_t* a, uint8_t* al, uint8_t* b, uint8_t* bl) {
+    const int lane = t & 31, pw = t >> 5;
+    auto split = [](uint8_t* hi, uint8_t* lo, uint32_t off) {
+        const float x = *reinterpret_cast<float*>(hi + off);
+        const float h = tf32_round(x);
+        *reinterpret_cast<float*>(hi + off) = h;
+        *reinterpret_cast<float*>(lo + off) = x - h;
+    };
+    if (KIND == kFwd || KIND == kDgrad) {
+#pragma unroll 8
+        for (int kk = 0; kk < 32; ++kk) split(a, al, off_mn(t, kk));
+    } else {
+#pragma unroll 8
+        for (int i = 0; i < 32; ++i) split(a, al, off_k(pw * 32 + i, lane));
+    }
+#pragma unroll 4
+    for (int row = pw; row < BN; row += 4) split(b, bl, off_k(row, lane));
 }
 
 template <int KIND, int BN, bool X3, int STAGES>
@@ -236,23 +264,43 @@ __global__ void __launch_bounds__(Cfg<BN, X3, STAGES>::THREADS, 1) conv_kernel(c
 
     if (warp >= 6) {
         // ------------------------------ gather producers ---------------------------
+        // Each thread keeps up to DEPTH stages of copies in flight: stage i is handed to
+        // the MMA issuer (split for 3xTF32, proxy fence, arrive on full) once the copies of
+        // stage i + DEPTH - 1 have been issued. DEPTH < STAGES, so the stage whose empty
+        // barrier the producer waits on was handed over long before (no cycle).
+        constexpr int DEPTH = (STAGES - 1) < 3 ? (STAGES - 1) : 3;
         const int t = threadIdx.x - 6 * 32;
-        int s = 0;
+        int s_issue = 0, s_done = 0, inflight = 0;
         uint32_t ph = 0;
+        auto hand_over = [&]() {
+            uint8_t* a = ring + s_done * G::STAGE_BYTES;
+            if (X3) {
+                uint8_t* al = ring_lo + s_done * G::STAGE_BYTES;
+                split_slots<KIND, BN>(t, a, al, a + G::A_BYTES, al + G::A_BYTES);
+            }
+            fence_proxy_async_smem();
+            mbar_arrive(smem_u32(&full[s_done]));
+            if (++s_done == STAGES) s_done = 0;
+            --inflight;
+        };
         for (long long u = first; u < p.num_units; u += step) {
             int mt, nt, sp, kb0, kb1;
             unit_coords(p, u, mt, nt, sp);
             kb_range(p, sp, kb0, kb1);
             for (int kb = kb0; kb < kb1; ++kb) {
-                if (!mbar_wait(smem_u32(&empty[s]), ph ^ 1, abort_flag, kDevTimeoutEmpty)) goto done;
-                uint8_t* a = ring + s * G::STAGE_BYTES;
-                uint8_t* al = ring_lo + s * G::STAGE_BYTES;
-                produce<KIND, BN, X3>(p, mt * G::BM, nt * BN, kb, t, a, al, a + G::A_BYTES, al + G::A_BYTES);
-                fence_proxy_async_smem();
-                mbar_arrive(smem_u32(&full[s]));
-                if (++s == STAGES) { s = 0; ph ^= 1; }
+                if (!mbar_wait(smem_u32(&empty[s_issue]), ph ^ 1, abort_flag, kDevTimeoutEmpty)) goto done;
+                const uint32_t a = smem_u32(ring + s_issue * G::STAGE_BYTES);
+                issue<KIND, BN>(p, mt * G::BM, nt * BN, kb, t, a, a + G::A_BYTES);
+                cp_async_commit();
+                if (++s_issue == STAGES) { s_issue = 0; ph ^= 1; }
+                if (++inflight == DEPTH) {
+                    cp_async_wait<DEPTH - 1>();
+                    hand_over();
+                }
             }
         }
+        cp_async_wait<0>();
+        while (inflight > 0) hand_over();
     } else if (warp == 1) {
         // ------------------------------ MMA issuer --------------------------------
         if (lane == 0) {
@@ -351,6 +399,7 @@ __global__ void __launch_bounds__(Cfg<BN, X3, STAGES>::THREADS, 1) conv_kernel(c
     }
 
 done:
+    cp_async_wait_all();   // no copy may still target this CTA's shared memory
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {

@@ -450,6 +450,14 @@ int conv_shape(const mt_tensor* x, const mt_tensor* w, const mt_tensor* y, uint6
     return MT_OK;
 }
 
+// Largest element offset a view can address; the implicit-GEMM gathers use 32-bit offsets.
+bool offsets_fit_32(const mt_tensor* t) {
+    uint64_t span = 0;
+    for (uint32_t i = 0; i < t->ndim; ++i)
+        if (t->shape[i]) span += (t->shape[i] - 1) * t->strides[i];
+    return span < (uint64_t(1) << 31);
+}
+
 mt::conv::Params conv_params(const ConvShape& s) {
     mt::conv::Params cp;
     memset(&cp, 0, sizeof cp);
@@ -498,6 +506,8 @@ int conv_fwd(const mt_tensor* x, const mt_tensor* w, const mt_tensor* bias, cons
         t_path = "conv_direct_fwd_fp32";
         return direct_launch(mt::conv::direct_fwd_kernel, cp, total, st, who);
     }
+    if (!offsets_fit_32(x) || !offsets_fit_32(w))
+        return fail(MT_EUNSUPPORTED, "%s: a view spans 2^31 elements or more", who);
     cp.M = (int)(s.N * s.Ho * s.Wo); cp.Ncol = (int)s.Co; cp.K = (int)(s.C * s.kh * s.kw);
     cp.tiles_m = (cp.M + 127) / 128;
     const int bn = pick_bn(cp.Ncol);
@@ -533,6 +543,8 @@ int conv_dgrad(const mt_tensor* dy, const mt_tensor* w, const mt_tensor* dx, uin
         t_path = "conv_direct_dgrad_fp32";
         return direct_launch(mt::conv::direct_dgrad_kernel, cp, total, st, who);
     }
+    if (!offsets_fit_32(dy) || !offsets_fit_32(w))
+        return fail(MT_EUNSUPPORTED, "%s: a view spans 2^31 elements or more", who);
     cp.M = (int)total / (int)s.C; cp.Ncol = (int)s.C; cp.K = (int)(s.Co * s.kh * s.kw);
     cp.tiles_m = (cp.M + 127) / 128;
     const int bn = pick_bn(cp.Ncol);
@@ -599,6 +611,8 @@ int conv_wgrad(const mt_tensor* dy, const mt_tensor* x, const mt_tensor* dw, uin
         t_path = "conv_direct_wgrad_fp32";
         return direct_launch(mt::conv::direct_wgrad_kernel, cp, total, st, who);
     }
+    if (!offsets_fit_32(dy) || !offsets_fit_32(x))
+        return fail(MT_EUNSUPPORTED, "%s: a view spans 2^31 elements or more", who);
     WgradPlan wp = wgrad_plan(s, di.sms);
     cp.M = (int)(s.C * s.kh * s.kw); cp.Ncol = (int)s.Co; cp.K = (int)(s.N * s.Ho * s.Wo);
     cp.tiles_m = wp.tiles_m; cp.tiles_n = wp.tiles_n;

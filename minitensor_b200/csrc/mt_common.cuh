@@ -97,6 +97,21 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
 }
 
 // ---------------------------------------------------------------------------------
+// cp.async: per-thread asynchronous global -> shared copies (used by gather producers
+// whose tiles no TMA box can describe). src_bytes 0 zero-fills the destination.
+// ---------------------------------------------------------------------------------
+__device__ __forceinline__ void cp_async4(uint32_t dst, const float* src, bool valid) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(valid ? 4 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------------
 // TMA: tiled bulk tensor loads global -> shared, completion on an mbarrier.
 // Every TMA load in this library is a plain per-CTA load (no cluster broadcast).
 // ---------------------------------------------------------------------------------
