@@ -1,6 +1,7 @@
 // mt_api.cu -- the C ABI of libmtgemm.so (declared in include/mtgemm.h): argument
 // checks with the reference's error semantics, view -> problem mapping, kernel
 // selection, TMA tensor-map encoding and launches.
+#include <algorithm>
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
@@ -272,7 +273,30 @@ int launch_umma(const GemmProblem& p, bool x3, cudaStream_t st, float* const* ex
     up.tiles_m = (int)tiles_m;
     up.tiles_n = (int)((p.N + bn - 1) / bn);
     up.num_tiles = (long long)up.tiles_m * up.tiles_n * p.batch;
-    const int grid = (int)std::min<long long>(up.num_tiles, (long long)di.sms);
+    // Split-K when the output has too few tiles to occupy the GPU (e.g. the Linear
+    // backward dX = dY . W^T: 16 tiles, K = 4096): fp32 partials in a stream-ordered
+    // workspace, then one pass that sums them in split order and applies the epilogue.
+    const int kblocks = (int)((p.K + bke - 1) / bke);
+    int splits = 1;
+    if (p.batch == 1 && nextra == 0 && up.num_tiles * 2 <= di.sms && kblocks >= 8)
+        splits = (int)std::max<long long>(
+            1, std::min<long long>(std::min<long long>(di.sms / up.num_tiles, kblocks / 4), 16));
+    up.splits = splits;
+    up.num_units = up.num_tiles * splits;
+    float* ws = nullptr;
+    if (splits > 1) {
+        const size_t bytes = (size_t)splits * (size_t)p.M * (size_t)p.N * sizeof(float);
+        cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&ws), bytes, st);
+        if (e != cudaSuccess) return cuda_fail(e, "gemm split-K workspace");
+        up.dst[0] = ws;
+        up.sc_m = p.N;
+        up.split_stride = (int64_t)p.M * p.N;
+        up.epi = 0;
+        up.vec_store = p.N % 4 == 0;
+    } else {
+        up.split_stride = 0;
+    }
+    const int grid = (int)std::min<long long>(up.num_units, (long long)di.sms);
 
     int rc;
 #define MT_UMMA_DISPATCH(BN_, BKE_, X3_, ST_)                                                       \
@@ -288,10 +312,21 @@ int launch_umma(const GemmProblem& p, bool x3, cudaStream_t st, float* const* ex
         else { MT_UMMA_DISPATCH(128, 16, true, 6) }
     }
 #undef MT_UMMA_DISPATCH
+    if (splits > 1) {
+        if (rc == MT_OK) {
+            const int blocks = (int)std::min<int64_t>((p.M * p.N + 255) / 256, 8 * di.sms);
+            mt::umma::splitk_epilogue_kernel<<<blocks, 256, 0, st>>>(ws, splits, (int)p.M, (int)p.N, p.C, p.sc_m,
+                                                                     p.bias, p.epi);
+            cudaError_t e = cudaGetLastError();
+            if (e != cudaSuccess && e != cudaErrorStreamCaptureUnsupported) rc = cuda_fail(e, "split-K epilogue");
+            else g_launches.fetch_add(1);
+        }
+        cudaFreeAsync(ws, st);
+    }
     if (rc == MT_OK) {
-        char buf[96];
-        snprintf(buf, sizeof buf, "umma_%s bn=%d a=%s b=%s", x3 ? "tf32x3" : "tf32", bn, a_mn ? "MN" : "K",
-                 b_mn ? "MN" : "K");
+        char buf[112];
+        snprintf(buf, sizeof buf, "umma_%s bn=%d a=%s b=%s%s", x3 ? "tf32x3" : "tf32", bn, a_mn ? "MN" : "K",
+                 b_mn ? "MN" : "K", splits > 1 ? (" splitk=" + std::to_string(splits)).c_str() : "");
         t_path = buf;
     }
     return rc;

@@ -45,8 +45,19 @@ struct Params {
     int epi;
     int vec_store;              // rows 16-byte aligned and N % 4 == 0
     int tiles_m, tiles_n;
-    long long num_tiles;
+    long long num_tiles;        // output tiles
+    // Split-K: unit u is tile u / splits, k-split u % splits (k-blocks [kb0, kb1)); the
+    // epilogue of split s writes raw partial sums at dst[d] + s * split_stride.
+    int splits;
+    int64_t split_stride;
+    long long num_units;        // num_tiles * splits
 };
+
+// k-blocks of split `sp`: a near-equal contiguous share of [0, kblocks).
+__device__ __forceinline__ void split_range(const Params& p, int kblocks, int sp, int& kb0, int& kb1) {
+    kb0 = (int)((long long)kblocks * sp / p.splits);
+    kb1 = (int)((long long)kblocks * (sp + 1) / p.splits);
+}
 
 template <int BN, int BKE_, bool X3, int STAGES>
 struct Cfg {
@@ -146,12 +157,13 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         if (lane == 0) {
             int s = 0;
             uint32_t ph = 0;
-            for (long long t = first_tile; t < p.num_tiles; t += tile_step) {
-                int b, mb, nb;
-                tile_coords(p, t, b, mb, nb);
+            for (long long u = first_tile; u < p.num_units; u += tile_step) {
+                int b, mb, nb, kb0, kb1;
+                tile_coords(p, u / p.splits, b, mb, nb);
+                split_range(p, kblocks, (int)(u % p.splits), kb0, kb1);
                 const int m0 = mb * BM, n0 = nb * BN;
                 const int ab = p.a_batched ? b : 0, bb = p.b_batched ? b : 0;
-                for (int kb = 0; kb < kblocks; ++kb) {
+                for (int kb = kb0; kb < kb1; ++kb) {
                     if (!mbar_wait(smem_u32(&empty[s]), ph ^ 1, abort_flag, kDevTimeoutEmpty)) goto done;
                     const uint32_t bar = smem_u32(&full[s]);
                     mbar_arrive_expect_tx(bar, G::STAGE_BYTES);
@@ -183,13 +195,15 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             int s = 0;
             uint32_t ph = 0;
             int it = 0;
-            for (long long t = first_tile; t < p.num_tiles; t += tile_step, ++it) {
+            for (long long u = first_tile; u < p.num_units; u += tile_step, ++it) {
+                int kb0, kb1;
+                split_range(p, kblocks, (int)(u % p.splits), kb0, kb1);
                 const int a = it & 1;
                 const uint32_t aph = (it >> 1) & 1;
                 if (!mbar_wait(smem_u32(&acc_empty[a]), aph ^ 1, abort_flag, kDevTimeoutAccEmpty)) goto done;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + a * BN;
-                for (int kb = 0; kb < kblocks; ++kb) {
+                for (int kb = kb0; kb < kb1; ++kb) {
                     uint32_t wbar = X3 ? smem_u32(&conv[s]) : smem_u32(&full[s]);
                     if (!mbar_wait(wbar, ph, abort_flag, kDevTimeoutFull)) goto done;
                     tc_fence_after();
@@ -199,7 +213,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                     for (int k = 0; k < G::KSTEPS; ++k) {
                         const uint64_t ad = operand_desc<A_MN, BKE>(sa, k);
                         const uint64_t bd = operand_desc<B_MN, BKE>(sb, k);
-                        const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+                        const uint32_t acc = (kb > kb0 || k > 0) ? 1u : 0u;
                         if (X3) {
                             const uint32_t la = smem_u32(ring_lo + s * G::STAGE_BYTES);
                             const uint32_t lb = la + G::A_BYTES;
@@ -222,16 +236,19 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         // ------------------------------ epilogue ----------------------------------
         const int q = warp & 3;   // TMEM lane quarter this warp may access
         int it = 0;
-        for (long long t = first_tile; t < p.num_tiles; t += tile_step, ++it) {
-            int b, mb, nb;
-            tile_coords(p, t, b, mb, nb);
+        for (long long u = first_tile; u < p.num_units; u += tile_step, ++it) {
+            int b, mb, nb, kb0, kb1;
+            tile_coords(p, u / p.splits, b, mb, nb);
+            const int sp = (int)(u % p.splits);
+            split_range(p, kblocks, sp, kb0, kb1);
+            const bool no_k = kb1 <= kb0;   // this split got no k-blocks: its partial is zero
             const int a = it & 1;
             const uint32_t aph = (it >> 1) & 1;
             if (!mbar_wait(smem_u32(&acc_full[a]), aph, abort_flag, kDevTimeoutAccFull)) goto done;
             __syncwarp();   // tcgen05.ld below is .sync.aligned: reconverge after the spin
             tc_fence_after();
             const int m = mb * BM + q * 32 + lane;
-            const int64_t row_off = (int64_t)b * p.sc_b + (int64_t)m * p.sc_m;
+            const int64_t row_off = (int64_t)b * p.sc_b + (int64_t)m * p.sc_m + (int64_t)sp * p.split_stride;
             const float bias_row = (p.epi & 1) && m < p.M ? __ldg(p.bias + m) : 0.f;
 #pragma unroll 1
             for (int c = 0; c < BN / 32; ++c) {
@@ -246,7 +263,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                 float v[32];
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
-                    float x = __uint_as_float(r[j]) + bias_row;
+                    float x = (no_k ? 0.f : __uint_as_float(r[j])) + bias_row;
                     if (p.epi & 2) x = x + ((n0 + j < p.N) ? __ldg(p.bias + n0 + j) : 0.f);
                     if (p.epi & 4) x = x > 0.f ? x : 0.f;
                     v[j] = x;
@@ -275,8 +292,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         const int ct = threadIdx.x - 6 * 32;   // 0..127
         int s = 0;
         uint32_t ph = 0;
-        for (long long t = first_tile; t < p.num_tiles; t += tile_step) {
-            for (int kb = 0; kb < kblocks; ++kb) {
+        for (long long u = first_tile; u < p.num_units; u += tile_step) {
+            int kb0, kb1;
+            split_range(p, kblocks, (int)(u % p.splits), kb0, kb1);
+            for (int kb = kb0; kb < kb1; ++kb) {
                 if (!mbar_wait(smem_u32(&full[s]), ph, abort_flag, kDevTimeoutMisc)) goto done;
                 float4* hi = reinterpret_cast<float4*>(ring + s * G::STAGE_BYTES);
                 float4* lo = reinterpret_cast<float4*>(ring_lo + s * G::STAGE_BYTES);
@@ -301,6 +320,22 @@ done:
         __syncwarp();
         tc_fence_after();
         tmem_dealloc(tmem_base, G::TMEM_COLS);
+    }
+}
+
+// C[m, n] = epi(sum over splits s (in order) of ws[s][m][n]); ws rows have N elements.
+__global__ void splitk_epilogue_kernel(const float* __restrict__ ws, int splits, int M, int N, float* C, int64_t sc_m,
+                                       const float* __restrict__ bias, int epi) {
+    const int64_t total = (int64_t)M * N;
+    const int64_t plane = total;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int m = (int)(i / N), n = (int)(i - (int64_t)m * N);
+        float acc = 0.f;
+        for (int s = 0; s < splits; ++s) acc += ws[s * plane + i];
+        if (epi & 1) acc = acc + __ldg(bias + m);
+        if (epi & 2) acc = acc + __ldg(bias + n);
+        if (epi & 4) acc = acc > 0.f ? acc : 0.f;
+        C[(int64_t)m * sc_m + n] = acc;
     }
 }
 
