@@ -15,6 +15,7 @@
 #include "simt_gemm.cuh"
 #include "umma_gemm.cuh"
 #include "conv_gemm.cuh"
+#include "conv_tma.cuh"
 
 namespace {
 
@@ -113,6 +114,24 @@ bool encode_3d(CUtensorMap* m, const float* base, uint64_t d0, uint64_t d1, uint
                           : swizzle_bytes == 32  ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
                                                  : CU_TENSOR_MAP_SWIZZLE_NONE;
     CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+// 4-D fp32 map {d0 (contiguous), d1, d2, d3}, byte strides s[0..2] of d1..d3, box b[4].
+bool encode_4d(CUtensorMap* m, const float* base, const uint64_t (&d)[4], const uint64_t (&st)[3],
+               const uint32_t (&b)[4], int swizzle_bytes) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[4] = {d[0], d[1], d[2], d[3]};
+    cuuint64_t strides[3] = {st[0], st[1], st[2]};
+    cuuint32_t box[4] = {b[0], b[1], b[2], b[3]};
+    cuuint32_t es[4] = {1, 1, 1, 1};
+    CUtensorMapSwizzle sw = swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                          : swizzle_bytes == 32  ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                                                 : CU_TENSOR_MAP_SWIZZLE_NONE;
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(base), dims, strides, box, es,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
@@ -514,6 +533,130 @@ int direct_launch(void (*kern)(const mt::conv::Params), const mt::conv::Params& 
     return MT_OK;
 }
 
+// ---- TMA conv path ----------------------------------------------------------------
+int launch_simple(cudaError_t e, const char* what) {
+    if (e != cudaSuccess && e != cudaErrorStreamCaptureUnsupported) return cuda_fail(e, what);
+    g_launches.fetch_add(1);
+    return MT_OK;
+}
+
+// NCHW view -> NHWC copy with Cp = round_up(C, 4) channels.
+int to_nhwc(const float* src, const int64_t (&sv)[4], float* dst, int N, int C, int H, int W, cudaStream_t st) {
+    const int Cp = (C + 3) & ~3;
+    dim3 grid((W + 31) / 32, (Cp + 31) / 32, (unsigned)(N * H));
+    mt::convt::nchw_to_nhwc_kernel<<<grid, dim3(32, 8), 0, st>>>(src, sv[0], sv[1], sv[2], sv[3], dst, C, H, W, Cp);
+    return launch_simple(cudaGetLastError(), "nchw_to_nhwc");
+}
+
+int reorder_w(const float* w, const int64_t (&sw)[4], float* wt, int Co, int C, int kh, int kw, bool dgrad,
+              cudaStream_t st) {
+    const int rows = dgrad ? C : Co, cols = dgrad ? Co : C;
+    const int64_t total = (int64_t)kh * kw * rows * ((cols + 3) & ~3);
+    const int blocks = (int)std::min<int64_t>((total + 255) / 256, 1024);
+    mt::convt::reorder_weights_kernel<<<blocks, 256, 0, st>>>(w, sw[0], sw[1], sw[2], sw[3], wt, Co, C, kh, kw,
+                                                              dgrad ? 1 : 0);
+    return launch_simple(cudaGetLastError(), "reorder_weights");
+}
+
+template <typename Kern>
+int set_smem(Kern kern, uint32_t bytes, std::atomic<uint64_t>& mask) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(mask.load() & bit)) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+        if (e != cudaSuccess) return cuda_fail(e, "conv: set smem attribute");
+        mask.fetch_or(bit);
+    }
+    return MT_OK;
+}
+
+template <int BN, bool X3, int STAGES>
+int launch_fwd_tma_inst(const CUtensorMap& ta, const CUtensorMap& tb, const mt::convt::FwdParams& fp, int grid,
+                        cudaStream_t st) {
+    using G = mt::convt::Cfg<BN, X3, STAGES>;
+    auto kern = mt::convt::conv_fwd_tma_kernel<BN, X3, STAGES>;
+    static std::atomic<uint64_t> mask{0};
+    int rc = set_smem(kern, G::SMEM_BYTES, mask);
+    if (rc) return rc;
+    kern<<<grid, G::THREADS, G::SMEM_BYTES, st>>>(ta, tb, fp);
+    return launch_simple(cudaGetLastError(), "conv fwd tma");
+}
+
+template <int BN, bool X3, int STAGES>
+int launch_wgrad_tma_inst(const CUtensorMap& ta, const CUtensorMap& tb, const mt::convt::WgradParams& wp, int grid,
+                          cudaStream_t st) {
+    using G = mt::convt::Cfg<BN, X3, STAGES>;
+    auto kern = mt::convt::conv_wgrad_tma_kernel<BN, X3, STAGES>;
+    static std::atomic<uint64_t> mask{0};
+    int rc = set_smem(kern, G::SMEM_BYTES, mask);
+    if (rc) return rc;
+    kern<<<grid, G::THREADS, G::SMEM_BYTES, st>>>(ta, tb, wp);
+    return launch_simple(cudaGetLastError(), "conv wgrad tma");
+}
+
+// Stages keep the ring (doubled for the lo copy) within ~192 KB of shared memory.
+template <bool X3>
+int launch_fwd_tma(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const mt::convt::FwdParams& fp, int grid,
+                   cudaStream_t st) {
+    switch (bn) {
+        case 32:  return launch_fwd_tma_inst<32, X3, X3 ? 4 : 8>(ta, tb, fp, grid, st);
+        case 64:  return launch_fwd_tma_inst<64, X3, X3 ? 4 : 8>(ta, tb, fp, grid, st);
+        case 128: return launch_fwd_tma_inst<128, X3, X3 ? 3 : 6>(ta, tb, fp, grid, st);
+        default:  return launch_fwd_tma_inst<256, X3, X3 ? 2 : 4>(ta, tb, fp, grid, st);
+    }
+}
+template <bool X3>
+int launch_wgrad_tma(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const mt::convt::WgradParams& wp, int grid,
+                     cudaStream_t st) {
+    switch (bn) {
+        case 32:  return launch_wgrad_tma_inst<32, X3, X3 ? 4 : 8>(ta, tb, wp, grid, st);
+        case 64:  return launch_wgrad_tma_inst<64, X3, X3 ? 4 : 8>(ta, tb, wp, grid, st);
+        case 128: return launch_wgrad_tma_inst<128, X3, X3 ? 3 : 6>(ta, tb, wp, grid, st);
+        default:  return launch_wgrad_tma_inst<256, X3, X3 ? 2 : 4>(ta, tb, wp, grid, st);
+    }
+}
+
+// Forward-shaped TMA conv: `act` is an NHWC activation [N, Hin, Win, Cin_p] (Cin real
+// channels), `wt` the reordered weights [taps][Ncol][Cin_p], output `out` NCHW [N, Ncol, Ho, Wo].
+int run_fwd_tma(const float* act, int N, int Hin, int Win, int Cin, const float* wt, int Ncol, int kh, int kw,
+                int pad, float* out, int Ho, int Wo, const float* bias, bool x3, cudaStream_t st, int sms,
+                std::string& path) {
+    const int Cinp = (Cin + 3) & ~3;
+    mt::convt::FwdParams fp;
+    memset(&fp, 0, sizeof fp);
+    fp.N = N; fp.Ho = Ho; fp.Wo = Wo; fp.Ncol = Ncol; fp.C = Cin; fp.kh = kh; fp.kw = kw; fp.pad = pad;
+    fp.TX = std::min(Wo, 128);
+    fp.TY = std::max(1, std::min(128 / fp.TX, Ho));
+    fp.tiles_y = (Ho + fp.TY - 1) / fp.TY;
+    fp.tiles_x = (Wo + fp.TX - 1) / fp.TX;
+    const int bn = pick_bn(Ncol);
+    fp.tiles_n = (Ncol + bn - 1) / bn;
+    fp.cblocks = (Cin + 31) / 32;
+    fp.kblocks = kh * kw * fp.cblocks;
+    fp.num_tiles = (long long)N * fp.tiles_y * fp.tiles_x * fp.tiles_n;
+    fp.a_box_bytes = 32u * fp.TX * fp.TY * 4u;
+    fp.out = out;
+    fp.bias = bias;
+    CUtensorMap ta, tb;
+    const uint64_t rowb = (uint64_t)Cinp * 4;
+    if (!encode_4d(&ta, act, {(uint64_t)Cin, (uint64_t)Win, (uint64_t)Hin, (uint64_t)N},
+                   {rowb, rowb * Win, rowb * Win * Hin}, {32u, (uint32_t)fp.TX, (uint32_t)fp.TY, 1u}, 128))
+        return fail(MT_EUNSUPPORTED, "conv tma: activation tensor map rejected");
+    if (!encode_3d(&tb, wt, (uint64_t)Cin, (uint64_t)Ncol, (uint64_t)(kh * kw), rowb, rowb * Ncol, 32, bn, 128))
+        return fail(MT_EUNSUPPORTED, "conv tma: weight tensor map rejected");
+    const int grid = (int)std::min<long long>(fp.num_tiles, sms);
+    int rc = x3 ? launch_fwd_tma<true>(bn, ta, tb, fp, grid, st) : launch_fwd_tma<false>(bn, ta, tb, fp, grid, st);
+    path = std::string("tma bn=") + std::to_string(bn) + " tile=" + std::to_string(fp.TY) + "x" +
+           std::to_string(fp.TX);
+    return rc;
+}
+
+size_t fwd_tma_scratch(int64_t N, int64_t H, int64_t W, int64_t C, int64_t Co, int64_t taps) {
+    const int64_t Cp = (C + 3) & ~3;
+    return (size_t)(N * H * W * Cp + taps * Co * Cp) * sizeof(float) + 256;
+}
+
 int conv_fwd(const mt_tensor* x, const mt_tensor* w, const mt_tensor* bias, const mt_tensor* y, uint64_t stride,
              uint64_t pad, int mode, cudaStream_t st, const char* who) {
     int rc;
@@ -541,6 +684,24 @@ int conv_fwd(const mt_tensor* x, const mt_tensor* w, const mt_tensor* bias, cons
         t_path = "conv_direct_fwd_fp32";
         return direct_launch(mt::conv::direct_fwd_kernel, cp, total, st, who);
     }
+    const bool x3 = mode == MT_TF32X3;
+    if (s.stride == 1) {
+        // TMA path: x -> NHWC and W -> [tap][co][ci] in a stream-ordered scratch buffer.
+        const size_t bytes = fwd_tma_scratch(s.N, s.H, s.W, s.C, s.Co, s.kh * s.kw);
+        float* scratch = nullptr;
+        cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&scratch), bytes, st);
+        if (e != cudaSuccess) return cuda_fail(e, "conv fwd scratch");
+        float* xt = scratch;
+        float* wt = scratch + ((s.N * s.H * s.W * ((s.C + 3) & ~3) + 63) & ~int64_t(63));
+        std::string path;
+        rc = to_nhwc(cp.x, cp.sx, xt, (int)s.N, (int)s.C, (int)s.H, (int)s.W, st);
+        if (!rc) rc = reorder_w(cp.w, cp.sw, wt, (int)s.Co, (int)s.C, (int)s.kh, (int)s.kw, false, st);
+        if (!rc) rc = run_fwd_tma(xt, (int)s.N, (int)s.H, (int)s.W, (int)s.C, wt, (int)s.Co, (int)s.kh, (int)s.kw,
+                                  (int)s.pad, cp.out, (int)s.Ho, (int)s.Wo, bp, x3, st, di.sms, path);
+        cudaFreeAsync(scratch, st);
+        if (rc == MT_OK) t_path = std::string("conv_umma_fwd_") + (x3 ? "tf32x3 " : "tf32 ") + path;
+        return rc;
+    }
     if (!offsets_fit_32(x) || !offsets_fit_32(w))
         return fail(MT_EUNSUPPORTED, "%s: a view spans 2^31 elements or more", who);
     cp.M = (int)(s.N * s.Ho * s.Wo); cp.Ncol = (int)s.Co; cp.K = (int)(s.C * s.kh * s.kw);
@@ -551,9 +712,8 @@ int conv_fwd(const mt_tensor* x, const mt_tensor* w, const mt_tensor* bias, cons
     cp.num_units = (long long)cp.tiles_m * cp.tiles_n;
     if (cp.K == 0) return fail(MT_EUNSUPPORTED, "%s: empty reduction", who);
     const int grid = (int)std::min<long long>(cp.num_units, di.sms);
-    const bool x3 = mode == MT_TF32X3;
     rc = x3 ? launch_conv_bn<mt::conv::kFwd, true>(cp, bn, grid, st) : launch_conv_bn<mt::conv::kFwd, false>(cp, bn, grid, st);
-    if (rc == MT_OK) t_path = std::string("conv_umma_fwd_") + (x3 ? "tf32x3" : "tf32") + " bn=" + std::to_string(bn);
+    if (rc == MT_OK) t_path = std::string("conv_umma_fwd_") + (x3 ? "tf32x3" : "tf32") + " gather bn=" + std::to_string(bn);
     return rc;
 }
 
@@ -578,6 +738,25 @@ int conv_dgrad(const mt_tensor* dy, const mt_tensor* w, const mt_tensor* dx, uin
         t_path = "conv_direct_dgrad_fp32";
         return direct_launch(mt::conv::direct_dgrad_kernel, cp, total, st, who);
     }
+    const bool x3 = mode == MT_TF32X3;
+    if (s.stride == 1 && s.Ho > 0 && s.Wo > 0 && s.kh - 1 - s.pad >= 0 && s.kw - 1 - s.pad >= 0) {
+        // Stride 1: dx = forward conv of NHWC dy with W flipped and transposed, padding
+        // kh-1-pad (the dy positions an input pixel receives from).
+        const size_t bytes = fwd_tma_scratch(s.N, s.Ho, s.Wo, s.Co, s.C, s.kh * s.kw);
+        float* scratch = nullptr;
+        cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&scratch), bytes, st);
+        if (e != cudaSuccess) return cuda_fail(e, "conv dgrad scratch");
+        float* dyt = scratch;
+        float* wt = scratch + ((s.N * s.Ho * s.Wo * ((s.Co + 3) & ~3) + 63) & ~int64_t(63));
+        std::string path;
+        rc = to_nhwc(cp.dy, cp.sdy, dyt, (int)s.N, (int)s.Co, (int)s.Ho, (int)s.Wo, st);
+        if (!rc) rc = reorder_w(cp.w, cp.sw, wt, (int)s.Co, (int)s.C, (int)s.kh, (int)s.kw, true, st);
+        if (!rc) rc = run_fwd_tma(dyt, (int)s.N, (int)s.Ho, (int)s.Wo, (int)s.Co, wt, (int)s.C, (int)s.kh, (int)s.kw,
+                                  (int)(s.kh - 1 - s.pad), cp.out, (int)s.H, (int)s.W, nullptr, x3, st, di.sms, path);
+        cudaFreeAsync(scratch, st);
+        if (rc == MT_OK) t_path = std::string("conv_umma_dgrad_") + (x3 ? "tf32x3 " : "tf32 ") + path;
+        return rc;
+    }
     if (!offsets_fit_32(dy) || !offsets_fit_32(w))
         return fail(MT_EUNSUPPORTED, "%s: a view spans 2^31 elements or more", who);
     cp.M = (int)total / (int)s.C; cp.Ncol = (int)s.C; cp.K = (int)(s.Co * s.kh * s.kw);
@@ -591,7 +770,6 @@ int conv_dgrad(const mt_tensor* dy, const mt_tensor* w, const mt_tensor* dx, uin
         return e == cudaSuccess ? MT_OK : cuda_fail(e, who);
     }
     const int grid = (int)std::min<long long>(cp.num_units, di.sms);
-    const bool x3 = mode == MT_TF32X3;
     rc = x3 ? launch_conv_bn<mt::conv::kDgrad, true>(cp, bn, grid, st) : launch_conv_bn<mt::conv::kDgrad, false>(cp, bn, grid, st);
     if (rc == MT_OK) t_path = std::string("conv_umma_dgrad_") + (x3 ? "tf32x3" : "tf32") + " bn=" + std::to_string(bn);
     return rc;
@@ -619,8 +797,75 @@ WgradPlan wgrad_plan(const ConvShape& s, int sms) {
     return w;
 }
 
+// Weight-grad on the TMA path: x -> NHWC (xt), partials [splits][taps*C][Cop].
+struct WgradTmaPlan {
+    bool ok;
+    int bn, tiles_m, tiles_n, xblocks, kb_per_img, kb_total, splits, M, ws_ld;
+    size_t xt_floats, part_floats, bytes;
+};
+
+WgradTmaPlan wgrad_tma_plan(const ConvShape& s, const mt_tensor* dy, int sms) {
+    WgradTmaPlan w;
+    memset(&w, 0, sizeof w);
+    const bool dy_ok = dy->strides[3] == 1 && dy->strides[2] % 4 == 0 && dy->strides[1] % 4 == 0 &&
+                       dy->strides[0] % 4 == 0 && (((uintptr_t)(dy->data + dy->offset)) & 15) == 0;
+    w.ok = s.stride == 1 && s.C % 32 == 0 && dy_ok && s.N * s.Ho * s.Wo > 0;
+    if (!w.ok) return w;
+    w.M = (int)(s.kh * s.kw * s.C);
+    w.bn = pick_bn((int)s.Co);
+    w.tiles_m = (w.M + 127) / 128;
+    w.tiles_n = ((int)s.Co + w.bn - 1) / w.bn;
+    w.ws_ld = w.tiles_n * w.bn;
+    w.xblocks = (int)((s.Wo + 31) / 32);
+    w.kb_per_img = (int)s.Ho * w.xblocks;
+    w.kb_total = (int)s.N * w.kb_per_img;
+    const int tiles = w.tiles_m * w.tiles_n;
+    w.splits = std::max(1, std::min(tiles >= sms ? 1 : sms / tiles, w.kb_total));
+    w.xt_floats = (size_t)(s.N * s.H * s.W * ((s.C + 3) & ~3));
+    w.xt_floats = (w.xt_floats + 63) & ~size_t(63);
+    w.part_floats = (size_t)w.splits * w.M * w.ws_ld;
+    w.bytes = (w.xt_floats + w.part_floats) * sizeof(float);
+    return w;
+}
+
+int conv_wgrad_tma(const ConvShape& s, const WgradTmaPlan& w, const mt::conv::Params& cp, float* dwp, float* scratch,
+                   bool x3, cudaStream_t st, int sms, const char* who) {
+    float* xt = scratch;
+    float* part = scratch + w.xt_floats;
+    int rc = to_nhwc(cp.x, cp.sx, xt, (int)s.N, (int)s.C, (int)s.H, (int)s.W, st);
+    if (rc) return rc;
+    mt::convt::WgradParams wp;
+    memset(&wp, 0, sizeof wp);
+    wp.N = (int)s.N; wp.Ho = (int)s.Ho; wp.Wo = (int)s.Wo; wp.C = (int)s.C; wp.Co = (int)s.Co;
+    wp.kh = (int)s.kh; wp.kw = (int)s.kw; wp.pad = (int)s.pad;
+    wp.M = w.M; wp.tiles_m = w.tiles_m; wp.tiles_n = w.tiles_n; wp.xblocks = w.xblocks;
+    wp.kb_per_img = w.kb_per_img; wp.kb_total = w.kb_total; wp.splits = w.splits;
+    wp.num_units = (long long)w.tiles_m * w.tiles_n * w.splits;
+    wp.ws = part;
+    wp.ws_ld = w.ws_ld;
+    CUtensorMap ta, tb;
+    const uint64_t Cp = (uint64_t)((s.C + 3) & ~3), rowb = Cp * 4;
+    // A: NHWC x as M-major 32-channel chunks x 32 pixels (K) of one row.
+    if (!encode_4d(&ta, xt, {(uint64_t)s.C, (uint64_t)s.W, (uint64_t)s.H, (uint64_t)s.N},
+                   {rowb, rowb * s.W, rowb * s.W * s.H}, {32u, 32u, 1u, 1u}, 32))
+        return fail(MT_EUNSUPPORTED, "%s: activation tensor map rejected", who);
+    // B: dy straight from NCHW, rows = C_out, 32 pixels of one output row (K-major).
+    if (!encode_4d(&tb, cp.dy, {(uint64_t)s.Wo, (uint64_t)s.Ho, (uint64_t)s.Co, (uint64_t)s.N},
+                   {(uint64_t)cp.sdy[2] * 4, (uint64_t)cp.sdy[1] * 4, (uint64_t)cp.sdy[0] * 4},
+                   {32u, 1u, (uint32_t)w.bn, 1u}, 128))
+        return fail(MT_EUNSUPPORTED, "%s: grad_output tensor map rejected", who);
+    const int grid = (int)std::min<long long>(wp.num_units, sms);
+    rc = x3 ? launch_wgrad_tma<true>(w.bn, ta, tb, wp, grid, st) : launch_wgrad_tma<false>(w.bn, ta, tb, wp, grid, st);
+    if (rc) return rc;
+    const int64_t total = s.Co * s.C * s.kh * s.kw;
+    const int blocks = (int)std::min<int64_t>((total + 255) / 256, 4 * sms);
+    mt::convt::wgrad_reduce_kernel<<<blocks, 256, 0, st>>>(part, w.splits, w.M, w.ws_ld, dwp, (int)s.Co, (int)s.C,
+                                                           (int)(s.kh * s.kw));
+    return launch_simple(cudaGetLastError(), "wgrad reduce");
+}
+
 int conv_wgrad(const mt_tensor* dy, const mt_tensor* x, const mt_tensor* dw, uint64_t stride, uint64_t pad, int mode,
-               void* workspace, size_t ws_bytes, cudaStream_t st, const char* who) {
+               void* workspace, size_t ws_bytes, cudaStream_t st, const char* who, bool allow_tma = true) {
     int rc;
     if ((rc = check4(dy, who, "grad_output")) || (rc = check4(x, who, "input")) || (rc = check4(dw, who, "grad_weight")))
         return rc;
@@ -648,6 +893,26 @@ int conv_wgrad(const mt_tensor* dy, const mt_tensor* x, const mt_tensor* dw, uin
     }
     if (!offsets_fit_32(dy) || !offsets_fit_32(x))
         return fail(MT_EUNSUPPORTED, "%s: a view spans 2^31 elements or more", who);
+    const bool x3w = mode == MT_TF32X3;
+    const WgradTmaPlan tp = allow_tma ? wgrad_tma_plan(s, dy, di.sms) : WgradTmaPlan{};
+    if (tp.ok) {
+        float* scratch = static_cast<float*>(workspace);
+        bool owned = false;
+        if (workspace) {
+            if (ws_bytes < tp.bytes)
+                return fail(MT_EINVAL, "%s: workspace of %zu bytes < %zu needed", who, ws_bytes, tp.bytes);
+        } else {
+            cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&scratch), tp.bytes, st);
+            if (e != cudaSuccess) return cuda_fail(e, "conv wgrad scratch");
+            owned = true;
+        }
+        rc = conv_wgrad_tma(s, tp, cp, dwp, scratch, x3w, st, di.sms, who);
+        if (owned) cudaFreeAsync(scratch, st);
+        if (rc == MT_OK)
+            t_path = std::string("conv_umma_wgrad_") + (x3w ? "tf32x3" : "tf32") + " tma bn=" + std::to_string(tp.bn) +
+                     " splits=" + std::to_string(tp.splits);
+        return rc;
+    }
     WgradPlan wp = wgrad_plan(s, di.sms);
     cp.M = (int)(s.C * s.kh * s.kw); cp.Ncol = (int)s.Co; cp.K = (int)(s.N * s.Ho * s.Wo);
     cp.tiles_m = wp.tiles_m; cp.tiles_n = wp.tiles_n;
@@ -669,7 +934,7 @@ int conv_wgrad(const mt_tensor* dy, const mt_tensor* x, const mt_tensor* dw, uin
     }
     cp.out = part;
     const int grid = (int)std::min<long long>(cp.num_units, di.sms);
-    const bool x3 = mode == MT_TF32X3;
+    const bool x3 = x3w;
     const int bn = pick_bn(cp.Ncol);
     rc = x3 ? launch_conv_bn<mt::conv::kWgrad, true>(cp, bn, grid, st) : launch_conv_bn<mt::conv::kWgrad, false>(cp, bn, grid, st);
     if (rc == MT_OK && wp.splits > 1) {
@@ -681,7 +946,7 @@ int conv_wgrad(const mt_tensor* dy, const mt_tensor* x, const mt_tensor* dw, uin
     }
     if (owned) cudaFreeAsync(part, st);
     if (rc == MT_OK)
-        t_path = std::string("conv_umma_wgrad_") + (x3 ? "tf32x3" : "tf32") + " bn=" + std::to_string(bn) +
+        t_path = std::string("conv_umma_wgrad_") + (x3 ? "tf32x3" : "tf32") + " gather bn=" + std::to_string(bn) +
                  " splits=" + std::to_string(wp.splits);
     return rc;
 }
@@ -898,7 +1163,14 @@ int noalloc_scratch(float** out) {
 MT_API int mt_conv2d_wgrad_noalloc(const mt_tensor* dy, const mt_tensor* x, const mt_tensor* dw, uint64_t stride,
                                    uint64_t padding, int mode, void* stream) {
     if (mode < MT_MODE_DEFAULT || mode > MT_TF32X3) return fail(MT_EINVAL, "conv2d_wgrad_noalloc: bad mode %d", mode);
-    const size_t need = mt_conv2d_wgrad_workspace_bytes(dy, x, dw, stride, padding, mode);
+    // This variant always takes the gather kernel (its only scratch is the partials).
+    size_t need = 0;
+    if (dy && x && dw && dy->ndim == 4 && x->ndim == 4 && dw->ndim == 4) {
+        ConvShape s;
+        if (!conv_shape(x, dw, dy, stride, padding, "conv2d_wgrad_noalloc", s) &&
+            resolve_mode(mode) != MT_STRICT_FP32 && s.N * s.Ho * s.Wo > 0)
+            need = wgrad_plan(s, dev_info().sms).ws_bytes;
+    }
     if (need > kNoAllocScratchBytes)
         return fail(MT_EINVAL,
                     "conv2d_wgrad_noalloc: this problem needs %zu bytes of split-K partials; the static scratch "
@@ -910,7 +1182,7 @@ MT_API int mt_conv2d_wgrad_noalloc(const mt_tensor* dy, const mt_tensor* x, cons
     // Every split writes its whole partial tile (zeros for an empty split), so nothing
     // left in the array by an earlier call is read.
     return conv_wgrad(dy, x, dw, stride, padding, mode, scratch, kNoAllocScratchBytes,
-                      static_cast<cudaStream_t>(stream), "conv2d_wgrad_noalloc");
+                      static_cast<cudaStream_t>(stream), "conv2d_wgrad_noalloc", /*allow_tma=*/false);
 }
 
 MT_API size_t mt_conv2d_wgrad_workspace_bytes(const mt_tensor* dy, const mt_tensor* x, const mt_tensor* dw,
@@ -920,7 +1192,8 @@ MT_API size_t mt_conv2d_wgrad_workspace_bytes(const mt_tensor* dy, const mt_tens
     ConvShape s;
     if (conv_shape(x, dw, dy, stride, padding, "wgrad_ws", s)) return 0;
     if (resolve_mode(mode) == MT_STRICT_FP32 || s.N * s.Ho * s.Wo == 0) return 0;
-    return wgrad_plan(s, dev_info().sms).ws_bytes;
+    const WgradTmaPlan tp = wgrad_tma_plan(s, dy, dev_info().sms);
+    return tp.ok ? tp.bytes : wgrad_plan(s, dev_info().sms).ws_bytes;
 }
 
 
