@@ -30,20 +30,23 @@ namespace convt {
 // One block per (32 channels x 32 columns) tile of one image row: coalesced reads along W,
 // coalesced writes along C. Channels in [C, Cp) are written as zeros.
 __global__ void nchw_to_nhwc_kernel(const float* __restrict__ x, int64_t s0, int64_t s1, int64_t s2, int64_t s3,
-                                    float* __restrict__ xt, int C, int H, int W, int Cp) {
+                                    float* __restrict__ xt, int N, int C, int H, int W, int Cp) {
     __shared__ float tile[32][33];
     const int w0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
-    const int nh = blockIdx.z, n = nh / H, h = nh - n * H;
     const int tx = threadIdx.x, ty = threadIdx.y;   // 32 x 8
-    for (int i = ty; i < 32; i += 8) {
-        const int c = c0 + i, w = w0 + tx;
-        tile[i][tx] = (c < C && w < W) ? __ldg(x + n * s0 + c * s1 + h * s2 + w * s3) : 0.f;
-    }
-    __syncthreads();
-    float* row = xt + (((int64_t)n * H + h) * W) * Cp;
-    for (int i = ty; i < 32; i += 8) {
-        const int w = w0 + i, c = c0 + tx;
-        if (w < W && c < Cp) row[(int64_t)w * Cp + c] = tile[tx][i];
+    for (int nh = blockIdx.z; nh < N * H; nh += gridDim.z) {
+        const int n = nh / H, h = nh - n * H;
+        for (int i = ty; i < 32; i += 8) {
+            const int c = c0 + i, w = w0 + tx;
+            tile[i][tx] = (c < C && w < W) ? __ldg(x + n * s0 + c * s1 + h * s2 + w * s3) : 0.f;
+        }
+        __syncthreads();
+        float* row = xt + (((int64_t)n * H + h) * W) * Cp;
+        for (int i = ty; i < 32; i += 8) {
+            const int w = w0 + i, c = c0 + tx;
+            if (w < W && c < Cp) row[(int64_t)w * Cp + c] = tile[tx][i];
+        }
+        __syncthreads();
     }
 }
 

@@ -543,8 +543,9 @@ int launch_simple(cudaError_t e, const char* what) {
 // NCHW view -> NHWC copy with Cp = round_up(C, 4) channels.
 int to_nhwc(const float* src, const int64_t (&sv)[4], float* dst, int N, int C, int H, int W, cudaStream_t st) {
     const int Cp = (C + 3) & ~3;
-    dim3 grid((W + 31) / 32, (Cp + 31) / 32, (unsigned)(N * H));
-    mt::convt::nchw_to_nhwc_kernel<<<grid, dim3(32, 8), 0, st>>>(src, sv[0], sv[1], sv[2], sv[3], dst, C, H, W, Cp);
+    if ((W + 31) / 32 > 65535 || (Cp + 31) / 32 > 65535) return fail(MT_EUNSUPPORTED, "nchw_to_nhwc: extent");
+    dim3 grid((W + 31) / 32, (Cp + 31) / 32, (unsigned)std::min(N * H, 65535));
+    mt::convt::nchw_to_nhwc_kernel<<<grid, dim3(32, 8), 0, st>>>(src, sv[0], sv[1], sv[2], sv[3], dst, N, C, H, W, Cp);
     return launch_simple(cudaGetLastError(), "nchw_to_nhwc");
 }
 
