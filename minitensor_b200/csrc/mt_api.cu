@@ -14,6 +14,7 @@
 #include "mt_common.cuh"
 #include "simt_gemm.cuh"
 #include "umma_gemm.cuh"
+#include "umma_gemm2.cuh"
 #include "conv_gemm.cuh"
 #include "conv_tma.cuh"
 
@@ -218,6 +219,55 @@ int launch_umma_inst(const CUtensorMap& ta, const CUtensorMap& tb, const mt::umm
     return MT_OK;
 }
 
+// CTA-pair kernel: grid = 2 x (clusters that fit at once, capped by the tile count).
+template <int BN, int BKE, bool AMN, bool BMN, bool X3, int STAGES>
+int launch_pair_inst(const CUtensorMap& ta, const CUtensorMap& tb, const mt::umma::Params& up, int sms,
+                     cudaStream_t st) {
+    using G = mt::umma2::Cfg<BN, BKE, X3, STAGES>;
+    auto kern = mt::umma2::gemm_pair_kernel<BN, BKE, AMN, BMN, X3, STAGES>;
+    static std::atomic<uint64_t> attr_set_mask{0};
+    static std::atomic<int> max_clusters[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(attr_set_mask.load() & bit)) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)G::SMEM_BYTES);
+        if (e != cudaSuccess) return cuda_fail(e, "umma pair gemm: set smem attribute");
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * (sms / 2), 1, 1);
+        cfg.blockDim = dim3(G::THREADS, 1, 1);
+        cfg.dynamicSmemBytes = G::SMEM_BYTES;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2; attr[0].val.clusterDim.y = 1; attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            n = sms / 2;
+        }
+        max_clusters[dev & 63].store(std::min(n, sms / 2));
+        attr_set_mask.fetch_or(bit);
+    }
+    const int clusters = (int)std::min<long long>(up.num_units, (long long)max_clusters[dev & 63].load());
+    kern<<<2 * clusters, G::THREADS, G::SMEM_BYTES, st>>>(ta, tb, up);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess && e != cudaErrorStreamCaptureUnsupported) return cuda_fail(e, "umma pair gemm launch");
+    g_launches.fetch_add(1);
+    return MT_OK;
+}
+
+// The pair kernel serves outputs with at least one 256 x 256 tile per SM pair; the
+// environment variable MT_GEMM_PAIR=0 turns it off (the 128-row kernel then runs).
+bool pair_enabled() {
+    static int v = [] {
+        const char* e = std::getenv("MT_GEMM_PAIR");
+        return (e && e[0] == '0') ? 0 : 1;
+    }();
+    return v != 0;
+}
+
 // Returns MT_OK when launched, MT_EUNSUPPORTED when the views do not fit the tensor-core
 // kernel (the caller then uses the SIMT kernel).
 int launch_umma(const GemmProblem& p, bool x3, cudaStream_t st, float* const* extra_dst = nullptr, int nextra = 0) {
@@ -244,9 +294,14 @@ int launch_umma(const GemmProblem& p, bool x3, cudaStream_t st, float* const* ex
     const uint32_t bke = x3 ? 16 : 32;        // k elements per stage
     const int kswz = (int)bke * 4;             // K-major swizzle span (bytes)
     const uint32_t chunk = 32;                 // MN-major box width (elements)
-    const int64_t tiles_m = (p.M + 127) / 128;
-    const bool small = tiles_m * ((p.N + 255) / 256) * p.batch < (int64_t)di.sms || p.N <= 128;
+    const int64_t tiles_m1 = (p.M + 127) / 128;
+    const bool small = tiles_m1 * ((p.N + 255) / 256) * p.batch < (int64_t)di.sms || p.N <= 128;
     const int bn = small ? 128 : 256;
+    // CTA pairs: 256 x 256 tiles, at least one per pair of SMs.
+    const bool pair = pair_enabled() && !small && p.M > 128 &&
+                      ((p.M + 255) / 256) * ((p.N + 255) / 256) * p.batch >= (int64_t)(di.sms / 2);
+    const int64_t tiles_m = pair ? (p.M + 255) / 256 : tiles_m1;
+    const uint32_t b_rows = pair ? (uint32_t)bn / 2 : (uint32_t)bn;   // B tile rows one CTA loads
 
     // Sizes of unit dims get a harmless 16-byte stride.
     auto st_or = [](int64_t extent, int64_t stride_elems, uint64_t fallback_bytes) -> uint64_t {
@@ -267,7 +322,7 @@ int launch_umma(const GemmProblem& p, bool x3, cudaStream_t st, float* const* ex
     if (b_mn == 0) {   // dims {K, N, batch}
         uint64_t s1 = st_or(p.N, p.sb_n, round16(p.K * 4));
         uint64_t s2 = b_batched ? (uint64_t)p.sb_b * 4 : round16(s1 * p.N);
-        ok = encode_3d(&tb, p.B, p.K, p.N, b_batched ? p.batch : 1, s1, s2, bke, bn, kswz);
+        ok = encode_3d(&tb, p.B, p.K, p.N, b_batched ? p.batch : 1, s1, s2, bke, b_rows, kswz);
     } else {           // dims {N, K, batch}
         uint64_t s1 = st_or(p.K, p.sb_k, round16(p.N * 4));
         uint64_t s2 = b_batched ? (uint64_t)p.sb_b * 4 : round16(s1 * p.K);
@@ -297,7 +352,7 @@ int launch_umma(const GemmProblem& p, bool x3, cudaStream_t st, float* const* ex
     // workspace, then one pass that sums them in split order and applies the epilogue.
     const int kblocks = (int)((p.K + bke - 1) / bke);
     int splits = 1;
-    if (p.batch == 1 && nextra == 0 && up.num_tiles * 2 <= di.sms && kblocks >= 8)
+    if (!pair && p.batch == 1 && nextra == 0 && up.num_tiles * 2 <= di.sms && kblocks >= 8)
         splits = (int)std::max<long long>(
             1, std::min<long long>(std::min<long long>(di.sms / up.num_tiles, kblocks / 4), 16));
     up.splits = splits;
@@ -323,7 +378,15 @@ int launch_umma(const GemmProblem& p, bool x3, cudaStream_t st, float* const* ex
     else if (a_mn == 0 && b_mn == 1) rc = launch_umma_inst<BN_, BKE_, false, true, X3_, ST_>(ta, tb, up, grid, st); \
     else if (a_mn == 1 && b_mn == 0) rc = launch_umma_inst<BN_, BKE_, true, false, X3_, ST_>(ta, tb, up, grid, st); \
     else rc = launch_umma_inst<BN_, BKE_, true, true, X3_, ST_>(ta, tb, up, grid, st);
-    if (!x3) {
+#define MT_PAIR_DISPATCH(BKE_, X3_, ST_)                                                                   \
+    if (a_mn == 0 && b_mn == 0) rc = launch_pair_inst<256, BKE_, false, false, X3_, ST_>(ta, tb, up, di.sms, st); \
+    else if (a_mn == 0 && b_mn == 1) rc = launch_pair_inst<256, BKE_, false, true, X3_, ST_>(ta, tb, up, di.sms, st); \
+    else if (a_mn == 1 && b_mn == 0) rc = launch_pair_inst<256, BKE_, true, false, X3_, ST_>(ta, tb, up, di.sms, st); \
+    else rc = launch_pair_inst<256, BKE_, true, true, X3_, ST_>(ta, tb, up, di.sms, st);
+    if (pair) {
+        if (!x3) { MT_PAIR_DISPATCH(32, false, 6) }
+        else { MT_PAIR_DISPATCH(16, true, 6) }
+    } else if (!x3) {
         if (bn == 256) { MT_UMMA_DISPATCH(256, 32, false, 4) }
         else { MT_UMMA_DISPATCH(128, 32, false, 6) }
     } else {
@@ -331,6 +394,7 @@ int launch_umma(const GemmProblem& p, bool x3, cudaStream_t st, float* const* ex
         else { MT_UMMA_DISPATCH(128, 16, true, 6) }
     }
 #undef MT_UMMA_DISPATCH
+#undef MT_PAIR_DISPATCH
     if (splits > 1) {
         if (rc == MT_OK) {
             const int blocks = (int)std::min<int64_t>((p.M * p.N + 255) / 256, 8 * di.sms);
@@ -344,8 +408,9 @@ int launch_umma(const GemmProblem& p, bool x3, cudaStream_t st, float* const* ex
     }
     if (rc == MT_OK) {
         char buf[112];
-        snprintf(buf, sizeof buf, "umma_%s bn=%d a=%s b=%s%s", x3 ? "tf32x3" : "tf32", bn, a_mn ? "MN" : "K",
-                 b_mn ? "MN" : "K", splits > 1 ? (" splitk=" + std::to_string(splits)).c_str() : "");
+        snprintf(buf, sizeof buf, "umma%s_%s bn=%d a=%s b=%s%s", pair ? "_pair" : "", x3 ? "tf32x3" : "tf32", bn,
+                 a_mn ? "MN" : "K", b_mn ? "MN" : "K",
+                 splits > 1 ? (" splitk=" + std::to_string(splits)).c_str() : "");
         t_path = buf;
     }
     return rc;

@@ -226,3 +226,51 @@ def test_column_major_output(eng, port):
 
 def test_device_status_clean(eng):
     assert eng.device_status(reset=True) == 0
+
+
+# ------------------------------------------------------- CTA-pair (256-row) kernel ---
+
+@pytest.mark.parametrize("mode", ["tf32", "tf32x3"])
+@pytest.mark.parametrize("layout", ["NN", "NT", "TN", "TT"])
+def test_pair_kernel_ragged_layouts(eng, port, mode, layout):
+    """Outputs with >= 74 tiles of 256 x 256 run on CTA pairs (M = 256 per MMA, B split
+    across the two SMs). Ragged M, N and K so that the odd CTA's rows, the second B half
+    and the k tail all meet the zero-filled edge; checked on sampled rows (both halves
+    of a pair tile) and sampled columns (both B halves) against the oracle."""
+    M, N, K = 2381, 2355, 301
+    a_np, a_t = padded((K, M) if layout[0] == "T" else (M, K), 91)
+    b_np, b_t = padded((N, K) if layout[1] == "T" else (K, N), 92)
+    A = a_t.t() if layout[0] == "T" else a_t
+    B = b_t.t() if layout[1] == "T" else b_t
+    An = np.ascontiguousarray(a_np.T if layout[0] == "T" else a_np)
+    Bn = np.ascontiguousarray(b_np.T if layout[1] == "T" else b_np)
+    bn = inputs.uniform((N,), -1, 1, 93)
+    C = torch.empty(M, N, device="cuda")
+    eng.gemm(A, B, C, bias=dev(bn), epi=eng.EPI_BIAS_COL | eng.EPI_RELU, mode=mode)
+    assert eng.last_path().startswith("umma_pair_" + mode), eng.last_path()
+    Ch = host(C)
+    rows = [0, 1, 127, 128, 129, 255, 256, 383, 384, 2303, 2304, M - 2, M - 1]
+    cols = [0, 1, 127, 128, 129, 255, 256, 1151, 1152, 2303, 2304, N - 2, N - 1]
+    R = port.matmul_strided(An[rows], Bn)
+    check(mode, Ch[rows], np.maximum(R + bn, 0), absmm(An[rows], Bn) + np.abs(bn), K, f"pair {layout} rows")
+    Cc = port.matmul_strided(An, np.ascontiguousarray(Bn[:, cols]))
+    check(mode, Ch[:, cols], np.maximum(Cc + bn[cols], 0), absmm(An, Bn[:, cols]) + np.abs(bn[cols]), K,
+          f"pair {layout} cols")
+
+
+@pytest.mark.parametrize("mode", ["tf32", "tf32x3"])
+def test_pair_kernel_batched_bias_row(eng, port, mode):
+    """Batched pair tiles (tile index walks batch, m, n) with a per-row bias."""
+    Bt, M, N, K = 3, 1290, 1100, 200
+    A = inputs.uniform((Bt, M, K), -1, 1, 95)
+    B = inputs.uniform((Bt, K, N), -1, 1, 96)
+    bm = inputs.uniform((M,), -1, 1, 97)
+    C = torch.empty(Bt, M, N, device="cuda")
+    eng.gemm(dev(A), dev(B), C, bias=dev(bm), epi=eng.EPI_BIAS_ROW, mode=mode)
+    assert eng.last_path().startswith("umma_pair_" + mode), eng.last_path()
+    Ch = host(C)
+    rows = [0, 127, 128, 255, 256, 1023, 1024, 1279, 1280, M - 1]
+    for b in range(Bt):
+        R = port.matmul_strided(A[b][rows], B[b])
+        check(mode, Ch[b][rows], R + bm[rows][:, None], absmm(A[b][rows], B[b]) + np.abs(bm[rows])[:, None], K,
+              f"pair batch {b}")
