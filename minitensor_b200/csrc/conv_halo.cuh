@@ -1,0 +1,308 @@
+// conv_halo.cuh -- stride-1 Conv2D forward (and input-grad, which is the same kernel on
+// dy with flipped, transposed weights) with ONE activation load per 32-channel block
+// serving every filter tap, and weight stages that carry several taps each.
+//
+// Pitched halo tile. For an output tile of TY rows x TXv columns, TMA loads the input
+// window it needs -- HR = TY + kh - 1 rows of P = TXv + kw - 1 pixels, 32 channels each
+// (NHWC, 128 bytes per pixel) -- into shared memory as P*HR consecutive 128-byte rows,
+// zero-filling the padding. Number the MMA's 128 M rows by the pitched position
+// p = ty * P + tx. The input pixel that tap (r, s) contributes to output p is halo row
+// p + r * P + s, so the A operand of every tap is the same buffer read from start row
+// o = r * P + s: 128 consecutive rows, a plain K-major SW128 operand whose descriptor
+// start moves by o * 128 bytes (the swizzle phase follows the address; see halo_desc).
+// Positions with tx >= TXv are computed and discarded; a valid position never reads
+// past the rows TMA wrote.
+//
+// Weights are read by every CTA for every tile; all CTAs start together, and reading one
+// copy they queue on the same L2 lines. The reorder kernel writes `copies` identical
+// copies and CTA b reads copy b % copies.
+//
+// Few, large pipeline stages. Each handoff between roles costs a few hundred cycles (an
+// mbarrier wait, an expect-tx, a TMA issue), which is more than the MMA time of one tap
+// of a 32-channel block at N = 64 (4 k-steps of 32 cycles). So a weight stage is ONE TMA
+// box holding G taps ({32 channels, BN, G}, or {32, BN, 2 (hi/lo), G} for TF32X3 with
+// the weights split into hi and lo in global memory by reorder_weights_kernel), and an
+// activation halo is one box per 32-channel block: the MMA issuer then waits once per
+// G * 4 (* 3) MMAs instead of once per 4.
+//
+// Warp roles: 0 weight (B) producer, 1 MMA issuer + TMEM owner, 2-5 epilogue, 6 halo (A)
+// producer, 7-10 (TF32X3) hi/lo splitter of the halos.
+#pragma once
+
+#include "conv_tma.cuh"
+
+namespace mt {
+namespace convh {
+
+constexpr int kMaxASlots = 2;
+constexpr int kMaxBStages = 8;
+
+struct HaloParams {
+    int N, Ho, Wo, Ncol, C, kh, kw, pad;  // Ncol = output channels, C = input channels
+    int P, TXv, TY, HR;                   // pitch, valid columns, output rows, halo rows
+    int tiles_y, tiles_x, tiles_n, cblocks, taps;
+    int G, tgroups;                       // taps per weight stage, stages per channel block
+    int copies;                           // identical weight copies; CTA b reads copy b % copies
+    long long num_tiles;
+    int a_slots, b_stages;
+    uint32_t halo_bytes;                  // bytes TMA writes per halo (P * HR * 128)
+    uint32_t slot_bytes;                  // shared bytes per halo slot (multiple of 1024)
+    uint32_t b_bytes;                     // bytes per weight stage (G * (1 or 2) * BN * 128)
+    uint32_t a_off, alo_off, b_off, bar_off;   // offsets from the 1024-aligned base
+    float* out;                           // [N, Ncol, Ho, Wo] contiguous
+    const float* bias;                    // [Ncol] or null
+};
+
+// Tile t -> (image, first output row, first output column, C_out block); C_out block
+// fastest so CTAs running the same pixels at once share halo reads in L2.
+__device__ __forceinline__ void halo_tile(const HaloParams& p, long long t, int& n, int& y0, int& x0, int& nt) {
+    long long r = t;
+    nt = (int)(r % p.tiles_n); r /= p.tiles_n;
+    const int xt = (int)(r % p.tiles_x); r /= p.tiles_x;
+    const int yt = (int)(r % p.tiles_y); r /= p.tiles_y;
+    n = (int)r;
+    y0 = yt * p.TY;
+    x0 = xt * p.TXv;
+}
+
+// K-major SW128 operand descriptor whose start may sit at any 128-byte row of a
+// 1024-aligned swizzled buffer. The base-offset field stays 0: the MMA takes the XOR
+// phase of each 128-byte row from the row's shared-memory address (address bits 7-9),
+// the same rule TMA used when it wrote the rows, so a moved start needs no correction
+// (checked against the oracle by the conv parity tests, where a wrong phase reads the
+// zero-filled channel chunks and loses every tap but the first).
+__device__ __forceinline__ uint64_t halo_desc(uint32_t start) {
+    return umma_desc(start, 16, 1024, kLayoutSw128);
+}
+
+template <bool X3>
+struct HaloCfg {
+    static constexpr int NUM_WARPS = X3 ? 11 : 7;
+    static constexpr int THREADS = NUM_WARPS * 32;
+};
+
+// Split `bytes` of shared memory at `hi` into hi (in place) and lo, 128 threads.
+__device__ __forceinline__ void split_block(uint8_t* hi_p, uint8_t* lo_p, uint32_t bytes, int ct) {
+    float4* hi = reinterpret_cast<float4*>(hi_p);
+    float4* lo = reinterpret_cast<float4*>(lo_p);
+#pragma unroll 4
+    for (uint32_t i = ct; i < bytes / 16; i += 128) {
+        const float4 x = hi[i];
+        const float4 h = make_float4(tf32_round(x.x), tf32_round(x.y), tf32_round(x.z), tf32_round(x.w));
+        hi[i] = h;
+        lo[i] = make_float4(x.x - h.x, x.y - h.y, x.z - h.z, x.w - h.w);
+    }
+}
+
+template <int BN, bool X3>
+__global__ void __launch_bounds__(HaloCfg<X3>::THREADS, 1)
+conv_fwd_halo_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const HaloParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* a_ring = smem + p.a_off;
+    uint8_t* alo_ring = smem + p.alo_off;
+    uint8_t* b_ring = smem + p.b_off;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.bar_off);
+    uint64_t* a_full = bars;                          // [kMaxASlots]
+    uint64_t* a_empty = a_full + kMaxASlots;
+    uint64_t* a_conv = a_empty + kMaxASlots;
+    uint64_t* b_full = a_conv + kMaxASlots;           // [kMaxBStages]
+    uint64_t* b_empty = b_full + kMaxBStages;
+    uint64_t* acc_full = b_empty + kMaxBStages;       // [2]
+    uint64_t* acc_empty = acc_full + 2;               // [2]
+    volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(acc_empty + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(acc_empty + 2) + 1;
+    constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+    constexpr uint32_t BMAT = BN * 128;               // one tap's weight matrix (hi or lo)
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long first = blockIdx.x, step = gridDim.x;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kMaxASlots; ++i) {
+            mbar_init(smem_u32(&a_full[i]), 1);
+            mbar_init(smem_u32(&a_empty[i]), 1);
+            mbar_init(smem_u32(&a_conv[i]), 128);
+        }
+        for (int i = 0; i < kMaxBStages; ++i) {
+            mbar_init(smem_u32(&b_full[i]), 1);
+            mbar_init(smem_u32(&b_empty[i]), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(smem_u32(&acc_full[a]), 1);
+            mbar_init(smem_u32(&acc_empty[a]), 4);   // one arrival per epilogue warp
+        }
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32((const void*)tmem_slot), TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------ weight producer -----------------------------
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            for (long long t = first; t < p.num_tiles; t += step) {
+                int n, y0, x0, nt;
+                halo_tile(p, t, n, y0, x0, nt);
+                for (int cb = 0; cb < p.cblocks; ++cb)
+                    for (int g = 0; g < p.tgroups; ++g) {
+                        if (!mbar_wait(smem_u32(&b_empty[s]), ph ^ 1, abort_flag, kDevTimeoutEmpty)) goto done;
+                        const uint32_t bar = smem_u32(&b_full[s]);
+                        mbar_arrive_expect_tx(bar, p.b_bytes);
+                        const uint32_t dst = smem_u32(b_ring + s * p.b_bytes);
+                        const int tap0 = (int)(blockIdx.x % p.copies) * p.taps + g * p.G;
+                        if (X3) tma_load_4d(dst, &tmB, bar, cb * 32, nt * BN, 0, tap0);
+                        else tma_load_4d(dst, &tmB, bar, cb * 32, nt * BN, tap0, 0);
+                        if (++s == p.b_stages) { s = 0; ph ^= 1; }
+                    }
+            }
+        }
+    } else if (warp == 6) {
+        // ------------------------------ halo producer -------------------------------
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            for (long long t = first; t < p.num_tiles; t += step) {
+                int n, y0, x0, nt;
+                halo_tile(p, t, n, y0, x0, nt);
+                for (int cb = 0; cb < p.cblocks; ++cb) {
+                    if (!mbar_wait(smem_u32(&a_empty[s]), ph ^ 1, abort_flag, kDevTimeoutEmpty)) goto done;
+                    const uint32_t bar = smem_u32(&a_full[s]);
+                    mbar_arrive_expect_tx(bar, p.halo_bytes);
+                    tma_load_4d(smem_u32(a_ring + s * p.slot_bytes), &tmA, bar, cb * 32, x0 - p.pad, y0 - p.pad, n);
+                    if (++s == p.a_slots) { s = 0; ph ^= 1; }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------ MMA issuer ----------------------------------
+        if (lane == 0) {
+            constexpr uint32_t idesc = umma_idesc_tf32(128, BN, 0, 0);
+            int as = 0, bs = 0, it = 0;
+            uint32_t aph = 0, bph = 0;
+            for (long long t = first; t < p.num_tiles; t += step, ++it) {
+                const int acc_i = it & 1;
+                if (!mbar_wait(smem_u32(&acc_empty[acc_i]), ((it >> 1) & 1) ^ 1, abort_flag, kDevTimeoutAccEmpty))
+                    goto done;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc_i * BN;
+                bool first_mma = true;
+                for (int cb = 0; cb < p.cblocks; ++cb) {
+                    const uint32_t abar = X3 ? smem_u32(&a_conv[as]) : smem_u32(&a_full[as]);
+                    if (!mbar_wait(abar, aph, abort_flag, kDevTimeoutFull)) goto done;
+                    tc_fence_after();
+                    const uint32_t a_base = smem_u32(a_ring + as * p.slot_bytes);
+                    const uint32_t alo_base = smem_u32(alo_ring + as * p.slot_bytes);
+                    for (int g = 0; g < p.tgroups; ++g) {
+                        if (!mbar_wait(smem_u32(&b_full[bs]), bph, abort_flag, kDevTimeoutFull)) goto done;
+                        tc_fence_after();
+                        const uint32_t sbase = smem_u32(b_ring + bs * p.b_bytes);
+                        for (int gi = 0; gi < p.G; ++gi) {
+                            const int tap = g * p.G + gi;
+                            const int r = tap / p.kw, sx = tap - r * p.kw;
+                            const uint32_t o = (uint32_t)(r * p.P + sx) * 128u;
+                            const uint32_t sb = sbase + (X3 ? 2u * gi : (uint32_t)gi) * BMAT;
+#pragma unroll
+                            for (int k = 0; k < 4; ++k) {
+                                const uint64_t ad = halo_desc(a_base + o + k * 32);
+                                const uint64_t bd = umma_desc(sb + k * 32, 16, 1024, kLayoutSw128);
+                                const uint32_t acc = (!first_mma || k > 0) ? 1u : 0u;
+                                if (X3) {
+                                    const uint64_t ald = halo_desc(alo_base + o + k * 32);
+                                    const uint64_t bld = umma_desc(sb + BMAT + k * 32, 16, 1024, kLayoutSw128);
+                                    umma_tf32(d_tmem, ald, bd, idesc, acc);
+                                    umma_tf32(d_tmem, ad, bld, idesc, 1u);
+                                    umma_tf32(d_tmem, ad, bd, idesc, 1u);
+                                } else {
+                                    umma_tf32(d_tmem, ad, bd, idesc, acc);
+                                }
+                            }
+                            first_mma = false;
+                        }
+                        umma_commit(smem_u32(&b_empty[bs]));
+                        if (++bs == p.b_stages) { bs = 0; bph ^= 1; }
+                    }
+                    umma_commit(smem_u32(&a_empty[as]));
+                    if (++as == p.a_slots) { as = 0; aph ^= 1; }
+                }
+                umma_commit(smem_u32(&acc_full[acc_i]));
+            }
+        }
+    } else if (warp < 6) {
+        // ------------------------------ epilogue ------------------------------------
+        const int q = warp & 3;
+        const int HoWo = p.Ho * p.Wo;
+        int it = 0;
+        for (long long t = first; t < p.num_tiles; t += step, ++it) {
+            int n, y0, x0, nt;
+            halo_tile(p, t, n, y0, x0, nt);
+            const int acc_i = it & 1;
+            if (!mbar_wait_warp(smem_u32(&acc_full[acc_i]), (it >> 1) & 1, abort_flag, kDevTimeoutAccFull)) goto done;
+            tc_fence_after();
+            const int l = q * 32 + lane;             // TMEM lane = pitched position
+            const int ty = l / p.P, tx = l - ty * p.P;
+            const int oy = y0 + ty, ox = x0 + tx;
+            const bool valid = ty < p.TY && tx < p.TXv && oy < p.Ho && ox < p.Wo;
+            float* obase = p.out + (int64_t)n * p.Ncol * HoWo + (int64_t)oy * p.Wo + ox;
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t rr[32];
+                tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + acc_i * BN + c * 32, rr);
+                tmem_ld_wait();
+                if (c == BN / 32 - 1) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(smem_u32(&acc_empty[acc_i]));
+                }
+                if (valid) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int co = nt * BN + c * 32 + j;
+                        if (co < p.Ncol) {
+                            float v = __uint_as_float(rr[j]);
+                            if (p.bias) v = v + __ldg(p.bias + co);
+                            obase[(int64_t)co * HoWo] = v;
+                        }
+                    }
+                }
+            }
+        }
+    } else if (X3) {
+        // ------------------------------ halo hi/lo splitter -------------------------
+        const int ct = threadIdx.x - 7 * 32;
+        int as = 0;
+        uint32_t aph = 0;
+        for (long long t = first; t < p.num_tiles; t += step)
+            for (int cb = 0; cb < p.cblocks; ++cb) {
+                if (!mbar_wait_warp(smem_u32(&a_full[as]), aph, abort_flag, kDevTimeoutMisc)) goto done;
+                split_block(a_ring + as * p.slot_bytes, alo_ring + as * p.slot_bytes, p.slot_bytes, ct);
+                fence_proxy_async_smem();
+                mbar_arrive(smem_u32(&a_conv[as]));
+                if (++as == p.a_slots) { as = 0; aph ^= 1; }
+            }
+    }
+done:
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+}  // namespace convh
+}  // namespace mt

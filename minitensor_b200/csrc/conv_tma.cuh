@@ -27,24 +27,34 @@ namespace mt {
 namespace convt {
 
 // ------------------------------------------------------------------ layout kernels --
-// One block per (32 channels x 32 columns) tile of one image row: coalesced reads along W,
-// coalesced writes along C. Channels in [C, Cp) are written as zeros.
-__global__ void nchw_to_nhwc_kernel(const float* __restrict__ x, int64_t s0, int64_t s1, int64_t s2, int64_t s3,
-                                    float* __restrict__ xt, int N, int C, int H, int W, int Cp) {
-    __shared__ float tile[32][33];
-    const int w0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
-    const int tx = threadIdx.x, ty = threadIdx.y;   // 32 x 8
+// One block per (64 channels x 64 columns) tile of one image row: each thread keeps 16
+// loads in flight (coalesced along W), then 16 stores (coalesced along C) from a padded
+// shared tile. Channels in [C, Cp) are written as zeros. Grid: x = column tiles,
+// y = channel tiles, z strides over the N*H rows.
+__global__ void __launch_bounds__(256) nchw_to_nhwc_kernel(const float* __restrict__ x, int64_t s0, int64_t s1,
+                                                           int64_t s2, int64_t s3, float* __restrict__ xt, int N,
+                                                           int C, int H, int W, int Cp) {
+    __shared__ float tile[64][65];
+    const int w0 = blockIdx.x * 64, c0 = blockIdx.y * 64;
+    const int t = threadIdx.x;
+    const int lo = t & 63, hi = t >> 6;   // 64 x 4
     for (int nh = blockIdx.z; nh < N * H; nh += gridDim.z) {
         const int n = nh / H, h = nh - n * H;
-        for (int i = ty; i < 32; i += 8) {
-            const int c = c0 + i, w = w0 + tx;
-            tile[i][tx] = (c < C && w < W) ? __ldg(x + n * s0 + c * s1 + h * s2 + w * s3) : 0.f;
+        const float* src = x + (int64_t)n * s0 + (int64_t)h * s2;
+        float v[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int c = c0 + hi + 4 * i, w = w0 + lo;
+            v[i] = (c < C && w < W) ? __ldg(src + (int64_t)c * s1 + (int64_t)w * s3) : 0.f;
         }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) tile[hi + 4 * i][lo] = v[i];
         __syncthreads();
-        float* row = xt + (((int64_t)n * H + h) * W) * Cp;
-        for (int i = ty; i < 32; i += 8) {
-            const int w = w0 + i, c = c0 + tx;
-            if (w < W && c < Cp) row[(int64_t)w * Cp + c] = tile[tx][i];
+        float* row = xt + ((int64_t)n * H + h) * W * Cp;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int w = w0 + hi + 4 * i, c = c0 + lo;
+            if (w < W && c < Cp) row[(int64_t)w * Cp + c] = tile[lo][hi + 4 * i];
         }
         __syncthreads();
     }
@@ -53,8 +63,14 @@ __global__ void nchw_to_nhwc_kernel(const float* __restrict__ x, int64_t s0, int
 // Wt[tap][row][col] (col padded to colsp with zeros), tap = r * kw + s:
 //   forward:    row = co, col = ci, value W[co, ci, r, s]
 //   input-grad: row = ci, col = co, value W[co, ci, kh-1-r, kw-1-s] (flipped, transposed)
+// split != 0 writes the TF32X3 pair instead, Wt[tap][h][row][col] with h = 0 the tf32
+// rounding hi = rna_tf32(v) and h = 1 the remainder lo = v - hi, so that one TMA box
+// brings both halves of a weight tile and no kernel has to split weights again.
+// copies > 1 writes that many identical copies back to back (see the halo kernel: CTAs
+// read different copies so that they do not all queue on the same L2 lines).
 __global__ void reorder_weights_kernel(const float* __restrict__ w, int64_t s0, int64_t s1, int64_t s2, int64_t s3,
-                                       float* __restrict__ wt, int Co, int C, int kh, int kw, int dgrad) {
+                                       float* __restrict__ wt, int Co, int C, int kh, int kw, int dgrad, int split,
+                                       int copies) {
     const int rows = dgrad ? C : Co, cols = dgrad ? Co : C;
     const int colsp = (cols + 3) & ~3;
     const int64_t total = (int64_t)kh * kw * rows * colsp;
@@ -69,7 +85,19 @@ __global__ void reorder_weights_kernel(const float* __restrict__ w, int64_t s0, 
             v = dgrad ? __ldg(w + col * s0 + row * s1 + (kh - 1 - r) * s2 + (kw - 1 - s) * s3)
                       : __ldg(w + row * s0 + col * s1 + r * s2 + s * s3);
         }
-        wt[i] = v;
+        const int64_t copy_stride = total * (split ? 2 : 1);
+        for (int c = 0; c < copies; ++c) {
+            float* dst = wt + c * copy_stride;
+            if (split) {
+                const int64_t plane = (int64_t)rows * colsp;
+                const int64_t o = (int64_t)tap * 2 * plane + (int64_t)row * colsp + col;
+                const float hi = tf32_round(v);
+                dst[o] = hi;
+                dst[o + plane] = v - hi;
+            } else {
+                dst[i] = v;
+            }
+        }
     }
 }
 

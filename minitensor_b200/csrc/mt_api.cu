@@ -17,6 +17,7 @@
 #include "umma_gemm2.cuh"
 #include "conv_gemm.cuh"
 #include "conv_tma.cuh"
+#include "conv_halo.cuh"
 
 namespace {
 
@@ -608,19 +609,19 @@ int launch_simple(cudaError_t e, const char* what) {
 // NCHW view -> NHWC copy with Cp = round_up(C, 4) channels.
 int to_nhwc(const float* src, const int64_t (&sv)[4], float* dst, int N, int C, int H, int W, cudaStream_t st) {
     const int Cp = (C + 3) & ~3;
-    if ((W + 31) / 32 > 65535 || (Cp + 31) / 32 > 65535) return fail(MT_EUNSUPPORTED, "nchw_to_nhwc: extent");
-    dim3 grid((W + 31) / 32, (Cp + 31) / 32, (unsigned)std::min(N * H, 65535));
-    mt::convt::nchw_to_nhwc_kernel<<<grid, dim3(32, 8), 0, st>>>(src, sv[0], sv[1], sv[2], sv[3], dst, N, C, H, W, Cp);
+    if ((W + 63) / 64 > 65535 || (Cp + 63) / 64 > 65535) return fail(MT_EUNSUPPORTED, "nchw_to_nhwc: extent");
+    dim3 grid((W + 63) / 64, (Cp + 63) / 64, (unsigned)std::min(N * H, 65535));
+    mt::convt::nchw_to_nhwc_kernel<<<grid, 256, 0, st>>>(src, sv[0], sv[1], sv[2], sv[3], dst, N, C, H, W, Cp);
     return launch_simple(cudaGetLastError(), "nchw_to_nhwc");
 }
 
 int reorder_w(const float* w, const int64_t (&sw)[4], float* wt, int Co, int C, int kh, int kw, bool dgrad,
-              cudaStream_t st) {
+              cudaStream_t st, bool split = false, int copies = 1) {
     const int rows = dgrad ? C : Co, cols = dgrad ? Co : C;
     const int64_t total = (int64_t)kh * kw * rows * ((cols + 3) & ~3);
     const int blocks = (int)std::min<int64_t>((total + 255) / 256, 1024);
     mt::convt::reorder_weights_kernel<<<blocks, 256, 0, st>>>(w, sw[0], sw[1], sw[2], sw[3], wt, Co, C, kh, kw,
-                                                              dgrad ? 1 : 0);
+                                                              dgrad ? 1 : 0, split ? 1 : 0, copies);
     return launch_simple(cudaGetLastError(), "reorder_weights");
 }
 
@@ -683,11 +684,143 @@ int launch_wgrad_tma(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const
     }
 }
 
+// ---- pitched-halo forward (one activation box per 32-channel block for all taps) ----
+constexpr uint32_t kHaloSmemMax = 227 * 1024;
+constexpr int kWeightCopies = 16;   // weight copies the halo kernel's CTAs spread over
+
+template <int BN, bool X3>
+int launch_halo_inst(const CUtensorMap& ta, const CUtensorMap& tb, const mt::convh::HaloParams& hp, uint32_t smem,
+                     int grid, cudaStream_t st) {
+    auto kern = mt::convh::conv_fwd_halo_kernel<BN, X3>;
+    static std::atomic<uint64_t> mask{0};
+    int rc = set_smem(kern, kHaloSmemMax, mask);
+    if (rc) return rc;
+    kern<<<grid, mt::convh::HaloCfg<X3>::THREADS, smem, st>>>(ta, tb, hp);
+    return launch_simple(cudaGetLastError(), "conv fwd halo");
+}
+
+// The halo kernel serves stride-1 forward-shaped convs whose halo ring fits in shared
+// memory; MT_CONV_HALO=0 turns it off (the per-tap TMA kernel then runs).
+bool halo_enabled() {
+    static int v = [] {
+        const char* e = std::getenv("MT_CONV_HALO");
+        return (e && e[0] == '0') ? 0 : 1;
+    }();
+    return v != 0;
+}
+
+// Fills the tile geometry and shared-memory layout; false when the halo does not fit.
+// The weight stage takes the largest G (a divisor of the tap count) for which two
+// stages fit beside two halo slots.
+bool plan_halo(int Ho, int Wo, int kh, int kw, int Ncol, bool x3, int& bn, mt::convh::HaloParams& hp,
+               uint32_t& smem) {
+    const int TXv = std::min(Wo, 128 - (kw - 1));
+    if (TXv < 1 || kh < 1 || kw < 1) return false;
+    const int P = TXv + kw - 1;                          // <= 128
+    const int TY = std::min(Ho, (128 - TXv) / P + 1);
+    const int HR = TY + kh - 1;
+    if (HR > 256) return false;
+    const int64_t rows = std::max<int64_t>((int64_t)P * HR, (int64_t)(kh - 1) * P + (kw - 1) + 128);
+    const int64_t nr = (rows + 7) / 8 * 8;
+    const uint64_t mult = x3 ? 2 : 1;
+    bn = std::min(pick_bn(Ncol), 128);
+    const int taps = kh * kw;
+    const uint64_t slot = (uint64_t)nr * 128, bmat = (uint64_t)bn * 128;
+    const uint32_t bars = 8u * (3 * mt::convh::kMaxASlots + 2 * mt::convh::kMaxBStages + 4) + 16u;
+    const uint64_t budget = kHaloSmemMax - 1024 - bars;
+    const int a_slots = mt::convh::kMaxASlots;
+    const uint64_t a_total = a_slots * slot * mult;
+    int G = 0;
+    for (int g = std::min(taps, 256); g >= 1; --g)
+        if (taps % g == 0 && a_total + 2 * (uint64_t)g * mult * bmat <= budget) { G = g; break; }
+    if (G == 0) return false;
+    const uint64_t bstage = (uint64_t)G * mult * bmat;
+    const int b_stages = (int)std::min<uint64_t>(mt::convh::kMaxBStages, (budget - a_total) / bstage);
+    hp.P = P; hp.TXv = TXv; hp.TY = TY; hp.HR = HR;
+    hp.G = G; hp.tgroups = taps / G;
+    hp.a_slots = a_slots; hp.b_stages = b_stages;
+    hp.halo_bytes = (uint32_t)P * HR * 128u;
+    hp.slot_bytes = (uint32_t)slot;
+    hp.b_bytes = (uint32_t)bstage;
+    hp.a_off = 0;
+    hp.alo_off = (uint32_t)(a_slots * slot);                  // used only by TF32X3
+    hp.b_off = (uint32_t)a_total;
+    hp.bar_off = hp.b_off + (uint32_t)(b_stages * bstage);
+    smem = 1024u + hp.bar_off + bars;
+    return smem <= kHaloSmemMax;
+}
+
+// `wt` holds the reordered weights: [taps][Ncol][Cinp] for TF32, [taps][2][Ncol][Cinp]
+// (hi, lo) for TF32X3.
+int run_fwd_halo(const float* act, int N, int Hin, int Win, int Cin, const float* wt, int Ncol, int kh, int kw,
+                 int pad, float* out, int Ho, int Wo, const float* bias, bool x3, cudaStream_t st, int sms,
+                 const mt::convh::HaloParams& plan, int bn, uint32_t smem, std::string& path) {
+    mt::convh::HaloParams hp = plan;
+    const int Cinp = (Cin + 3) & ~3;
+    hp.N = N; hp.Ho = Ho; hp.Wo = Wo; hp.Ncol = Ncol; hp.C = Cin; hp.kh = kh; hp.kw = kw; hp.pad = pad;
+    hp.tiles_y = (Ho + hp.TY - 1) / hp.TY;
+    hp.tiles_x = (Wo + hp.TXv - 1) / hp.TXv;
+    hp.tiles_n = (Ncol + bn - 1) / bn;
+    hp.cblocks = (Cin + 31) / 32;
+    hp.taps = kh * kw;
+    hp.num_tiles = (long long)N * hp.tiles_y * hp.tiles_x * hp.tiles_n;
+    hp.out = out;
+    hp.bias = bias;
+    CUtensorMap ta, tb;
+    const uint64_t rowb = (uint64_t)Cinp * 4;
+    if (!encode_4d(&ta, act, {(uint64_t)Cin, (uint64_t)Win, (uint64_t)Hin, (uint64_t)N},
+                   {rowb, rowb * Win, rowb * Win * Hin}, {32u, (uint32_t)hp.P, (uint32_t)hp.HR, 1u}, 128))
+        return fail(MT_EUNSUPPORTED, "conv halo: activation tensor map rejected");
+    // Outer dimension: taps of all kWeightCopies copies (a box of G taps never straddles
+    // two copies because G divides the tap count).
+    const uint64_t taps_all = (uint64_t)(kh * kw) * kWeightCopies;
+    hp.copies = kWeightCopies;
+    bool ok;
+    if (x3)
+        ok = encode_4d(&tb, wt, {(uint64_t)Cin, (uint64_t)Ncol, 2, taps_all}, {rowb, rowb * Ncol, rowb * Ncol * 2},
+                       {32u, (uint32_t)bn, 2u, (uint32_t)hp.G}, 128);
+    else
+        ok = encode_4d(&tb, wt, {(uint64_t)Cin, (uint64_t)Ncol, taps_all, 1},
+                       {rowb, rowb * Ncol, rowb * Ncol * taps_all}, {32u, (uint32_t)bn, (uint32_t)hp.G, 1u}, 128);
+    if (!ok) return fail(MT_EUNSUPPORTED, "conv halo: weight tensor map rejected");
+    const int grid = (int)std::min<long long>(hp.num_tiles, sms);
+    int rc;
+    switch (bn) {
+        case 32:  rc = x3 ? launch_halo_inst<32, true>(ta, tb, hp, smem, grid, st)
+                          : launch_halo_inst<32, false>(ta, tb, hp, smem, grid, st); break;
+        case 64:  rc = x3 ? launch_halo_inst<64, true>(ta, tb, hp, smem, grid, st)
+                          : launch_halo_inst<64, false>(ta, tb, hp, smem, grid, st); break;
+        default:  rc = x3 ? launch_halo_inst<128, true>(ta, tb, hp, smem, grid, st)
+                          : launch_halo_inst<128, false>(ta, tb, hp, smem, grid, st); break;
+    }
+    path = std::string("tma_halo bn=") + std::to_string(bn) + " tile=" + std::to_string(hp.TY) + "x" +
+           std::to_string(hp.TXv) + " pitch=" + std::to_string(hp.P) + " taps/stage=" + std::to_string(hp.G) +
+           " bstages=" + std::to_string(hp.b_stages);
+    return rc;
+}
+
 // Forward-shaped TMA conv: `act` is an NHWC activation [N, Hin, Win, Cin_p] (Cin real
 // channels), `wt` the reordered weights [taps][Ncol][Cin_p], output `out` NCHW [N, Ncol, Ho, Wo].
-int run_fwd_tma(const float* act, int N, int Hin, int Win, int Cin, const float* wt, int Ncol, int kh, int kw,
-                int pad, float* out, int Ho, int Wo, const float* bias, bool x3, cudaStream_t st, int sms,
-                std::string& path) {
+// `w` / `sw`: the weight view [Co, C, kh, kw]; `wt`: scratch for the reordered weights
+// (2 * taps * Ncol * Cinp floats); `dgrad` selects the flipped, transposed input-grad form.
+int run_fwd_tma(const float* act, int N, int Hin, int Win, int Cin, const float* w, const int64_t (&sw)[4],
+                bool dgrad, float* wt, int Ncol, int kh, int kw, int pad, float* out, int Ho, int Wo,
+                const float* bias, bool x3, cudaStream_t st, int sms, std::string& path) {
+    const int Co = dgrad ? Cin : Ncol, Ci = dgrad ? Ncol : Cin;   // the weight view's own dims
+    if (halo_enabled()) {
+        mt::convh::HaloParams plan;
+        memset(&plan, 0, sizeof plan);
+        int bn = 0;
+        uint32_t smem = 0;
+        if (plan_halo(Ho, Wo, kh, kw, Ncol, x3, bn, plan, smem)) {
+            int rc = reorder_w(w, sw, wt, Co, Ci, kh, kw, dgrad, st, x3, kWeightCopies);
+            if (rc) return rc;
+            return run_fwd_halo(act, N, Hin, Win, Cin, wt, Ncol, kh, kw, pad, out, Ho, Wo, bias, x3, st, sms, plan,
+                                bn, smem, path);
+        }
+    }
+    int rc = reorder_w(w, sw, wt, Co, Ci, kh, kw, dgrad, st, false);
+    if (rc) return rc;
     const int Cinp = (Cin + 3) & ~3;
     mt::convt::FwdParams fp;
     memset(&fp, 0, sizeof fp);
@@ -712,7 +845,7 @@ int run_fwd_tma(const float* act, int N, int Hin, int Win, int Cin, const float*
     if (!encode_3d(&tb, wt, (uint64_t)Cin, (uint64_t)Ncol, (uint64_t)(kh * kw), rowb, rowb * Ncol, 32, bn, 128))
         return fail(MT_EUNSUPPORTED, "conv tma: weight tensor map rejected");
     const int grid = (int)std::min<long long>(fp.num_tiles, sms);
-    int rc = x3 ? launch_fwd_tma<true>(bn, ta, tb, fp, grid, st) : launch_fwd_tma<false>(bn, ta, tb, fp, grid, st);
+    rc = x3 ? launch_fwd_tma<true>(bn, ta, tb, fp, grid, st) : launch_fwd_tma<false>(bn, ta, tb, fp, grid, st);
     path = std::string("tma bn=") + std::to_string(bn) + " tile=" + std::to_string(fp.TY) + "x" +
            std::to_string(fp.TX);
     return rc;
@@ -720,7 +853,8 @@ int run_fwd_tma(const float* act, int N, int Hin, int Win, int Cin, const float*
 
 size_t fwd_tma_scratch(int64_t N, int64_t H, int64_t W, int64_t C, int64_t Co, int64_t taps) {
     const int64_t Cp = (C + 3) & ~3;
-    return (size_t)(N * H * W * Cp + taps * Co * Cp) * sizeof(float) + 256;
+    // weights: hi + lo, kWeightCopies copies (the halo kernel's L2 spreading)
+    return (size_t)(N * H * W * Cp + 2 * kWeightCopies * taps * Co * Cp) * sizeof(float) + 256;
 }
 
 int conv_fwd(const mt_tensor* x, const mt_tensor* w, const mt_tensor* bias, const mt_tensor* y, uint64_t stride,
@@ -761,8 +895,8 @@ int conv_fwd(const mt_tensor* x, const mt_tensor* w, const mt_tensor* bias, cons
         float* wt = scratch + ((s.N * s.H * s.W * ((s.C + 3) & ~3) + 63) & ~int64_t(63));
         std::string path;
         rc = to_nhwc(cp.x, cp.sx, xt, (int)s.N, (int)s.C, (int)s.H, (int)s.W, st);
-        if (!rc) rc = reorder_w(cp.w, cp.sw, wt, (int)s.Co, (int)s.C, (int)s.kh, (int)s.kw, false, st);
-        if (!rc) rc = run_fwd_tma(xt, (int)s.N, (int)s.H, (int)s.W, (int)s.C, wt, (int)s.Co, (int)s.kh, (int)s.kw,
+        if (!rc) rc = run_fwd_tma(xt, (int)s.N, (int)s.H, (int)s.W, (int)s.C, cp.w, cp.sw, false, wt, (int)s.Co,
+                                  (int)s.kh, (int)s.kw,
                                   (int)s.pad, cp.out, (int)s.Ho, (int)s.Wo, bp, x3, st, di.sms, path);
         cudaFreeAsync(scratch, st);
         if (rc == MT_OK) t_path = std::string("conv_umma_fwd_") + (x3 ? "tf32x3 " : "tf32 ") + path;
@@ -816,8 +950,8 @@ int conv_dgrad(const mt_tensor* dy, const mt_tensor* w, const mt_tensor* dx, uin
         float* wt = scratch + ((s.N * s.Ho * s.Wo * ((s.Co + 3) & ~3) + 63) & ~int64_t(63));
         std::string path;
         rc = to_nhwc(cp.dy, cp.sdy, dyt, (int)s.N, (int)s.Co, (int)s.Ho, (int)s.Wo, st);
-        if (!rc) rc = reorder_w(cp.w, cp.sw, wt, (int)s.Co, (int)s.C, (int)s.kh, (int)s.kw, true, st);
-        if (!rc) rc = run_fwd_tma(dyt, (int)s.N, (int)s.Ho, (int)s.Wo, (int)s.Co, wt, (int)s.C, (int)s.kh, (int)s.kw,
+        if (!rc) rc = run_fwd_tma(dyt, (int)s.N, (int)s.Ho, (int)s.Wo, (int)s.Co, cp.w, cp.sw, true, wt, (int)s.C,
+                                  (int)s.kh, (int)s.kw,
                                   (int)(s.kh - 1 - s.pad), cp.out, (int)s.H, (int)s.W, nullptr, x3, st, di.sms, path);
         cudaFreeAsync(scratch, st);
         if (rc == MT_OK) t_path = std::string("conv_umma_dgrad_") + (x3 ? "tf32x3 " : "tf32 ") + path;

@@ -96,6 +96,18 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     }
 }
 
+// Warp-cooperative bounded wait for roles where a whole warp consumes the phase: lane 0
+// spins (a warp of spinning threads would compete with the producer and MMA threads for
+// the barrier unit), then every lane issues one try_wait of its own, which succeeds at
+// once and gives that lane the acquire of the completed phase.
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, volatile int* abort_flag, int code) {
+    int ok = 1;
+    if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort_flag, code) ? 1 : 0;
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    if (ok) (void)mbar_try_wait(bar, parity);
+    return ok != 0;
+}
+
 // ---------------------------------------------------------------------------------
 // cp.async: per-thread asynchronous global -> shared copies (used by gather producers
 // whose tiles no TMA box can describe). src_bytes 0 zero-fills the destination.

@@ -95,6 +95,8 @@ def test_config4_resnet_3x3(eng, port, mode):
     (2, 5, 9, 12, 7, 5, 2, 2),
     (1, 64, 14, 14, 256, 3, 1, 1),
     (4, 2, 6, 6, 3, 7, 1, 3),
+    (1, 4, 5, 140, 8, 3, 1, 1),       # stride-1 rows wider than one pitched tile
+    (2, 40, 9, 20, 48, 3, 1, 0),      # no padding, channels not a multiple of 32
 ])
 def test_conv_shapes(eng, port, mode, shape):
     N, C, H, W, Co, k, s, p = shape
