@@ -13,10 +13,6 @@
 // Positions with tx >= TXv are computed and discarded; a valid position never reads
 // past the rows TMA wrote.
 //
-// Weights are read by every CTA for every tile; all CTAs start together, and reading one
-// copy they queue on the same L2 lines. The reorder kernel writes `copies` identical
-// copies and CTA b reads copy b % copies.
-//
 // Few, large pipeline stages. Each handoff between roles costs a few hundred cycles (an
 // mbarrier wait, an expect-tx, a TMA issue), which is more than the MMA time of one tap
 // of a 32-channel block at N = 64 (4 k-steps of 32 cycles). So a weight stage is ONE TMA
@@ -42,7 +38,6 @@ struct HaloParams {
     int P, TXv, TY, HR;                   // pitch, valid columns, output rows, halo rows
     int tiles_y, tiles_x, tiles_n, cblocks, taps;
     int G, tgroups;                       // taps per weight stage, stages per channel block
-    int copies;                           // identical weight copies; CTA b reads copy b % copies
     long long num_tiles;
     int a_slots, b_stages;
     uint32_t halo_bytes;                  // bytes TMA writes per halo (P * HR * 128)
@@ -163,7 +158,7 @@ conv_fwd_halo_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                         const uint32_t bar = smem_u32(&b_full[s]);
                         mbar_arrive_expect_tx(bar, p.b_bytes);
                         const uint32_t dst = smem_u32(b_ring + s * p.b_bytes);
-                        const int tap0 = (int)(blockIdx.x % p.copies) * p.taps + g * p.G;
+                        const int tap0 = g * p.G;
                         if (X3) tma_load_4d(dst, &tmB, bar, cb * 32, nt * BN, 0, tap0);
                         else tma_load_4d(dst, &tmB, bar, cb * 32, nt * BN, tap0, 0);
                         if (++s == p.b_stages) { s = 0; ph ^= 1; }

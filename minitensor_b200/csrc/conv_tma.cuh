@@ -12,9 +12,9 @@
 //                         TMEM lanes), N = C_out, K = (tap, 32-channel block); A and B are
 //                         one TMA box each per stage. Stride 1. Input-grad (stride 1) is
 //                         the same kernel on NHWC dy with flipped, transposed weights.
-//   conv_wgrad_tma_kernel M = (tap, channel), N = C_out, K = output pixels (runs of 32 in
-//                         one row); A = four 32-channel chunks of NHWC x (M-major), B = dy
-//                         straight from NCHW. Split-K partials, then
+//   (conv_wgrad.cuh)      weight-grad: M = (tap, channel), N = C_out, K = output pixels;
+//                         A = four 32-channel chunks of NHWC x (M-major), B = dy straight
+//                         from NCHW. Split-K partials, then
 //   wgrad_reduce_kernel   dW[co,c,r,s] = sum over splits (in order) of the partials.
 //
 // Warp roles as in the GEMM kernel: 0 TMA producer, 1 MMA issuer + TMEM owner, 2-5
@@ -66,11 +66,8 @@ __global__ void __launch_bounds__(256) nchw_to_nhwc_kernel(const float* __restri
 // split != 0 writes the TF32X3 pair instead, Wt[tap][h][row][col] with h = 0 the tf32
 // rounding hi = rna_tf32(v) and h = 1 the remainder lo = v - hi, so that one TMA box
 // brings both halves of a weight tile and no kernel has to split weights again.
-// copies > 1 writes that many identical copies back to back (see the halo kernel: CTAs
-// read different copies so that they do not all queue on the same L2 lines).
 __global__ void reorder_weights_kernel(const float* __restrict__ w, int64_t s0, int64_t s1, int64_t s2, int64_t s3,
-                                       float* __restrict__ wt, int Co, int C, int kh, int kw, int dgrad, int split,
-                                       int copies) {
+                                       float* __restrict__ wt, int Co, int C, int kh, int kw, int dgrad, int split) {
     const int rows = dgrad ? C : Co, cols = dgrad ? Co : C;
     const int colsp = (cols + 3) & ~3;
     const int64_t total = (int64_t)kh * kw * rows * colsp;
@@ -85,18 +82,14 @@ __global__ void reorder_weights_kernel(const float* __restrict__ w, int64_t s0, 
             v = dgrad ? __ldg(w + col * s0 + row * s1 + (kh - 1 - r) * s2 + (kw - 1 - s) * s3)
                       : __ldg(w + row * s0 + col * s1 + r * s2 + s * s3);
         }
-        const int64_t copy_stride = total * (split ? 2 : 1);
-        for (int c = 0; c < copies; ++c) {
-            float* dst = wt + c * copy_stride;
-            if (split) {
-                const int64_t plane = (int64_t)rows * colsp;
-                const int64_t o = (int64_t)tap * 2 * plane + (int64_t)row * colsp + col;
-                const float hi = tf32_round(v);
-                dst[o] = hi;
-                dst[o + plane] = v - hi;
-            } else {
-                dst[i] = v;
-            }
+        if (split) {
+            const int64_t plane = (int64_t)rows * colsp;
+            const int64_t o = (int64_t)tap * 2 * plane + (int64_t)row * colsp + col;
+            const float hi = tf32_round(v);
+            wt[o] = hi;
+            wt[o + plane] = v - hi;
+        } else {
+            wt[i] = v;
         }
     }
 }
@@ -351,157 +344,7 @@ done:
 }
 
 // ------------------------------------------------------------------ weight-grad -----
-__device__ __forceinline__ void wgrad_unit(const WgradParams& p, long long u, int& mt, int& nt, int& kb0, int& kb1) {
-    const int sp = (int)(u % p.splits);
-    const long long r = u / p.splits;
-    nt = (int)(r % p.tiles_n);
-    mt = (int)(r / p.tiles_n);
-    kb0 = (int)((long long)p.kb_total * sp / p.splits);
-    kb1 = (int)((long long)p.kb_total * (sp + 1) / p.splits);
-}
-
-template <int BN, bool X3, int STAGES>
-__global__ void __launch_bounds__(Cfg<BN, X3, STAGES>::THREADS, 1)
-conv_wgrad_tma_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                      const WgradParams p) {
-    using G = Cfg<BN, X3, STAGES>;
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* ring = smem;
-    uint8_t* ring_lo = smem + G::STAGE_BYTES * STAGES;
-    const Bars bb = carve_bars<STAGES>(smem + G::RING_BYTES);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const long long first = blockIdx.x, step = gridDim.x;
-
-    if (threadIdx.x == 0) init_bars<STAGES>(bb);
-    if (warp == 0 && lane == 0) {
-        tma_prefetch_desc(&tmA);
-        tma_prefetch_desc(&tmB);
-    }
-    if (warp == 1) {
-        tmem_alloc(smem_u32((const void*)bb.tmem_slot), G::TMEM_COLS);
-        tmem_relinquish();
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem_base = *bb.tmem_slot;
-
-    if (warp == 0) {
-        if (lane == 0) {
-            int s = 0;
-            uint32_t ph = 0;
-            for (long long u = first; u < p.num_units; u += step) {
-                int mt, nt, kb0, kb1;
-                wgrad_unit(p, u, mt, nt, kb0, kb1);
-                // The tile's four 32-row chunks: (tap, channel block) of rows m0 + 32 q.
-                int ctap[4], cc0[4];
-                uint32_t a_bytes = 0;
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const int m = mt * 128 + q * 32;
-                    ctap[q] = m < p.M ? m / p.C : -1;
-                    cc0[q] = m < p.M ? m - ctap[q] * p.C : 0;
-                    if (ctap[q] >= 0) a_bytes += 32 * 32 * 4;
-                }
-                for (int kb = kb0; kb < kb1; ++kb) {
-                    const int img = kb / p.kb_per_img, rem = kb - img * p.kb_per_img;
-                    const int y = rem / p.xblocks, x0 = (rem - y * p.xblocks) * 32;
-                    if (!mbar_wait(smem_u32(&bb.empty[s]), ph ^ 1, bb.abort_flag, kDevTimeoutEmpty)) goto done;
-                    const uint32_t bar = smem_u32(&bb.full[s]);
-                    mbar_arrive_expect_tx(bar, a_bytes + G::B_BYTES);
-                    const uint32_t sa = smem_u32(ring + s * G::STAGE_BYTES);
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        if (ctap[q] < 0) continue;
-                        const int r = ctap[q] / p.kw, sx = ctap[q] - r * p.kw;
-                        tma_load_4d(sa + q * 4096, &tmA, bar, cc0[q], x0 + sx - p.pad, y + r - p.pad, img);
-                    }
-                    tma_load_4d(sa + G::A_BYTES, &tmB, bar, x0, y, nt * BN, img);
-                    if (++s == STAGES) { s = 0; ph ^= 1; }
-                }
-            }
-        }
-    } else if (warp == 1) {
-        if (lane == 0) {
-            constexpr uint32_t idesc = umma_idesc_tf32(128, BN, 1, 0);
-            int s = 0, it = 0;
-            uint32_t ph = 0;
-            for (long long u = first; u < p.num_units; u += step, ++it) {
-                int mt, nt, kb0, kb1;
-                wgrad_unit(p, u, mt, nt, kb0, kb1);
-                const int a = it & 1;
-                if (!mbar_wait(smem_u32(&bb.acc_empty[a]), ((it >> 1) & 1) ^ 1, bb.abort_flag, kDevTimeoutAccEmpty))
-                    goto done;
-                tc_fence_after();
-                for (int kb = kb0; kb < kb1; ++kb) {
-                    const uint32_t wbar = X3 ? smem_u32(&bb.conv[s]) : smem_u32(&bb.full[s]);
-                    if (!mbar_wait(wbar, ph, bb.abort_flag, kDevTimeoutFull)) goto done;
-                    tc_fence_after();
-                    mma_stage<true, X3, G::A_BYTES>(tmem_base + a * BN, smem_u32(ring + s * G::STAGE_BYTES),
-                                                    smem_u32(ring_lo + s * G::STAGE_BYTES), idesc, kb == kb0);
-                    umma_commit(smem_u32(&bb.empty[s]));
-                    if (++s == STAGES) { s = 0; ph ^= 1; }
-                }
-                umma_commit(smem_u32(&bb.acc_full[a]));
-            }
-        }
-    } else if (warp < 6) {
-        const int q = warp & 3;
-        int it = 0;
-        for (long long u = first; u < p.num_units; u += step, ++it) {
-            int mt, nt, kb0, kb1;
-            wgrad_unit(p, u, mt, nt, kb0, kb1);
-            const int sp = (int)(u % p.splits);
-            const bool no_k = kb1 <= kb0;
-            const int a = it & 1;
-            if (!mbar_wait(smem_u32(&bb.acc_full[a]), (it >> 1) & 1, bb.abort_flag, kDevTimeoutAccFull)) goto done;
-            __syncwarp();
-            tc_fence_after();
-            const int m = mt * 128 + q * 32 + lane;
-            float* row = p.ws + ((int64_t)sp * p.M + m) * p.ws_ld + nt * BN;
-#pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
-                uint32_t rr[32];
-                tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + a * BN + c * 32, rr);
-                tmem_ld_wait();
-                if (c == BN / 32 - 1) {
-                    tc_fence_before();
-                    mbar_arrive(smem_u32(&bb.acc_empty[a]));
-                }
-                if (m < p.M) {
-#pragma unroll
-                    for (int j = 0; j < 32; j += 4)
-                        *reinterpret_cast<float4*>(row + c * 32 + j) =
-                            no_k ? make_float4(0.f, 0.f, 0.f, 0.f)
-                                 : make_float4(__uint_as_float(rr[j]), __uint_as_float(rr[j + 1]),
-                                               __uint_as_float(rr[j + 2]), __uint_as_float(rr[j + 3]));
-                }
-            }
-        }
-    } else if (X3) {
-        const int ct = threadIdx.x - 6 * 32;
-        int s = 0;
-        uint32_t ph = 0;
-        for (long long u = first; u < p.num_units; u += step) {
-            int mt, nt, kb0, kb1;
-            wgrad_unit(p, u, mt, nt, kb0, kb1);
-            for (int kb = kb0; kb < kb1; ++kb) {
-                if (!splitter_stage<STAGES, G::STAGE_BYTES>(bb, ring, ring_lo, s, ph, ct)) goto done;
-                if (++s == STAGES) { s = 0; ph ^= 1; }
-            }
-        }
-    }
-done:
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 1) {
-        __syncwarp();
-        tc_fence_after();
-        tmem_dealloc(tmem_base, G::TMEM_COLS);
-    }
-}
-
+// The weight-gradient kernel itself lives in conv_wgrad.cuh; its partials are summed here.
 // dW[co, c, r, s] = sum over splits (in order) of ws[split][(r*kw + s) * C + c][co].
 __global__ void wgrad_reduce_kernel(const float* __restrict__ ws, int splits, int M, int ws_ld, float* __restrict__ dw,
                                     int Co, int C, int taps) {

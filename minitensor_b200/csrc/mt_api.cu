@@ -18,6 +18,7 @@
 #include "conv_gemm.cuh"
 #include "conv_tma.cuh"
 #include "conv_halo.cuh"
+#include "conv_wgrad.cuh"
 
 namespace {
 
@@ -616,12 +617,12 @@ int to_nhwc(const float* src, const int64_t (&sv)[4], float* dst, int N, int C, 
 }
 
 int reorder_w(const float* w, const int64_t (&sw)[4], float* wt, int Co, int C, int kh, int kw, bool dgrad,
-              cudaStream_t st, bool split = false, int copies = 1) {
+              cudaStream_t st, bool split = false) {
     const int rows = dgrad ? C : Co, cols = dgrad ? Co : C;
     const int64_t total = (int64_t)kh * kw * rows * ((cols + 3) & ~3);
     const int blocks = (int)std::min<int64_t>((total + 255) / 256, 1024);
     mt::convt::reorder_weights_kernel<<<blocks, 256, 0, st>>>(w, sw[0], sw[1], sw[2], sw[3], wt, Co, C, kh, kw,
-                                                              dgrad ? 1 : 0, split ? 1 : 0, copies);
+                                                              dgrad ? 1 : 0, split ? 1 : 0);
     return launch_simple(cudaGetLastError(), "reorder_weights");
 }
 
@@ -650,18 +651,6 @@ int launch_fwd_tma_inst(const CUtensorMap& ta, const CUtensorMap& tb, const mt::
     return launch_simple(cudaGetLastError(), "conv fwd tma");
 }
 
-template <int BN, bool X3, int STAGES>
-int launch_wgrad_tma_inst(const CUtensorMap& ta, const CUtensorMap& tb, const mt::convt::WgradParams& wp, int grid,
-                          cudaStream_t st) {
-    using G = mt::convt::Cfg<BN, X3, STAGES>;
-    auto kern = mt::convt::conv_wgrad_tma_kernel<BN, X3, STAGES>;
-    static std::atomic<uint64_t> mask{0};
-    int rc = set_smem(kern, G::SMEM_BYTES, mask);
-    if (rc) return rc;
-    kern<<<grid, G::THREADS, G::SMEM_BYTES, st>>>(ta, tb, wp);
-    return launch_simple(cudaGetLastError(), "conv wgrad tma");
-}
-
 // Stages keep the ring (doubled for the lo copy) within ~192 KB of shared memory.
 template <bool X3>
 int launch_fwd_tma(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const mt::convt::FwdParams& fp, int grid,
@@ -673,20 +662,40 @@ int launch_fwd_tma(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const m
         default:  return launch_fwd_tma_inst<256, X3, X3 ? 2 : 4>(ta, tb, fp, grid, st);
     }
 }
+
+// ---- weight-grad with wide stages -------------------------------------------------
+template <int BN, bool X3, int STAGES, int XCS, int RS>
+int launch_wgrad_wide_inst(const CUtensorMap& ta, const CUtensorMap& tb, const mt::convt::WgradParams& wp, int grid,
+                           cudaStream_t st) {
+    using G = mt::convw::WCfg<BN, X3, STAGES, XCS, RS>;
+    auto kern = mt::convw::conv_wgrad_wide_kernel<BN, X3, STAGES, XCS, RS>;
+    static std::atomic<uint64_t> mask{0};
+    int rc = set_smem(kern, G::SMEM_BYTES, mask);
+    if (rc) return rc;
+    kern<<<grid, G::THREADS, G::SMEM_BYTES, st>>>(ta, tb, wp);
+    return launch_simple(cudaGetLastError(), "conv wgrad wide");
+}
+
+// Stage shape per precision: XCS runs of 32 pixels of one output row (RS = 1) and ring
+// depth, rings of <= ~192 KB (doubled for the TF32X3 lo copies). Measured on c4: TF32
+// takes 2 runs with 4 stages; TF32X3 is better with 1 run and 4 stages than with 2 runs
+// and only 2 stages (a second output row per stage gained nothing either way).
+struct WideShape { int xcs, rs; };
+WideShape wgrad_shape(bool x3) { return x3 ? WideShape{1, 1} : WideShape{2, 1}; }
 template <bool X3>
-int launch_wgrad_tma(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const mt::convt::WgradParams& wp, int grid,
-                     cudaStream_t st) {
+int launch_wgrad_wide(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const mt::convt::WgradParams& wp,
+                      int grid, cudaStream_t st) {
+    constexpr int XCS = X3 ? 1 : 2;
     switch (bn) {
-        case 32:  return launch_wgrad_tma_inst<32, X3, X3 ? 4 : 8>(ta, tb, wp, grid, st);
-        case 64:  return launch_wgrad_tma_inst<64, X3, X3 ? 4 : 8>(ta, tb, wp, grid, st);
-        case 128: return launch_wgrad_tma_inst<128, X3, X3 ? 3 : 6>(ta, tb, wp, grid, st);
-        default:  return launch_wgrad_tma_inst<256, X3, X3 ? 2 : 4>(ta, tb, wp, grid, st);
+        case 32:  return launch_wgrad_wide_inst<32, X3, X3 ? 4 : 4, XCS, 1>(ta, tb, wp, grid, st);
+        case 64:  return launch_wgrad_wide_inst<64, X3, X3 ? 4 : 4, XCS, 1>(ta, tb, wp, grid, st);
+        case 128: return launch_wgrad_wide_inst<128, X3, X3 ? 3 : 3, XCS, 1>(ta, tb, wp, grid, st);
+        default:  return launch_wgrad_wide_inst<256, X3, X3 ? 2 : 2, XCS, 1>(ta, tb, wp, grid, st);
     }
 }
 
 // ---- pitched-halo forward (one activation box per 32-channel block for all taps) ----
 constexpr uint32_t kHaloSmemMax = 227 * 1024;
-constexpr int kWeightCopies = 16;   // weight copies the halo kernel's CTAs spread over
 
 template <int BN, bool X3>
 int launch_halo_inst(const CUtensorMap& ta, const CUtensorMap& tb, const mt::convh::HaloParams& hp, uint32_t smem,
@@ -771,10 +780,7 @@ int run_fwd_halo(const float* act, int N, int Hin, int Win, int Cin, const float
     if (!encode_4d(&ta, act, {(uint64_t)Cin, (uint64_t)Win, (uint64_t)Hin, (uint64_t)N},
                    {rowb, rowb * Win, rowb * Win * Hin}, {32u, (uint32_t)hp.P, (uint32_t)hp.HR, 1u}, 128))
         return fail(MT_EUNSUPPORTED, "conv halo: activation tensor map rejected");
-    // Outer dimension: taps of all kWeightCopies copies (a box of G taps never straddles
-    // two copies because G divides the tap count).
-    const uint64_t taps_all = (uint64_t)(kh * kw) * kWeightCopies;
-    hp.copies = kWeightCopies;
+    const uint64_t taps_all = (uint64_t)(kh * kw);
     bool ok;
     if (x3)
         ok = encode_4d(&tb, wt, {(uint64_t)Cin, (uint64_t)Ncol, 2, taps_all}, {rowb, rowb * Ncol, rowb * Ncol * 2},
@@ -813,7 +819,7 @@ int run_fwd_tma(const float* act, int N, int Hin, int Win, int Cin, const float*
         int bn = 0;
         uint32_t smem = 0;
         if (plan_halo(Ho, Wo, kh, kw, Ncol, x3, bn, plan, smem)) {
-            int rc = reorder_w(w, sw, wt, Co, Ci, kh, kw, dgrad, st, x3, kWeightCopies);
+            int rc = reorder_w(w, sw, wt, Co, Ci, kh, kw, dgrad, st, x3);
             if (rc) return rc;
             return run_fwd_halo(act, N, Hin, Win, Cin, wt, Ncol, kh, kw, pad, out, Ho, Wo, bias, x3, st, sms, plan,
                                 bn, smem, path);
@@ -853,8 +859,7 @@ int run_fwd_tma(const float* act, int N, int Hin, int Win, int Cin, const float*
 
 size_t fwd_tma_scratch(int64_t N, int64_t H, int64_t W, int64_t C, int64_t Co, int64_t taps) {
     const int64_t Cp = (C + 3) & ~3;
-    // weights: hi + lo, kWeightCopies copies (the halo kernel's L2 spreading)
-    return (size_t)(N * H * W * Cp + 2 * kWeightCopies * taps * Co * Cp) * sizeof(float) + 256;
+    return (size_t)(N * H * W * Cp + 2 * taps * Co * Cp) * sizeof(float) + 256;   // weights: room for hi + lo
 }
 
 int conv_fwd(const mt_tensor* x, const mt_tensor* w, const mt_tensor* bias, const mt_tensor* y, uint64_t stride,
@@ -1000,11 +1005,11 @@ WgradPlan wgrad_plan(const ConvShape& s, int sms) {
 // Weight-grad on the TMA path: x -> NHWC (xt), partials [splits][taps*C][Cop].
 struct WgradTmaPlan {
     bool ok;
-    int bn, tiles_m, tiles_n, xblocks, kb_per_img, kb_total, splits, M, ws_ld;
+    int bn, xcs, rs, tiles_m, tiles_n, xblocks, kb_per_img, kb_total, splits, M, ws_ld;
     size_t xt_floats, part_floats, bytes;
 };
 
-WgradTmaPlan wgrad_tma_plan(const ConvShape& s, const mt_tensor* dy, int sms) {
+WgradTmaPlan wgrad_tma_plan(const ConvShape& s, const mt_tensor* dy, int sms, bool x3) {
     WgradTmaPlan w;
     memset(&w, 0, sizeof w);
     const bool dy_ok = dy->strides[3] == 1 && dy->strides[2] % 4 == 0 && dy->strides[1] % 4 == 0 &&
@@ -1016,8 +1021,11 @@ WgradTmaPlan wgrad_tma_plan(const ConvShape& s, const mt_tensor* dy, int sms) {
     w.tiles_m = (w.M + 127) / 128;
     w.tiles_n = ((int)s.Co + w.bn - 1) / w.bn;
     w.ws_ld = w.tiles_n * w.bn;
-    w.xblocks = (int)((s.Wo + 31) / 32);
-    w.kb_per_img = (int)s.Ho * w.xblocks;
+    const WideShape ws = wgrad_shape(x3);
+    w.xcs = ws.xcs;
+    w.rs = ws.rs;
+    w.xblocks = (int)((s.Wo + 32 * w.xcs - 1) / (32 * w.xcs));   // runs of 32 * xcs pixels per row
+    w.kb_per_img = (int)((s.Ho + w.rs - 1) / w.rs) * w.xblocks;
     w.kb_total = (int)s.N * w.kb_per_img;
     const int tiles = w.tiles_m * w.tiles_n;
     w.splits = std::max(1, std::min(tiles >= sms ? 1 : sms / tiles, w.kb_total));
@@ -1045,17 +1053,18 @@ int conv_wgrad_tma(const ConvShape& s, const WgradTmaPlan& w, const mt::conv::Pa
     wp.ws_ld = w.ws_ld;
     CUtensorMap ta, tb;
     const uint64_t Cp = (uint64_t)((s.C + 3) & ~3), rowb = Cp * 4;
-    // A: NHWC x as M-major 32-channel chunks x 32 pixels (K) of one row.
+    // A: NHWC x as M-major 32-channel chunks x 32 * xcs pixels (K) of one row.
     if (!encode_4d(&ta, xt, {(uint64_t)s.C, (uint64_t)s.W, (uint64_t)s.H, (uint64_t)s.N},
-                   {rowb, rowb * s.W, rowb * s.W * s.H}, {32u, 32u, 1u, 1u}, 32))
+                   {rowb, rowb * s.W, rowb * s.W * s.H}, {32u, 32u * (uint32_t)w.xcs, (uint32_t)w.rs, 1u}, 32))
         return fail(MT_EUNSUPPORTED, "%s: activation tensor map rejected", who);
-    // B: dy straight from NCHW, rows = C_out, 32 pixels of one output row (K-major).
-    if (!encode_4d(&tb, cp.dy, {(uint64_t)s.Wo, (uint64_t)s.Ho, (uint64_t)s.Co, (uint64_t)s.N},
-                   {(uint64_t)cp.sdy[2] * 4, (uint64_t)cp.sdy[1] * 4, (uint64_t)cp.sdy[0] * 4},
-                   {32u, 1u, (uint32_t)w.bn, 1u}, 128))
+    // B: dy straight from NCHW with the map's dimensions ordered (W, C_out, H, N): a box
+    // {32 pixels, BN channels, rs rows} lands as rs blocks of BN 128-byte rows (K-major).
+    if (!encode_4d(&tb, cp.dy, {(uint64_t)s.Wo, (uint64_t)s.Co, (uint64_t)s.Ho, (uint64_t)s.N},
+                   {(uint64_t)cp.sdy[1] * 4, (uint64_t)cp.sdy[2] * 4, (uint64_t)cp.sdy[0] * 4},
+                   {32u, (uint32_t)w.bn, (uint32_t)w.rs, 1u}, 128))
         return fail(MT_EUNSUPPORTED, "%s: grad_output tensor map rejected", who);
     const int grid = (int)std::min<long long>(wp.num_units, sms);
-    rc = x3 ? launch_wgrad_tma<true>(w.bn, ta, tb, wp, grid, st) : launch_wgrad_tma<false>(w.bn, ta, tb, wp, grid, st);
+    rc = x3 ? launch_wgrad_wide<true>(w.bn, ta, tb, wp, grid, st) : launch_wgrad_wide<false>(w.bn, ta, tb, wp, grid, st);
     if (rc) return rc;
     const int64_t total = s.Co * s.C * s.kh * s.kw;
     const int blocks = (int)std::min<int64_t>((total + 255) / 256, 4 * sms);
@@ -1094,7 +1103,7 @@ int conv_wgrad(const mt_tensor* dy, const mt_tensor* x, const mt_tensor* dw, uin
     if (!offsets_fit_32(dy) || !offsets_fit_32(x))
         return fail(MT_EUNSUPPORTED, "%s: a view spans 2^31 elements or more", who);
     const bool x3w = mode == MT_TF32X3;
-    const WgradTmaPlan tp = allow_tma ? wgrad_tma_plan(s, dy, di.sms) : WgradTmaPlan{};
+    const WgradTmaPlan tp = allow_tma ? wgrad_tma_plan(s, dy, di.sms, x3w) : WgradTmaPlan{};
     if (tp.ok) {
         float* scratch = static_cast<float*>(workspace);
         bool owned = false;
@@ -1392,7 +1401,7 @@ MT_API size_t mt_conv2d_wgrad_workspace_bytes(const mt_tensor* dy, const mt_tens
     ConvShape s;
     if (conv_shape(x, dw, dy, stride, padding, "wgrad_ws", s)) return 0;
     if (resolve_mode(mode) == MT_STRICT_FP32 || s.N * s.Ho * s.Wo == 0) return 0;
-    const WgradTmaPlan tp = wgrad_tma_plan(s, dy, dev_info().sms);
+    const WgradTmaPlan tp = wgrad_tma_plan(s, dy, dev_info().sms, resolve_mode(mode) == MT_TF32X3);
     return tp.ok ? tp.bytes : wgrad_plan(s, dev_info().sms).ws_bytes;
 }
 
