@@ -21,6 +21,10 @@
 // activation halo is one box per 32-channel block: the MMA issuer then waits once per
 // G * 4 (* 3) MMAs instead of once per 4.
 //
+// Resident weights. When C_out fits one N tile and every weight stage fits beside the
+// halo ring (TF32 at C_out = 64: 2 x 72 KB), stage cb * tgroups + g holds its taps for
+// the whole kernel: loaded once, never released, waited for once.
+//
 // Warp roles: 0 weight (B) producer, 1 MMA issuer + TMEM owner, 2-5 epilogue, 6 halo (A)
 // producer, 7-10 (TF32X3) hi/lo splitter of the halos.
 #pragma once
@@ -38,6 +42,7 @@ struct HaloParams {
     int P, TXv, TY, HR;                   // pitch, valid columns, output rows, halo rows
     int tiles_y, tiles_x, tiles_n, cblocks, taps;
     int G, tgroups;                       // taps per weight stage, stages per channel block
+    int b_resident;                       // 1: every weight stage is loaded once and kept
     long long num_tiles;
     int a_slots, b_stages;
     uint32_t halo_bytes;                  // bytes TMA writes per halo (P * HR * 128)
@@ -152,9 +157,12 @@ conv_fwd_halo_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
             for (long long t = first; t < p.num_tiles; t += step) {
                 int n, y0, x0, nt;
                 halo_tile(p, t, n, y0, x0, nt);
+                if (p.b_resident && t != first) break;   // resident weights: loaded for the first tile only
                 for (int cb = 0; cb < p.cblocks; ++cb)
                     for (int g = 0; g < p.tgroups; ++g) {
-                        if (!mbar_wait(smem_u32(&b_empty[s]), ph ^ 1, abort_flag, kDevTimeoutEmpty)) goto done;
+                        if (!p.b_resident &&
+                            !mbar_wait(smem_u32(&b_empty[s]), ph ^ 1, abort_flag, kDevTimeoutEmpty))
+                            goto done;
                         const uint32_t bar = smem_u32(&b_full[s]);
                         mbar_arrive_expect_tx(bar, p.b_bytes);
                         const uint32_t dst = smem_u32(b_ring + s * p.b_bytes);
@@ -202,7 +210,10 @@ conv_fwd_halo_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                     const uint32_t a_base = smem_u32(a_ring + as * p.slot_bytes);
                     const uint32_t alo_base = smem_u32(alo_ring + as * p.slot_bytes);
                     for (int g = 0; g < p.tgroups; ++g) {
-                        if (!mbar_wait(smem_u32(&b_full[bs]), bph, abort_flag, kDevTimeoutFull)) goto done;
+                        if (p.b_resident) bs = cb * p.tgroups + g;
+                        if ((!p.b_resident || it == 0) &&
+                            !mbar_wait(smem_u32(&b_full[bs]), p.b_resident ? 0u : bph, abort_flag, kDevTimeoutFull))
+                            goto done;
                         tc_fence_after();
                         const uint32_t sbase = smem_u32(b_ring + bs * p.b_bytes);
                         for (int gi = 0; gi < p.G; ++gi) {
@@ -227,8 +238,10 @@ conv_fwd_halo_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                             }
                             first_mma = false;
                         }
-                        umma_commit(smem_u32(&b_empty[bs]));
-                        if (++bs == p.b_stages) { bs = 0; bph ^= 1; }
+                        if (!p.b_resident) {
+                            umma_commit(smem_u32(&b_empty[bs]));
+                            if (++bs == p.b_stages) { bs = 0; bph ^= 1; }
+                        }
                     }
                     umma_commit(smem_u32(&a_empty[as]));
                     if (++as == p.a_slots) { as = 0; aph ^= 1; }

@@ -60,6 +60,44 @@ __global__ void __launch_bounds__(256) nchw_to_nhwc_kernel(const float* __restri
     }
 }
 
+// Fast form for activations whose H x W plane is contiguous (and 16-byte aligned rows of
+// channels): one block per (image, 32 channels, 256 pixels) moves 32 KB with 8 float4
+// loads and 8 float4 stores per thread. The shared tile [32][256] stores element (c, p)
+// at column p ^ (4 * ((c / 4) % 8)): float4 writes along p stay aligned and conflict-free,
+// and the transposed reads (8 channel groups x 4 pixels per warp) hit 32 distinct banks.
+// Requires HW % 4 == 0; channels in [C, Cp) are written as zeros.
+__global__ void __launch_bounds__(256) nchw_to_nhwc_flat_kernel(const float* __restrict__ x, int64_t s0, int64_t s1,
+                                                                float* __restrict__ xt, int N, int C, int HW, int Cp) {
+    __shared__ __align__(16) float tile[32][256];
+    const int p0 = blockIdx.x * 256, c0 = blockIdx.y * 32;
+    const int t = threadIdx.x;
+    for (int n = blockIdx.z; n < N; n += gridDim.z) {
+        const float* src = x + (int64_t)n * s0;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int i = t + 256 * k;
+            const int c = i >> 6, q = i & 63;
+            const int p = p0 + 4 * q;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (c0 + c < C && p < HW) v = __ldg(reinterpret_cast<const float4*>(src + (int64_t)(c0 + c) * s1 + p));
+            *reinterpret_cast<float4*>(&tile[c][(4 * q) ^ (4 * ((c >> 2) & 7))]) = v;
+        }
+        __syncthreads();
+        float* dst = xt + (int64_t)n * HW * Cp;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int i = t + 256 * k;
+            const int pl = i >> 3, cg = i & 7;
+            const int p = p0 + pl, c = c0 + 4 * cg;
+            const int col = pl ^ (4 * cg);
+            if (p < HW && c < Cp)
+                *reinterpret_cast<float4*>(dst + (int64_t)p * Cp + c) =
+                    make_float4(tile[4 * cg][col], tile[4 * cg + 1][col], tile[4 * cg + 2][col], tile[4 * cg + 3][col]);
+        }
+        __syncthreads();
+    }
+}
+
 // Wt[tap][row][col] (col padded to colsp with zeros), tap = r * kw + s:
 //   forward:    row = co, col = ci, value W[co, ci, r, s]
 //   input-grad: row = ci, col = co, value W[co, ci, kh-1-r, kw-1-s] (flipped, transposed)
@@ -346,18 +384,28 @@ done:
 // ------------------------------------------------------------------ weight-grad -----
 // The weight-gradient kernel itself lives in conv_wgrad.cuh; its partials are summed here.
 // dW[co, c, r, s] = sum over splits (in order) of ws[split][(r*kw + s) * C + c][co].
+// Threads run along C_out (the partials' contiguous dimension) so reads coalesce; the
+// split loads are issued eight at a time ahead of the in-order sum.
 __global__ void wgrad_reduce_kernel(const float* __restrict__ ws, int splits, int M, int ws_ld, float* __restrict__ dw,
                                     int Co, int C, int taps) {
-    const int64_t total = (int64_t)Co * C * taps;
+    const int64_t total = (int64_t)M * Co;           // M = taps * C partial rows
+    const int64_t plane = (int64_t)M * ws_ld;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        const int tap = (int)(i % taps);
-        const int64_t t2 = i / taps;
-        const int c = (int)(t2 % C);
-        const int co = (int)(t2 / C);
-        const int64_t src = (int64_t)(tap * C + c) * ws_ld + co;
+        const int co = (int)(i % Co);
+        const int m = (int)(i / Co);
+        const int tap = m / C, c = m - tap * C;
+        const float* src = ws + (int64_t)m * ws_ld + co;
         float acc = 0.f;
-        for (int s = 0; s < splits; ++s) acc += ws[(int64_t)s * M * ws_ld + src];
-        dw[i] = acc;
+        int sp = 0;
+        for (; sp + 8 <= splits; sp += 8) {
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = __ldg(src + (int64_t)(sp + j) * plane);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc += v[j];
+        }
+        for (; sp < splits; ++sp) acc += __ldg(src + (int64_t)sp * plane);
+        dw[((int64_t)co * C + c) * taps + tap] = acc;
     }
 }
 

@@ -610,6 +610,13 @@ int launch_simple(cudaError_t e, const char* what) {
 // NCHW view -> NHWC copy with Cp = round_up(C, 4) channels.
 int to_nhwc(const float* src, const int64_t (&sv)[4], float* dst, int N, int C, int H, int W, cudaStream_t st) {
     const int Cp = (C + 3) & ~3;
+    const int64_t HW = (int64_t)H * W;
+    if (sv[3] == 1 && sv[2] == W && HW % 4 == 0 && sv[1] % 4 == 0 && sv[0] % 4 == 0 && aligned16(src) &&
+        HW <= INT32_MAX && (HW + 255) / 256 <= INT32_MAX && (Cp + 31) / 32 <= 65535) {
+        dim3 grid((unsigned)((HW + 255) / 256), (unsigned)((Cp + 31) / 32), (unsigned)std::min(N, 65535));
+        mt::convt::nchw_to_nhwc_flat_kernel<<<grid, 256, 0, st>>>(src, sv[0], sv[1], dst, N, C, (int)HW, Cp);
+        return launch_simple(cudaGetLastError(), "nchw_to_nhwc");
+    }
     if ((W + 63) / 64 > 65535 || (Cp + 63) / 64 > 65535) return fail(MT_EUNSUPPORTED, "nchw_to_nhwc: extent");
     dim3 grid((W + 63) / 64, (Cp + 63) / 64, (unsigned)std::min(N * H, 65535));
     mt::convt::nchw_to_nhwc_kernel<<<grid, 256, 0, st>>>(src, sv[0], sv[1], sv[2], sv[3], dst, N, C, H, W, Cp);
@@ -721,7 +728,7 @@ bool halo_enabled() {
 // Fills the tile geometry and shared-memory layout; false when the halo does not fit.
 // The weight stage takes the largest G (a divisor of the tap count) for which two
 // stages fit beside two halo slots.
-bool plan_halo(int Ho, int Wo, int kh, int kw, int Ncol, bool x3, int& bn, mt::convh::HaloParams& hp,
+bool plan_halo(int Ho, int Wo, int Cin, int kh, int kw, int Ncol, bool x3, int& bn, mt::convh::HaloParams& hp,
                uint32_t& smem) {
     const int TXv = std::min(Wo, 128 - (kw - 1));
     if (TXv < 1 || kh < 1 || kw < 1) return false;
@@ -744,7 +751,11 @@ bool plan_halo(int Ho, int Wo, int kh, int kw, int Ncol, bool x3, int& bn, mt::c
         if (taps % g == 0 && a_total + 2 * (uint64_t)g * mult * bmat <= budget) { G = g; break; }
     if (G == 0) return false;
     const uint64_t bstage = (uint64_t)G * mult * bmat;
-    const int b_stages = (int)std::min<uint64_t>(mt::convh::kMaxBStages, (budget - a_total) / bstage);
+    int b_stages = (int)std::min<uint64_t>(mt::convh::kMaxBStages, (budget - a_total) / bstage);
+    // Resident weights: one N tile, and every (channel block, tap group) stage fits.
+    const int cblocks = (Cin + 31) / 32, all_stages = cblocks * (taps / G);
+    hp.b_resident = (Ncol <= bn && all_stages <= mt::convh::kMaxBStages && all_stages <= b_stages) ? 1 : 0;
+    if (hp.b_resident) b_stages = all_stages;
     hp.P = P; hp.TXv = TXv; hp.TY = TY; hp.HR = HR;
     hp.G = G; hp.tgroups = taps / G;
     hp.a_slots = a_slots; hp.b_stages = b_stages;
@@ -801,7 +812,7 @@ int run_fwd_halo(const float* act, int N, int Hin, int Win, int Cin, const float
     }
     path = std::string("tma_halo bn=") + std::to_string(bn) + " tile=" + std::to_string(hp.TY) + "x" +
            std::to_string(hp.TXv) + " pitch=" + std::to_string(hp.P) + " taps/stage=" + std::to_string(hp.G) +
-           " bstages=" + std::to_string(hp.b_stages);
+           " bstages=" + std::to_string(hp.b_stages) + (hp.b_resident ? " resident" : "");
     return rc;
 }
 
@@ -818,7 +829,7 @@ int run_fwd_tma(const float* act, int N, int Hin, int Win, int Cin, const float*
         memset(&plan, 0, sizeof plan);
         int bn = 0;
         uint32_t smem = 0;
-        if (plan_halo(Ho, Wo, kh, kw, Ncol, x3, bn, plan, smem)) {
+        if (plan_halo(Ho, Wo, Cin, kh, kw, Ncol, x3, bn, plan, smem)) {
             int rc = reorder_w(w, sw, wt, Co, Ci, kh, kw, dgrad, st, x3);
             if (rc) return rc;
             return run_fwd_halo(act, N, Hin, Win, Cin, wt, Ncol, kh, kw, pad, out, Ho, Wo, bias, x3, st, sms, plan,
