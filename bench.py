@@ -446,30 +446,39 @@ def run_gpu(args, rank, world, local_rank):
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
+
     # Single GPU: the K timed steps are captured once into a CUDA graph and replayed, so
     # host launch overhead is not timed (the kernels are capture-safe). Several GPUs: eager
-    # launches (the cross-GPU flag barrier takes a fresh epoch every step).
-    graph = None
-    n0 = engine.launch_count()
-    if world == 1:
+    # launches (the cross-GPU flag barrier takes a fresh epoch every step). Every mode
+    # (the headline one and the extras) is timed this same way.
+    def capture(mode, steps):
+        if world > 1:
+            return None, 0
+        n0 = engine.launch_count()
         try:
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
-                for _ in range(args.steps):
-                    wl.step(args.mode)
-            graph.replay()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for _ in range(steps):
+                    wl.step(mode)
+            g.replay()
             torch.cuda.synchronize()
+            return g, engine.launch_count() - n0
         except Exception as exc:   # capture is an optimisation of the timing only
             print(f"graph capture failed ({exc}); timing eager launches", file=sys.stderr)
-            graph = None
-    launches = engine.launch_count() - n0
-    with ClockSampler(local_rank) as clk:
+            return None, 0
+
+    def timed(mode, steps, graph):
+        """(seconds for `steps` steps, kernel launches per timed region)."""
         if graph is not None:
-            t = time_steps(graph.replay, 1, stream)
-        else:
-            n0 = engine.launch_count()
-            t = time_steps(lambda: wl.step(args.mode), args.steps, stream)
-            launches = engine.launch_count() - n0
+            return time_steps(graph.replay, 1, stream), None
+        n0 = engine.launch_count()
+        return time_steps(lambda: wl.step(mode), steps, stream), engine.launch_count() - n0
+
+    graph, launches = capture(args.mode, args.steps)
+    with ClockSampler(local_rank) as clk:
+        t, eager_launches = timed(args.mode, args.steps, graph)
+    if eager_launches is not None:
+        launches = eager_launches
     t = max_over_ranks(t)
     path = engine.last_path()
     tflops = wl.flops * args.steps / t / 1e12
@@ -481,11 +490,14 @@ def run_gpu(args, rank, world, local_rank):
             if m == args.mode:
                 continue
             s = 3 if m == "strict" else max(5, args.steps // 2)
-            wl.step(m)
+            for _ in range(max(1, min(args.warmup, 3))):
+                wl.step(m)
             torch.cuda.synchronize()
             if dist:
                 dist.barrier()
-            tm = max_over_ranks(time_steps(lambda: wl.step(m), s, stream))
+            gm, _ = capture(m, s)
+            tm = max_over_ranks(timed(m, s, gm)[0])
+            del gm
             extras[m] = {"value": wl.flops * s / tm / 1e12, "ms_per_step": tm / s * 1e3}
 
         # End to end through the public API from pinned host buffers: H2D of this rank's

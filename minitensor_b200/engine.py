@@ -82,6 +82,19 @@ def lib() -> ctypes.CDLL:
     L.mt_conv2d_wgrad.restype = ctypes.c_int
     L.mt_conv2d_wgrad_workspace_bytes.argtypes = [P, P, P, u64, u64, ctypes.c_int]
     L.mt_conv2d_wgrad_workspace_bytes.restype = ctypes.c_size_t
+    L.mt_conv2d_wgrad_noalloc.argtypes = [P, P, P, u64, u64, ctypes.c_int, vp]
+    L.mt_conv2d_wgrad_noalloc.restype = ctypes.c_int
+    # multi-GPU entry points (used by sharded.py)
+    L.mt_ipc_get_handle.argtypes = [vp, vp, ctypes.POINTER(u64)]
+    L.mt_ipc_get_handle.restype = ctypes.c_int
+    L.mt_ipc_open.argtypes = [vp, u64, ctypes.POINTER(vp)]
+    L.mt_ipc_open.restype = ctypes.c_int
+    L.mt_ipc_close.argtypes = [vp, u64]
+    L.mt_ipc_close.restype = ctypes.c_int
+    L.mt_gemm_multi.argtypes = [P, P, P, vp, ctypes.c_int, vp, ctypes.c_int, ctypes.c_int, vp]
+    L.mt_gemm_multi.restype = ctypes.c_int
+    L.mt_peer_barrier.argtypes = [vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, u64, vp]
+    L.mt_peer_barrier.restype = ctypes.c_int
     L.mt_set_default_mode.argtypes = [ctypes.c_int]
     L.mt_set_default_mode.restype = ctypes.c_int
     L.mt_get_default_mode.restype = ctypes.c_int

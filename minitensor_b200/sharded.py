@@ -35,9 +35,6 @@ class PeerTensor:
 
     def __init__(self, t: torch.Tensor, rank: int, world: int, group=None):
         L = engine.lib()
-        L.mt_ipc_get_handle.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint64)]
-        L.mt_ipc_open.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p)]
-        L.mt_ipc_close.argtypes = [ctypes.c_void_p, ctypes.c_uint64]
         self.t = t   # keep the local allocation alive while peers map it
         self.rank, self.world = rank, world
         h = (ctypes.c_char * 64)()
@@ -84,14 +81,6 @@ class ShardedGemm:
         self._flag_peers = PeerTensor(self.flags, self.rank, self.world, group)
         self._flag_arr = (ctypes.c_void_p * self.world)(*self._flag_peers.ptrs)
         self._bound = {}
-        L = engine.lib()
-        P = ctypes.POINTER(engine.MtTensor)
-        L.mt_gemm_multi.argtypes = [P, P, P, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
-                                    ctypes.c_int, ctypes.c_void_p]
-        L.mt_gemm_multi.restype = ctypes.c_int
-        L.mt_peer_barrier.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_uint64,
-                                      ctypes.c_void_p]
-        L.mt_peer_barrier.restype = ctypes.c_int
 
     def _peers(self, C: torch.Tensor) -> PeerTensor:
         key = (C.data_ptr(), C.numel())

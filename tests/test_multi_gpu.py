@@ -46,6 +46,23 @@ def test_multi_destination_epilogue(eng, port, mode):
         assert np.array_equal(host(e), c)
 
 
+@pytest.mark.parametrize("mode", ["tf32", "tf32x3"])
+def test_multi_destination_epilogue_pair_kernel(eng, port, mode):
+    """The CTA-pair kernel (>= 74 tiles of 256 x 256) writing every tile to 4 outputs."""
+    M, K, N = 2304, 160, 2336
+    A = inputs.uniform((M, K), -1, 1, 75)
+    B = inputs.uniform((K, N), -1, 1, 76)
+    C = torch.empty(M, N, device="cuda")
+    extras = [torch.full((M, N), -7.0, device="cuda") for _ in range(3)]
+    _multi(dev(A), dev(B), C, extras, mode)
+    assert eng.last_path().startswith("umma_pair_" + mode), eng.last_path()
+    c = host(C)
+    rows = [0, 127, 128, 255, 256, 2047, 2048, M - 1]
+    check(mode, c[rows], port.matmul_strided(A[rows], B), absmm(A[rows], B), K, "pair local")
+    for e in extras:
+        assert np.array_equal(host(e), c)
+
+
 def test_column_shard_into_wide_buffers(eng, port):
     # The sharded layout on one GPU: 4 "ranks" write their column blocks into 4 full-width Cs.
     M, K, N, world = 256, 192, 512, 4
@@ -88,13 +105,13 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _sharded_worker(rank, world, port, out, mode):
+def _sharded_worker(rank, world, port, out, mode, shape=(1024, 1536, 512)):
     import torch.distributed as dist
     from minitensor_b200 import sharded
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
-    M, N, K = 1024, 1536, 512
+    M, N, K = shape
     A = inputs.uniform((M, K), -1, 1, 81)
     B = inputs.uniform((K, N), -1, 1, 82)
     plan = sharded.ShardedGemm(M, N, K, rank, world, timeout_s=5.0)
@@ -111,13 +128,19 @@ def _sharded_worker(rank, world, port, out, mode):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("mode", ["tf32x3", "strict"])
-def test_sharded_gemm_two_gpus(eng, port, tmp_path, mode):
+@pytest.mark.parametrize("mode,shape", [("tf32x3", (1024, 1536, 512)), ("strict", (1024, 1536, 512)),
+                                        ("tf32", (2304, 4672, 128)), ("tf32x3", (2304, 4672, 128))])
+def test_sharded_gemm_two_gpus(eng, port, tmp_path, mode, shape):
+    """Column shards on two GPUs, every rank ending with the full C; the (2304, 4672, 128)
+    cases give each rank >= 74 tiles of 256 x 256, i.e. the CTA-pair kernel with the
+    peer-store epilogue."""
     import torch.multiprocessing as mp
     world = 2
-    mp.spawn(_sharded_worker, args=(world, _free_port(), str(tmp_path), mode), nprocs=world, join=True)
-    A = inputs.uniform((1024, 512), -1, 1, 81)
-    B = inputs.uniform((512, 1536), -1, 1, 82)
-    ref = port.matmul(A, B)
+    mp.spawn(_sharded_worker, args=(world, _free_port(), str(tmp_path), mode, shape), nprocs=world, join=True)
+    M, N, K = shape
+    A = inputs.uniform((M, K), -1, 1, 81)
+    B = inputs.uniform((K, N), -1, 1, 82)
+    rows = sorted(set([0, 127, 128, 255, 256, M // 2, M - 1]))
+    ref = port.matmul_strided(A[rows], B)
     for r in range(world):
-        check(mode, np.load(tmp_path / f"c{r}.npy"), ref, absmm(A, B), 512, f"rank {r}")
+        check(mode, np.load(tmp_path / f"c{r}.npy")[rows], ref, absmm(A[rows], B), K, f"rank {r}")
