@@ -71,8 +71,9 @@ struct Cfg {
     static constexpr int NUM_WARPS = X3 ? 10 : 6;
     static constexpr int THREADS = NUM_WARPS * 32;
     static constexpr uint32_t RING_BYTES = STAGE_BYTES * STAGES * (X3 ? 2 : 1);
+    static constexpr uint32_t EPI_BYTES = 4 * 4096;                // epilogue staging, 4 KB per warp
     static constexpr uint32_t BAR_BYTES = 8 * (3 * STAGES + 4) + 16;
-    static constexpr uint32_t SMEM_BYTES = 1024 + RING_BYTES + BAR_BYTES;
+    static constexpr uint32_t SMEM_BYTES = 1024 + RING_BYTES + EPI_BYTES + BAR_BYTES;
     static constexpr uint32_t CHUNK = 32;                      // MN-major: 32 elements (128 B) per row
     // MN-major: one chunk = BKE k-rows x 128 bytes.
     static constexpr uint32_t MN_CHUNK_BYTES = BKE * 128;
@@ -91,6 +92,35 @@ __device__ __forceinline__ void tile_coords(const Params& p, long long t, int& b
     long long in_group = r % ((long long)G * p.tiles_n);
     mb = first_m + (int)(in_group % gsize);
     nb = (int)(in_group / gsize);
+}
+
+// Stores one warp's 32 x 32 block of C (lane i holds row m0w + i, columns n0 .. n0+31 in
+// v) to every destination as whole 128-byte rows: the block passes through a 4 KB shared
+// tile (16-byte chunks XOR-swizzled by row, conflict-free both ways) so that each store
+// instruction covers 4 complete rows instead of 16 bytes of 32 rows. Over NVLink this turns
+// 32 partial-line writes per instruction into 4 full-line ones. Warp-collective; rows at or
+// past M are skipped. `base` = offset of row 0 (batch and split already applied).
+__device__ __forceinline__ void store_block_lines(float4* stage, const float (&v)[32], int lane, const Params& p,
+                                                  int64_t base, int m0w, int n0) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+        stage[lane * 8 + (j ^ (lane & 7))] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    __syncwarp();
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const int r = 4 * k + (lane >> 3), c = lane & 7;
+        const float4 x = stage[r * 8 + (c ^ (r & 7))];
+        const int m = m0w + r;
+        if (m < p.M) {
+            const int64_t off = base + (int64_t)m * p.sc_m + n0 + 4 * c;
+#pragma unroll
+            for (int d = 0; d < kMaxDst; ++d) {
+                if (d >= p.ndst) break;
+                *reinterpret_cast<float4*>(p.dst[d] + off) = x;
+            }
+        }
+    }
+    __syncwarp();   // the tile is rewritten by the next block
 }
 
 template <bool MN_MAJOR, int BKE>
@@ -113,7 +143,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* ring = smem;                                      // [STAGES][A|B]
     uint8_t* ring_lo = smem + G::STAGE_BYTES * STAGES;         // X3: [STAGES][Alo|Blo]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + G::RING_BYTES);
+    float4* epi_stage = reinterpret_cast<float4*>(smem + G::RING_BYTES);   // [4 warps][256]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + G::RING_BYTES + G::EPI_BYTES);
     uint64_t* full = bars;                                     // TMA landed
     uint64_t* empty = bars + STAGES;                           // MMA done with stage
     uint64_t* conv = bars + 2 * STAGES;                        // X3: split done
@@ -268,21 +299,17 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                     if (p.epi & 4) x = x > 0.f ? x : 0.f;
                     v[j] = x;
                 }
-                if (m < p.M) {
+                if (p.vec_store && n0 + 32 <= p.N) {
+                    store_block_lines(epi_stage + q * 256, v, lane, p,
+                                      (int64_t)b * p.sc_b + (int64_t)sp * p.split_stride, mb * BM + q * 32, n0);
+                } else if (m < p.M) {
 #pragma unroll
                     for (int d = 0; d < kMaxDst; ++d) {
                         if (d >= p.ndst) break;
                         float* crow = p.dst[d] + row_off;
-                        if (p.vec_store && n0 + 32 <= p.N) {
 #pragma unroll
-                            for (int j = 0; j < 32; j += 4)
-                                *reinterpret_cast<float4*>(crow + n0 + j) =
-                                    make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-                        } else {
-#pragma unroll
-                            for (int j = 0; j < 32; ++j)
-                                if (n0 + j < p.N) crow[n0 + j] = v[j];
-                        }
+                        for (int j = 0; j < 32; ++j)
+                            if (n0 + j < p.N) crow[n0 + j] = v[j];
                     }
                 }
             }

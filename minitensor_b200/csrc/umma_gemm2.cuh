@@ -48,8 +48,9 @@ struct Cfg {
     static constexpr int NUM_WARPS = X3 ? 10 : 6;
     static constexpr int THREADS = NUM_WARPS * 32;
     static constexpr uint32_t RING_BYTES = STAGE_BYTES * STAGES * (X3 ? 2 : 1);
+    static constexpr uint32_t EPI_BYTES = 4 * 4096;                // epilogue staging, 4 KB per warp
     static constexpr uint32_t BAR_BYTES = 8 * (3 * STAGES + 4) + 16;
-    static constexpr uint32_t SMEM_BYTES = 1024 + RING_BYTES + BAR_BYTES;
+    static constexpr uint32_t SMEM_BYTES = 1024 + RING_BYTES + EPI_BYTES + BAR_BYTES;
     static constexpr uint32_t CHUNK = 32;
     static constexpr uint32_t MN_CHUNK_BYTES = BKE * 128;
     static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "pair TMEM allocation must be a power of two");
@@ -73,7 +74,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* ring = smem;
     uint8_t* ring_lo = smem + G::STAGE_BYTES * STAGES;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + G::RING_BYTES);
+    float4* epi_stage = reinterpret_cast<float4*>(smem + G::RING_BYTES);   // [4 warps][256]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + G::RING_BYTES + G::EPI_BYTES);
     uint64_t* full = bars;
     uint64_t* empty = bars + STAGES;
     uint64_t* conv = bars + 2 * STAGES;
@@ -242,21 +244,18 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                     if (p.epi & 4) x = x > 0.f ? x : 0.f;
                     v[j] = x;
                 }
-                if (m < p.M) {
+                if (p.vec_store && n0 + 32 <= p.N) {
+                    umma::store_block_lines(epi_stage + q * 256, v, lane, p,
+                                            (int64_t)b * p.sc_b + (int64_t)sp * p.split_stride,
+                                            mb * BM + (int)rank * BMC + q * 32, n0);
+                } else if (m < p.M) {
 #pragma unroll
                     for (int d = 0; d < umma::kMaxDst; ++d) {
                         if (d >= p.ndst) break;
                         float* crow = p.dst[d] + row_off;
-                        if (p.vec_store && n0 + 32 <= p.N) {
 #pragma unroll
-                            for (int j = 0; j < 32; j += 4)
-                                *reinterpret_cast<float4*>(crow + n0 + j) =
-                                    make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-                        } else {
-#pragma unroll
-                            for (int j = 0; j < 32; ++j)
-                                if (n0 + j < p.N) crow[n0 + j] = v[j];
-                        }
+                        for (int j = 0; j < 32; ++j)
+                            if (n0 + j < p.N) crow[n0 + j] = v[j];
                     }
                 }
             }
