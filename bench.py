@@ -232,7 +232,7 @@ class C1(Workload):
 class C2(Workload):
     name = "c2"
     desc = ("config2: Linear 1024->4096, batch 256: Y = X.W + b (bias fused), dX = dY.W^T and dW = X^T.dY "
-            "read from transposed views, db = 1^T.dY; W [in,out] He-normal seed 42, X, dY ~ N(0,1)")
+            "read from transposed views, db = the column sums of dY; W [in,out] He-normal seed 42, X, dY ~ N(0,1)")
     M, K, N = 256, 1024, 4096
     flops = 3 * 2.0 * M * K * N + 2.0 * M * N
     bytes = 3 * 4.0 * (M * K + K * N + M * N) + 4.0 * (M * N + 2 * N)
@@ -252,7 +252,6 @@ class C2(Workload):
         self.dX = torch.empty(256, 1024, device="cuda")
         self.dW = torch.empty(1024, 4096, device="cuda")
         self.db = torch.empty(1, 4096, device="cuda")
-        self.ones = torch.ones(1, 256, device="cuda")
         self.h2d = [(_pin(X), self.X), (_pin(dY), self.dY)]
         self.d2h = [(self.Y, torch.empty(256, 4096).pin_memory()), (self.dW, torch.empty(1024, 4096).pin_memory())]
 
@@ -261,7 +260,7 @@ class C2(Workload):
         e.gemm(self.X, self.W, self.Y, bias=self.b.reshape(-1), epi=e.EPI_BIAS_COL, mode=mode)
         e.gemm(self.dY, self.W.t(), self.dX, mode=mode)
         e.gemm(self.X.t(), self.dY, self.dW, mode=mode)
-        e.gemm(self.ones, self.dY, self.db, mode="strict")
+        e.sum_rows(self.dY, self.db)
 
     def cpu_sample(self, threads):
         impl, kind = _ref()

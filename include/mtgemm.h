@@ -131,6 +131,14 @@ MT_API int mt_conv2d_backward_weight_gpu(const mt_tensor* dY, const mt_tensor* x
  * sum over n (ascending) of the spatial sum of dY[n,co], the order of :398-418. */
 MT_API int mt_conv2d_backward_bias_gpu(const mt_tensor* dY, const mt_tensor* db, void* stream);
 
+/* out[n] = sum over m of X[m, n] for a 2-D view X [M, N] and a 1-D (or [1, N]) view out:
+ * the axis-0 sum that unbroadcast (include/TensorOps.hpp:1305-1345) applies to the bias
+ * gradient of Linear (forward = matmul(x, W) + bias, include/Module.hpp:112-114). The
+ * reference runs it through its own reduction kernels; this is not one of its nine GPU
+ * entry points. Order: 8 partial sums over rows m = w (mod 8), each ascending, then added
+ * in order w = 0..7 (deterministic). */
+MT_API int mt_sum_rows_gpu(const mt_tensor* X, const mt_tensor* out, void* stream);
+
 /* Explicit-mode variants of the three convolution products. */
 MT_API int mt_conv2d_fwd(const mt_tensor* x, const mt_tensor* w, const mt_tensor* bias, const mt_tensor* y,
                          uint64_t stride, uint64_t padding, int mode, void* stream);

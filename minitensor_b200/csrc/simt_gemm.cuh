@@ -215,5 +215,37 @@ __global__ void fill_epilogue_kernel(GemmProblem p) {
     }
 }
 
+// out[n] = sum over rows m of X[m, n] (the axis-0 sum). One block of 8 warps per 32
+// columns: lane = column, warp w sums rows w, w + 8, ... in ascending order, then thread
+// (0, lane) adds the 8 partial sums in warp order -- a fixed order, so the result is
+// deterministic. X is any 2-D view (strides in elements), out any 1-D view.
+__global__ void __launch_bounds__(256) sum_rows_kernel(const float* __restrict__ x, int64_t sm, int64_t sn, int M,
+                                                       int N, float* __restrict__ out, int64_t so) {
+    __shared__ float part[8][33];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int n = blockIdx.x * 32 + lane;
+    float acc = 0.f;
+    if (n < N) {
+        const float* col = x + (int64_t)n * sn;
+        int m = w;
+        for (; m + 56 < M; m += 64) {          // 8 independent loads in flight
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = __ldg(col + (int64_t)(m + 8 * j) * sm);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc += v[j];
+        }
+        for (; m < M; m += 8) acc += __ldg(col + (int64_t)m * sm);
+    }
+    part[w][lane] = acc;
+    __syncthreads();
+    if (w == 0 && n < N) {
+        float t = part[0][lane];
+#pragma unroll
+        for (int j = 1; j < 8; ++j) t += part[j][lane];
+        out[(int64_t)n * so] = t;
+    }
+}
+
 }  // namespace simt
 }  // namespace mt

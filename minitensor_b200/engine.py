@@ -82,6 +82,8 @@ def lib() -> ctypes.CDLL:
     L.mt_conv2d_wgrad.restype = ctypes.c_int
     L.mt_conv2d_wgrad_workspace_bytes.argtypes = [P, P, P, u64, u64, ctypes.c_int]
     L.mt_conv2d_wgrad_workspace_bytes.restype = ctypes.c_size_t
+    L.mt_sum_rows_gpu.argtypes = [P, P, vp]
+    L.mt_sum_rows_gpu.restype = ctypes.c_int
     L.mt_conv2d_wgrad_noalloc.argtypes = [P, P, P, u64, u64, ctypes.c_int, vp]
     L.mt_conv2d_wgrad_noalloc.restype = ctypes.c_int
     # multi-GPU entry points (used by sharded.py)
@@ -236,15 +238,20 @@ def linear_forward(x, W, bias=None, relu=False, mode=MODE_DEFAULT, stream=None):
 def linear_backward(x, W, dY, mode=MODE_DEFAULT, stream=None):
     """MatmulBackward for Linear (include/Autograd.hpp:124-141): dX = dY @ W^T and
     dW = x^T @ dY, both read through transposed views (no copies), plus the bias gradient
-    db = ones[1,M] @ dY (the reference's unbroadcast sum over rows) as a GEMM."""
+    db = the sum of dY over rows (the reference's unbroadcast of the bias add,
+    include/TensorOps.hpp:1305-1345)."""
     dX = torch.empty_like(x)
     dW = torch.empty_like(W)
     gemm(dY, W.t(), dX, mode=mode, stream=stream)
     gemm(x.t(), dY, dW, mode=mode, stream=stream)
-    ones = torch.ones((1, dY.shape[0]), dtype=torch.float32, device=dY.device)
     db = torch.empty((1, dY.shape[1]), dtype=torch.float32, device=dY.device)
-    gemm(ones, dY, db, mode=STRICT_FP32, stream=stream)
+    sum_rows(dY, db, stream=stream)
     return dX, dW, db
+
+
+def sum_rows(X, out, stream=None):
+    """out[n] = sum over m of X[m, n] (X 2-D, out [N] or [1, N])."""
+    _check(lib().mt_sum_rows_gpu(_ref(view(X)), _ref(view(out)), _stream(stream)))
 
 
 # ---- Conv2D (include/TensorOps.hpp:708-712, :1076-1149) --------------------------------

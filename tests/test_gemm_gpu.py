@@ -109,6 +109,41 @@ def test_config2_linear(eng, port, mode):
     XT = np.ascontiguousarray(X.T)
     dWr = port.matmul_rows(XT, dY, 0, 1024, THREADS)
     check(mode, host(dW), dWr, absmm(XT, dY), 256, "config2 dW (TN)")
+    # db: the sum of dY over the batch (fp32 adds in a fixed order, every mode).
+    db = host(eng.linear_backward(Xd, Wd, dYd, mode=mode)[2]).ravel()
+    ref = dY.astype(np.float64).sum(0)
+    assert np.max(np.abs(db - ref) / np.abs(dY).astype(np.float64).sum(0)) < 1e-6
+
+
+@pytest.mark.parametrize("shape", [(256, 4096), (1, 7), (77, 33), (1000, 65), (0, 5)])
+def test_sum_rows(eng, shape):
+    """out[n] = sum over rows; X read through a transposed view, out a strided [1, N] row."""
+    M, N = shape
+    base = inputs.uniform((N, M), -1, 1, 61)          # X = base^T: column stride 1 in memory rows
+    X = dev(base).t()
+    out_buf = torch.full((3, N), 5.0, device="cuda")
+    out = out_buf[1:2]                                 # [1, N] window of a larger buffer
+    eng.sum_rows(X, out)
+    first = host(out).ravel()
+    eng.sum_rows(X, out)
+    assert np.array_equal(host(out).ravel(), first)   # deterministic
+    ref = base.T.astype(np.float64).sum(0)
+    bound = np.abs(base.T).astype(np.float64).sum(0) + 1e-30
+    assert np.max(np.abs(first - ref) / bound) < 1e-6
+    assert np.all(host(out_buf)[[0, 2]] == 5.0)        # neighbours untouched
+
+
+@pytest.mark.parametrize("mode", ["tf32", "tf32x3"])
+def test_split_k_ragged_with_bias(eng, port, mode):
+    """Few output tiles and a long K: split-K partials, ordered sum, fused bias epilogue."""
+    M, N, K = 200, 136, 5000
+    A = inputs.uniform((M, K), -1, 1, 63)
+    B = inputs.uniform((K, N), -1, 1, 64)
+    bn = inputs.uniform((N,), -1, 1, 65)
+    C = torch.empty(M, N, device="cuda")
+    eng.gemm(dev(A), dev(B), C, bias=dev(bn), epi=eng.EPI_BIAS_COL, mode=mode)
+    assert "splitk=" in eng.last_path(), eng.last_path()
+    check(mode, host(C), port.matmul(A, B) + bn, absmm(A, B) + np.abs(bn), K, "split-K")
 
 
 @pytest.mark.parametrize("mode", MODES)
