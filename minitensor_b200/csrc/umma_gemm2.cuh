@@ -244,10 +244,20 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                     if (p.epi & 4) x = x > 0.f ? x : 0.f;
                     v[j] = x;
                 }
-                if (p.vec_store && n0 + 32 <= p.N) {
+                if (p.vec_store && n0 + 32 <= p.N && p.ndst > 1) {
+                    // several destinations (peers over NVLink): whole-row stores
                     umma::store_block_lines(epi_stage + q * 256, v, lane, p,
                                             (int64_t)b * p.sc_b + (int64_t)sp * p.split_stride,
                                             mb * BM + (int)rank * BMC + q * 32, n0);
+                } else if (p.vec_store && n0 + 32 <= p.N) {
+                    // one local destination: straight from registers (the shared-memory
+                    // round trip costs more than it saves when the epilogue is the bound)
+                    if (m < p.M) {
+                        float* crow = p.dst[0] + row_off;
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4)
+                            *reinterpret_cast<float4*>(crow + n0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                    }
                 } else if (m < p.M) {
 #pragma unroll
                     for (int d = 0; d < umma::kMaxDst; ++d) {
