@@ -44,6 +44,8 @@ def parse():
     ap.add_argument("--no-extras", action="store_true", help="skip the other modes, e2e and CPU legs")
     ap.add_argument("--size", type=int, default=8192,
                     help="c5 square size; 8192 is the benchmark, smaller sizes are profiling cases")
+    ap.add_argument("--gather", default="auto", choices=["auto", "epilogue", "copy"],
+                    help="N>1: how shards reach the peers (auto = epilogue: TMA stores from the GEMM epilogue)")
     return ap.parse_args()
 
 
@@ -157,9 +159,10 @@ class Workload:
 class C5(Workload):
     name = "c5"
 
-    def __init__(self, gpu=True, n=8192, rank=0, world=1):
+    def __init__(self, gpu=True, n=8192, rank=0, world=1, gather="auto"):
         from minitensor_b200 import inputs
         self.n, self.rank, self.world = n, rank, world
+        self.gather = None if gather == "auto" else gather
         self.desc = (f"config5: C[{n},{n}] = A[{n},{n}] . B[{n},{n}], A,B ~ U[-1,1] seed 1" if n == 8192
                      else f"profiling case: config5 generator at {n}^3 (not the benchmark shape)")
         self.flops = 2.0 * n ** 3
@@ -178,7 +181,7 @@ class C5(Workload):
             Bsrc = self.B_h
         else:
             from minitensor_b200 import sharded
-            self.plan = sharded.ShardedGemm(n, n, n, self.rank, self.world)
+            self.plan = sharded.ShardedGemm(n, n, n, self.rank, self.world, gather=self.gather)
             Bsrc = np.ascontiguousarray(self.B_h[:, self.plan.n0:self.plan.n1])
         self.B = _cuda(Bsrc)
         self.h2d = [(_pin(self.A_h), self.A), (_pin(Bsrc), self.B)]
@@ -370,7 +373,7 @@ class C4(Workload):
 
 def make_workload(args, rank, world, gpu=True):
     if args.workload == "c5":
-        return C5(gpu, args.size, rank, world)
+        return C5(gpu, args.size, rank, world, getattr(args, "gather", "auto"))
     if world > 1 and gpu:
         raise SystemExit("workloads c1-c4 are single-GPU problems (replicas only)")
     return {"c1": C1, "c2": C2, "c3": C3, "c4": C4}[args.workload](gpu)
@@ -561,7 +564,9 @@ def run_gpu(args, rank, world, local_rank):
         "config": {"workload": wl.desc, "mode": args.mode,
                    "timing": "one CUDA-graph replay of the K captured steps" if graph is not None
                              else "K eager steps",
-                   "parallelism": f"N-column shards x{world}" if world > 1 else "single GPU",
+                   "parallelism": (f"N-column shards x{world}, all-gather by "
+                                   + ("epilogue peer stores" if wl.plan.gather == "epilogue" else "copy engines"))
+                                  if world > 1 else "single GPU",
                    "l2": "inputs larger than the 126 MB L2, no flush" if wl.name == "c5" else
                          "steps back to back without an L2 flush (working set fits L2)"},
         "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "modes": extras,

@@ -195,6 +195,12 @@ MT_API int mt_gemm_multi(const mt_tensor* A, const mt_tensor* B, const mt_tensor
  * the device status word (mt_device_status) instead of hanging. */
 MT_API int mt_peer_barrier(int* const* flags, int rank, int world, int epoch, uint64_t timeout_ns, void* stream);
 
+/* Stream-ordered 2-D copy of `rows` rows of `width_bytes` bytes (row pitches dpitch /
+ * spitch bytes) from src to dst, by the copy engines -- dst may be a peer-mapped pointer,
+ * which makes this a push over NVLink without SM involvement. One cudaMemcpy2DAsync. */
+MT_API int mt_copy_rows_async(void* dst, uint64_t dpitch, const void* src, uint64_t spitch, uint64_t width_bytes,
+                              uint64_t rows, void* stream);
+
 /* ---- process settings and diagnostics ---------------------------------------------- */
 
 MT_API int mt_set_default_mode(int mode);   /* returns the previous default */

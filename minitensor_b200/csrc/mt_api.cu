@@ -201,8 +201,8 @@ int launch_simt(const GemmProblem& p, cudaStream_t st) {
 }
 
 template <int BN, int BKE, bool AMN, bool BMN, bool X3, int STAGES>
-int launch_umma_inst(const CUtensorMap& ta, const CUtensorMap& tb, const mt::umma::Params& up, int grid,
-                     cudaStream_t st) {
+int launch_umma_inst(const CUtensorMap& ta, const CUtensorMap& tb, const mt::umma::DstMaps& dm,
+                     const mt::umma::Params& up, int grid, cudaStream_t st) {
     using G = mt::umma::Cfg<BN, BKE, X3, STAGES>;
     auto kern = mt::umma::gemm_kernel<BN, BKE, AMN, BMN, X3, STAGES>;
     static std::atomic<uint64_t> attr_set_mask{0};
@@ -214,7 +214,7 @@ int launch_umma_inst(const CUtensorMap& ta, const CUtensorMap& tb, const mt::umm
         if (e != cudaSuccess) return cuda_fail(e, "umma gemm: set smem attribute");
         attr_set_mask.fetch_or(bit);
     }
-    kern<<<grid, G::THREADS, G::SMEM_BYTES, st>>>(ta, tb, up);
+    kern<<<grid, G::THREADS, G::SMEM_BYTES, st>>>(ta, tb, dm, up);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess && e != cudaErrorStreamCaptureUnsupported) return cuda_fail(e, "umma gemm launch");
     g_launches.fetch_add(1);
@@ -223,8 +223,8 @@ int launch_umma_inst(const CUtensorMap& ta, const CUtensorMap& tb, const mt::umm
 
 // CTA-pair kernel: grid = 2 x (clusters that fit at once, capped by the tile count).
 template <int BN, int BKE, bool AMN, bool BMN, bool X3, int STAGES>
-int launch_pair_inst(const CUtensorMap& ta, const CUtensorMap& tb, const mt::umma::Params& up, int sms,
-                     cudaStream_t st) {
+int launch_pair_inst(const CUtensorMap& ta, const CUtensorMap& tb, const mt::umma::DstMaps& dm,
+                     const mt::umma::Params& up, int sms, cudaStream_t st) {
     using G = mt::umma2::Cfg<BN, BKE, X3, STAGES>;
     auto kern = mt::umma2::gemm_pair_kernel<BN, BKE, AMN, BMN, X3, STAGES>;
     static std::atomic<uint64_t> attr_set_mask{0};
@@ -253,7 +253,7 @@ int launch_pair_inst(const CUtensorMap& ta, const CUtensorMap& tb, const mt::umm
         attr_set_mask.fetch_or(bit);
     }
     const int clusters = (int)std::min<long long>(up.num_units, (long long)max_clusters[dev & 63].load());
-    kern<<<2 * clusters, G::THREADS, G::SMEM_BYTES, st>>>(ta, tb, up);
+    kern<<<2 * clusters, G::THREADS, G::SMEM_BYTES, st>>>(ta, tb, dm, up);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess && e != cudaErrorStreamCaptureUnsupported) return cuda_fail(e, "umma pair gemm launch");
     g_launches.fetch_add(1);
@@ -265,6 +265,15 @@ int launch_pair_inst(const CUtensorMap& ta, const CUtensorMap& tb, const mt::umm
 bool pair_enabled() {
     static int v = [] {
         const char* e = std::getenv("MT_GEMM_PAIR");
+        return (e && e[0] == '0') ? 0 : 1;
+    }();
+    return v != 0;
+}
+
+// TMA-store epilogue for several destinations; MT_TMA_EPILOGUE=0 keeps the SM-store one.
+bool tma_epilogue_enabled() {
+    static int v = [] {
+        const char* e = std::getenv("MT_TMA_EPILOGUE");
         return (e && e[0] == '0') ? 0 : 1;
     }();
     return v != 0;
@@ -374,19 +383,32 @@ int launch_umma(const GemmProblem& p, bool x3, cudaStream_t st, float* const* ex
     } else {
         up.split_stride = 0;
     }
+    // Several destinations (a sharded GEMM's peers): TMA tensor stores from the epilogue,
+    // one map per destination over the same {N, M, batch} view.
+    mt::umma::DstMaps dm;
+    memset(&dm, 0, sizeof dm);
+    up.tma_multi = 0;
+    if (splits == 1 && up.ndst > 1 && up.vec_store && tma_epilogue_enabled()) {
+        const uint64_t s1 = (uint64_t)p.sc_m * 4;
+        const uint64_t s2 = p.batch > 1 ? (uint64_t)p.sc_b * 4 : round16(s1 * (uint64_t)p.M);
+        bool ok = true;
+        for (int d = 0; d < up.ndst && ok; ++d)
+            ok = encode_3d(&dm.m[d], up.dst[d], (uint64_t)p.N, (uint64_t)p.M, (uint64_t)p.batch, s1, s2, 32, 32, 128);
+        up.tma_multi = ok ? 1 : 0;
+    }
     const int grid = (int)std::min<long long>(up.num_units, (long long)di.sms);
 
     int rc;
 #define MT_UMMA_DISPATCH(BN_, BKE_, X3_, ST_)                                                       \
-    if (a_mn == 0 && b_mn == 0) rc = launch_umma_inst<BN_, BKE_, false, false, X3_, ST_>(ta, tb, up, grid, st); \
-    else if (a_mn == 0 && b_mn == 1) rc = launch_umma_inst<BN_, BKE_, false, true, X3_, ST_>(ta, tb, up, grid, st); \
-    else if (a_mn == 1 && b_mn == 0) rc = launch_umma_inst<BN_, BKE_, true, false, X3_, ST_>(ta, tb, up, grid, st); \
-    else rc = launch_umma_inst<BN_, BKE_, true, true, X3_, ST_>(ta, tb, up, grid, st);
+    if (a_mn == 0 && b_mn == 0) rc = launch_umma_inst<BN_, BKE_, false, false, X3_, ST_>(ta, tb, dm, up, grid, st); \
+    else if (a_mn == 0 && b_mn == 1) rc = launch_umma_inst<BN_, BKE_, false, true, X3_, ST_>(ta, tb, dm, up, grid, st); \
+    else if (a_mn == 1 && b_mn == 0) rc = launch_umma_inst<BN_, BKE_, true, false, X3_, ST_>(ta, tb, dm, up, grid, st); \
+    else rc = launch_umma_inst<BN_, BKE_, true, true, X3_, ST_>(ta, tb, dm, up, grid, st);
 #define MT_PAIR_DISPATCH(BKE_, X3_, ST_)                                                                   \
-    if (a_mn == 0 && b_mn == 0) rc = launch_pair_inst<256, BKE_, false, false, X3_, ST_>(ta, tb, up, di.sms, st); \
-    else if (a_mn == 0 && b_mn == 1) rc = launch_pair_inst<256, BKE_, false, true, X3_, ST_>(ta, tb, up, di.sms, st); \
-    else if (a_mn == 1 && b_mn == 0) rc = launch_pair_inst<256, BKE_, true, false, X3_, ST_>(ta, tb, up, di.sms, st); \
-    else rc = launch_pair_inst<256, BKE_, true, true, X3_, ST_>(ta, tb, up, di.sms, st);
+    if (a_mn == 0 && b_mn == 0) rc = launch_pair_inst<256, BKE_, false, false, X3_, ST_>(ta, tb, dm, up, di.sms, st); \
+    else if (a_mn == 0 && b_mn == 1) rc = launch_pair_inst<256, BKE_, false, true, X3_, ST_>(ta, tb, dm, up, di.sms, st); \
+    else if (a_mn == 1 && b_mn == 0) rc = launch_pair_inst<256, BKE_, true, false, X3_, ST_>(ta, tb, dm, up, di.sms, st); \
+    else rc = launch_pair_inst<256, BKE_, true, true, X3_, ST_>(ta, tb, dm, up, di.sms, st);
     if (pair) {
         if (!x3) { MT_PAIR_DISPATCH(32, false, 6) }
         else { MT_PAIR_DISPATCH(16, true, 6) }
@@ -1532,6 +1554,17 @@ MT_API int mt_peer_barrier(int* const* flags, int rank, int world, int epoch, ui
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess && e != cudaErrorStreamCaptureUnsupported) return cuda_fail(e, "peer barrier launch");
     g_launches.fetch_add(1);
+    return MT_OK;
+}
+
+MT_API int mt_copy_rows_async(void* dst, uint64_t dpitch, const void* src, uint64_t spitch, uint64_t width_bytes,
+                              uint64_t rows, void* stream) {
+    if (rows == 0 || width_bytes == 0) return MT_OK;
+    if (!dst || !src) return fail(MT_EINVAL, "copy_rows_async: null pointer");
+    if (dpitch < width_bytes || spitch < width_bytes) return fail(MT_EINVAL, "copy_rows_async: pitch < width");
+    cudaError_t e = cudaMemcpy2DAsync(dst, dpitch, src, spitch, width_bytes, rows, cudaMemcpyDeviceToDevice,
+                                      static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "copy_rows_async");
     return MT_OK;
 }
 

@@ -51,6 +51,15 @@ struct Params {
     int splits;
     int64_t split_stride;
     long long num_units;        // num_tiles * splits
+    // Several destinations: the epilogue hands each warp's 32 x 32 block to the TMA engine,
+    // one tensor store per destination (maps in DstMaps, C as {N, M, batch}, box {32, 32, 1},
+    // 128-byte swizzle). SM stores to peer memory top out far below the link rate.
+    int tma_multi;
+};
+
+// Tensor maps of the ndst destinations (same view, different base pointers).
+struct DstMaps {
+    CUtensorMap m[kMaxDst];
 };
 
 // k-blocks of split `sp`: a near-equal contiguous share of [0, kblocks).
@@ -71,7 +80,7 @@ struct Cfg {
     static constexpr int NUM_WARPS = X3 ? 10 : 6;
     static constexpr int THREADS = NUM_WARPS * 32;
     static constexpr uint32_t RING_BYTES = STAGE_BYTES * STAGES * (X3 ? 2 : 1);
-    static constexpr uint32_t EPI_BYTES = 4 * 4096;                // epilogue staging, 4 KB per warp
+    static constexpr uint32_t EPI_BYTES = 4 * 8192;                // epilogue staging, 2 x 4 KB per warp
     static constexpr uint32_t BAR_BYTES = 8 * (3 * STAGES + 4) + 16;
     static constexpr uint32_t SMEM_BYTES = 1024 + RING_BYTES + EPI_BYTES + BAR_BYTES;
     static constexpr uint32_t CHUNK = 32;                      // MN-major: 32 elements (128 B) per row
@@ -123,6 +132,33 @@ __device__ __forceinline__ void store_block_lines(float4* stage, const float (&v
     __syncwarp();   // the tile is rewritten by the next block
 }
 
+// Hands one warp's 32 x 32 block (lane i = row m0w + i, columns n0..n0+31 in v) to the TMA
+// engine for every destination: the block goes into a 4 KB shared buffer in the 128-byte
+// swizzled layout of the maps (16-byte chunk j of row r at j ^ (r & 7)), then lane 0
+// issues one tensor store per destination; TMA clips rows / columns past C's edge, and a
+// block wholly past the edge is skipped (no store starts outside C). Two buffers per warp
+// alternate; `seq` counts the warp's blocks, and a buffer is rewritten only after the
+// stores that read it two blocks earlier are done reading.
+__device__ __forceinline__ void store_block_tma(const DstMaps& dm, int ndst, float4* bufs, int& seq,
+                                                const float (&v)[32], int lane, int n0, int m0w, int bz, int M, int N) {
+    if (m0w >= M || n0 >= N) return;
+    float4* buf = bufs + (seq & 1) * 256;
+    if (seq >= 2) {
+        if (lane == 0) bulk_wait_read<1>();
+        __syncwarp();
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+        buf[lane * 8 + (j ^ (lane & 7))] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+        for (int d = 0; d < ndst; ++d) tma_store_3d(&dm.m[d], smem_u32(buf), n0, m0w, bz);
+        bulk_commit();
+    }
+    ++seq;
+}
+
 template <bool MN_MAJOR, int BKE>
 __device__ __forceinline__ uint64_t operand_desc(uint32_t base, int kstep) {
     if (MN_MAJOR) {
@@ -137,13 +173,14 @@ __device__ __forceinline__ uint64_t operand_desc(uint32_t base, int kstep) {
 
 template <int BN, int BKE, bool A_MN, bool B_MN, bool X3, int STAGES>
 __global__ void __launch_bounds__(Cfg<BN, BKE, X3, STAGES>::THREADS, 1)
-gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
+gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+            const __grid_constant__ DstMaps dm, const Params p) {
     using G = Cfg<BN, BKE, X3, STAGES>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* ring = smem;                                      // [STAGES][A|B]
     uint8_t* ring_lo = smem + G::STAGE_BYTES * STAGES;         // X3: [STAGES][Alo|Blo]
-    float4* epi_stage = reinterpret_cast<float4*>(smem + G::RING_BYTES);   // [4 warps][256]
+    float4* epi_stage = reinterpret_cast<float4*>(smem + G::RING_BYTES);   // [4 warps][2][256]
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + G::RING_BYTES + G::EPI_BYTES);
     uint64_t* full = bars;                                     // TMA landed
     uint64_t* empty = bars + STAGES;                           // MMA done with stage
@@ -266,7 +303,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     } else if (warp < 6) {
         // ------------------------------ epilogue ----------------------------------
         const int q = warp & 3;   // TMEM lane quarter this warp may access
-        int it = 0;
+        int it = 0, seq = 0;
         for (long long u = first_tile; u < p.num_units; u += tile_step, ++it) {
             int b, mb, nb, kb0, kb1;
             tile_coords(p, u / p.splits, b, mb, nb);
@@ -299,9 +336,11 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                     if (p.epi & 4) x = x > 0.f ? x : 0.f;
                     v[j] = x;
                 }
-                if (p.vec_store && n0 + 32 <= p.N && p.ndst > 1) {
+                if (p.tma_multi) {
+                    store_block_tma(dm, p.ndst, epi_stage + q * 512, seq, v, lane, n0, mb * BM + q * 32, b, p.M, p.N);
+                } else if (p.vec_store && n0 + 32 <= p.N && p.ndst > 1) {
                     // several destinations (peers over NVLink): whole-row stores
-                    store_block_lines(epi_stage + q * 256, v, lane, p,
+                    store_block_lines(epi_stage + q * 512, v, lane, p,
                                       (int64_t)b * p.sc_b + (int64_t)sp * p.split_stride, mb * BM + q * 32, n0);
                 } else if (p.vec_store && n0 + 32 <= p.N) {
                     // one local destination: straight from registers (the shared-memory
@@ -351,6 +390,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     }
 
 done:
+    if (warp >= 2 && warp < 6 && lane == 0) bulk_wait_all();   // TMA stores performed, buffers free
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {

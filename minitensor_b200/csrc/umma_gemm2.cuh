@@ -48,7 +48,7 @@ struct Cfg {
     static constexpr int NUM_WARPS = X3 ? 10 : 6;
     static constexpr int THREADS = NUM_WARPS * 32;
     static constexpr uint32_t RING_BYTES = STAGE_BYTES * STAGES * (X3 ? 2 : 1);
-    static constexpr uint32_t EPI_BYTES = 4 * 4096;                // epilogue staging, 4 KB per warp
+    static constexpr uint32_t EPI_BYTES = 4 * 8192;                // epilogue staging, 2 x 4 KB per warp
     static constexpr uint32_t BAR_BYTES = 8 * (3 * STAGES + 4) + 16;
     static constexpr uint32_t SMEM_BYTES = 1024 + RING_BYTES + EPI_BYTES + BAR_BYTES;
     static constexpr uint32_t CHUNK = 32;
@@ -66,7 +66,8 @@ __device__ __forceinline__ void drain_pause() {
 
 template <int BN, int BKE, bool A_MN, bool B_MN, bool X3, int STAGES>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg<BN, BKE, X3, STAGES>::THREADS, 1)
-gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
+gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                 const __grid_constant__ umma::DstMaps dm, const Params p) {
     using G = Cfg<BN, BKE, X3, STAGES>;
     extern __shared__ uint8_t smem_raw[];
     // Same dynamic-smem base in both CTAs, so the aligned layout (and every descriptor
@@ -74,7 +75,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* ring = smem;
     uint8_t* ring_lo = smem + G::STAGE_BYTES * STAGES;
-    float4* epi_stage = reinterpret_cast<float4*>(smem + G::RING_BYTES);   // [4 warps][256]
+    float4* epi_stage = reinterpret_cast<float4*>(smem + G::RING_BYTES);   // [4 warps][2][256]
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + G::RING_BYTES + G::EPI_BYTES);
     uint64_t* full = bars;
     uint64_t* empty = bars + STAGES;
@@ -210,7 +211,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     } else if (warp < 6) {
         // ------------------------------ epilogue ----------------------------------
         const int q = warp & 3;
-        int it = 0;
+        int it = 0, seq = 0;
         for (long long u = first; u < p.num_units; u += step, ++it) {
             int b, mb, nb, kb0, kb1;
             umma::tile_coords(p, u / p.splits, b, mb, nb);
@@ -244,9 +245,12 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                     if (p.epi & 4) x = x > 0.f ? x : 0.f;
                     v[j] = x;
                 }
-                if (p.vec_store && n0 + 32 <= p.N && p.ndst > 1) {
+                if (p.tma_multi) {
+                    umma::store_block_tma(dm, p.ndst, epi_stage + q * 512, seq, v, lane, n0,
+                                          mb * BM + (int)rank * BMC + q * 32, b, p.M, p.N);
+                } else if (p.vec_store && n0 + 32 <= p.N && p.ndst > 1) {
                     // several destinations (peers over NVLink): whole-row stores
-                    umma::store_block_lines(epi_stage + q * 256, v, lane, p,
+                    umma::store_block_lines(epi_stage + q * 512, v, lane, p,
                                             (int64_t)b * p.sc_b + (int64_t)sp * p.split_stride,
                                             mb * BM + (int)rank * BMC + q * 32, n0);
                 } else if (p.vec_store && n0 + 32 <= p.N) {
@@ -299,6 +303,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 
 done:
     if (warp == 0 && lane == 0 && *abort_flag) drain_pause();
+    if (warp >= 2 && warp < 6 && lane == 0) bulk_wait_all();   // TMA stores performed, buffers free
     tc_fence_before();
     __syncthreads();
     cluster_sync_all();   // the peer no longer signals us or reads our shared memory / TMEM

@@ -97,6 +97,8 @@ def lib() -> ctypes.CDLL:
     L.mt_gemm_multi.restype = ctypes.c_int
     L.mt_peer_barrier.argtypes = [vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, u64, vp]
     L.mt_peer_barrier.restype = ctypes.c_int
+    L.mt_copy_rows_async.argtypes = [vp, u64, vp, u64, u64, u64, vp]
+    L.mt_copy_rows_async.restype = ctypes.c_int
     L.mt_set_default_mode.argtypes = [ctypes.c_int]
     L.mt_set_default_mode.restype = ctypes.c_int
     L.mt_get_default_mode.restype = ctypes.c_int

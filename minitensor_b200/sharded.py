@@ -4,11 +4,21 @@ The reference is single-GPU (README.md:273). For the large-GEMM configuration th
 C = A.B is split by N-columns: rank r holds A and B[:, n0:n1] and computes C[:, n0:n1].
 Every rank needs the whole C afterwards, so the shards must be all-gathered.
 
-Product path (``ShardedGemm.run``): the GEMM and the all-gather are ONE kernel. Each
-rank opens the other ranks' C buffers through CUDA IPC; the tcgen05 kernel's epilogue
-stores each finished 128x256 tile into the local C and, over NVLink, into the same
-columns of every peer's C while the next tile's main loop runs. A stream-ordered flag
-barrier (bounded wait, device status on timeout) then makes all ranks' writes visible.
+Product path (``ShardedGemm.run``). Each rank opens the other ranks' C buffers through
+CUDA IPC, then pushes its columns into every peer's C in one of two ways:
+
+* ``gather="epilogue"`` (default): the GEMM and the all-gather are ONE kernel -- the
+  tcgen05 epilogue hands each finished 32x32 block of a tile to the TMA engine, which
+  stores it into the local C and, over NVLink, into the same columns of every peer's C
+  while the next tile's main loop runs (measured ~630 GB/s of egress per GPU with 2 and
+  4 ranks).
+* ``gather="copy"``: the GEMM runs in row chunks into the local C; after each chunk the
+  copy engines push that chunk's columns to every peer (one 2-D copy per peer, each peer
+  on its own stream) while the next chunk is computed. Slower here at every size (the
+  shard rows are narrow strided runs: 4 KB at 8 ranks); kept as an option.
+
+A stream-ordered flag barrier (bounded wait, device status on timeout) then makes all
+ranks' writes visible.
 
 Baseline (``allgather_shards``): local GEMM into a shard buffer, then an NCCL (or gloo on
 CPU) all-gather and a relayout into row-major C.
@@ -67,7 +77,7 @@ class ShardedGemm:
     ends with the full C. Call collectively (same order on every rank)."""
 
     def __init__(self, M: int, N: int, K: int, rank: int | None = None, world: int | None = None, group=None,
-                 timeout_s: float = 10.0):
+                 timeout_s: float = 10.0, gather: str | None = None, chunks: int | None = None):
         self.M, self.N, self.K = M, N, K
         self.rank = dist.get_rank(group) if rank is None else rank
         self.world = dist.get_world_size(group) if world is None else world
@@ -81,6 +91,20 @@ class ShardedGemm:
         self._flag_peers = PeerTensor(self.flags, self.rank, self.world, group)
         self._flag_arr = (ctypes.c_void_p * self.world)(*self._flag_peers.ptrs)
         self._bound = {}
+        if gather is None:
+            gather = "epilogue"
+        if gather not in ("epilogue", "copy"):
+            raise ValueError("gather must be 'epilogue' or 'copy'")
+        self.gather = gather
+        # Row chunks for the copy pipeline: boundaries on 256-row tiles; fewer chunks when
+        # the shard is narrow so that each chunk still has work for most SM pairs.
+        if chunks is None:
+            chunks = 4 if self.world <= 4 else 2
+        tiles_m = (M + 255) // 256
+        chunks = max(1, min(chunks, tiles_m))
+        self.row_chunks = [(256 * (tiles_m * c // chunks), min(M, 256 * (tiles_m * (c + 1) // chunks)))
+                           for c in range(chunks)]
+        self._copy_streams = [torch.cuda.Stream() for _ in range(self.world - 1)] if gather == "copy" else []
 
     def _peers(self, C: torch.Tensor) -> PeerTensor:
         key = (C.data_ptr(), C.numel())
@@ -99,13 +123,34 @@ class ShardedGemm:
             raise ValueError("A must be [M, K] and B_shard [K, n1 - n0]")
         pt = self._peers(C)
         es = C.element_size()
-        extra = [pt.ptrs[d] + self.n0 * es for d in range(self.world) if d != self.rank]
-        arr = (ctypes.c_void_p * max(1, len(extra)))(*extra)
-        Cv = C[:, self.n0:self.n1]
         s = engine._stream(stream)
         L = engine.lib()
-        engine._check(L.mt_gemm_multi(ctypes.byref(engine.view(A)), ctypes.byref(engine.view(B_shard)),
-                                      ctypes.byref(engine.view(Cv)), arr, len(extra), None, 0, engine._mode(mode), s))
+        if self.gather == "epilogue":
+            extra = [pt.ptrs[d] + self.n0 * es for d in range(self.world) if d != self.rank]
+            arr = (ctypes.c_void_p * max(1, len(extra)))(*extra)
+            Cv = C[:, self.n0:self.n1]
+            engine._check(L.mt_gemm_multi(ctypes.byref(engine.view(A)), ctypes.byref(engine.view(B_shard)),
+                                          ctypes.byref(engine.view(Cv)), arr, len(extra), None, 0,
+                                          engine._mode(mode), s))
+        else:
+            main = torch.cuda.current_stream() if stream is None else stream
+            if not isinstance(main, torch.cuda.Stream):
+                main = torch.cuda.ExternalStream(int(main))
+            peers = [d for d in range(self.world) if d != self.rank]
+            pitch, width = self.N * es, (self.n1 - self.n0) * es
+            for r0, r1 in self.row_chunks:
+                engine.gemm(A[r0:r1], B_shard, C[r0:r1, self.n0:self.n1], mode=mode, stream=main)
+                ev = torch.cuda.Event()
+                ev.record(main)
+                off = (r0 * self.N + self.n0) * es
+                for cs, d in zip(self._copy_streams, peers):
+                    cs.wait_event(ev)
+                    engine._check(L.mt_copy_rows_async(pt.ptrs[d] + off, pitch, pt.ptrs[self.rank] + off, pitch,
+                                                       width, r1 - r0, cs.cuda_stream))
+            for cs in self._copy_streams:
+                ev = torch.cuda.Event()
+                ev.record(cs)
+                main.wait_event(ev)
         self.epoch += 1
         engine._check(L.mt_peer_barrier(self._flag_arr, self.rank, self.world, self.epoch, self.timeout_ns, s))
 

@@ -105,7 +105,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _sharded_worker(rank, world, port, out, mode, shape=(1024, 1536, 512)):
+def _sharded_worker(rank, world, port, out, mode, shape=(1024, 1536, 512), gather=None):
     import torch.distributed as dist
     from minitensor_b200 import sharded
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -114,7 +114,7 @@ def _sharded_worker(rank, world, port, out, mode, shape=(1024, 1536, 512)):
     M, N, K = shape
     A = inputs.uniform((M, K), -1, 1, 81)
     B = inputs.uniform((K, N), -1, 1, 82)
-    plan = sharded.ShardedGemm(M, N, K, rank, world, timeout_s=5.0)
+    plan = sharded.ShardedGemm(M, N, K, rank, world, timeout_s=5.0, gather=gather)
     C = torch.zeros(M, N, device="cuda")
     for _ in range(2):   # twice: the second call reuses the IPC mappings and a new epoch
         plan.run(dev(A), dev(np.ascontiguousarray(B[:, plan.n0:plan.n1])), C, mode=mode)
@@ -128,15 +128,21 @@ def _sharded_worker(rank, world, port, out, mode, shape=(1024, 1536, 512)):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("mode,shape", [("tf32x3", (1024, 1536, 512)), ("strict", (1024, 1536, 512)),
-                                        ("tf32", (2304, 4672, 128)), ("tf32x3", (2304, 4672, 128))])
-def test_sharded_gemm_two_gpus(eng, port, tmp_path, mode, shape):
-    """Column shards on two GPUs, every rank ending with the full C; the (2304, 4672, 128)
-    cases give each rank >= 74 tiles of 256 x 256, i.e. the CTA-pair kernel with the
-    peer-store epilogue."""
+@pytest.mark.parametrize("mode,shape,gather", [("tf32x3", (1024, 1536, 512), "epilogue"),
+                                               ("strict", (1024, 1536, 512), "epilogue"),
+                                               ("tf32", (2304, 4672, 128), "epilogue"),
+                                               ("tf32x3", (2304, 4672, 128), "epilogue"),
+                                               ("tf32x3", (1000, 1536, 512), "copy"),
+                                               ("tf32", (2304, 4672, 128), "copy")])
+def test_sharded_gemm_two_gpus(eng, port, tmp_path, mode, shape, gather):
+    """Column shards on two GPUs, every rank ending with the full C. `epilogue`: the GEMM
+    epilogue stores into the peers (the (2304, 4672, 128) cases give each rank >= 74 tiles
+    of 256 x 256: the CTA-pair kernel); `copy`: row chunks pushed by the copy engines
+    (M = 1000: a ragged last chunk)."""
     import torch.multiprocessing as mp
     world = 2
-    mp.spawn(_sharded_worker, args=(world, _free_port(), str(tmp_path), mode, shape), nprocs=world, join=True)
+    mp.spawn(_sharded_worker, args=(world, _free_port(), str(tmp_path), mode, shape, gather), nprocs=world,
+             join=True)
     M, N, K = shape
     A = inputs.uniform((M, K), -1, 1, 81)
     B = inputs.uniform((K, N), -1, 1, 82)
