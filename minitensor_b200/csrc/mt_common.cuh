@@ -150,7 +150,8 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* m, 
 }
 
 // TMA tensor store shared -> global (bulk-group completion). The destination may be a
-// peer GPU's memory (a non-multicast store; the TMA engine moves the tile over NVLink).
+// peer GPU's memory (a plain per-CTA tensor store, no cluster broadcast; the TMA engine
+// moves the tile over NVLink).
 __device__ __forceinline__ void tma_store_3d(const CUtensorMap* m, uint32_t src, int c0, int c1, int c2) {
     asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];"
                  ::"l"(reinterpret_cast<uint64_t>(m)), "r"(src), "r"(c0), "r"(c1), "r"(c2)
