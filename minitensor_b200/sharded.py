@@ -40,6 +40,14 @@ def shard_columns(N: int, world: int, rank: int) -> tuple[int, int]:
     return N * rank // world, N * (rank + 1) // world
 
 
+def row_chunks(M: int, chunks: int) -> list[tuple[int, int]]:
+    """Row ranges [r0, r1) of the copy pipeline: `chunks` near-equal parts of [0, M) with
+    boundaries on 256-row tiles (fewer parts when M has fewer tiles)."""
+    tiles_m = (M + 255) // 256
+    chunks = max(1, min(chunks, tiles_m))
+    return [(256 * (tiles_m * c // chunks), min(M, 256 * (tiles_m * (c + 1) // chunks))) for c in range(chunks)]
+
+
 class PeerTensor:
     """Device pointers to the same tensor on every rank (own pointer at index `rank`)."""
 
@@ -100,10 +108,7 @@ class ShardedGemm:
         # the shard is narrow so that each chunk still has work for most SM pairs.
         if chunks is None:
             chunks = 4 if self.world <= 4 else 2
-        tiles_m = (M + 255) // 256
-        chunks = max(1, min(chunks, tiles_m))
-        self.row_chunks = [(256 * (tiles_m * c // chunks), min(M, 256 * (tiles_m * (c + 1) // chunks)))
-                           for c in range(chunks)]
+        self.row_chunks = row_chunks(M, chunks)
         self._copy_streams = [torch.cuda.Stream() for _ in range(self.world - 1)] if gather == "copy" else []
 
     def _peers(self, C: torch.Tensor) -> PeerTensor:

@@ -87,3 +87,15 @@ def test_dead_rank_is_detected_not_hung(tmp_path):
     status, secs = open(tmp_path / "survivor.txt").read().split()
     assert status.startswith("error"), status
     assert float(secs) < 30
+
+
+def test_row_chunks_cover_rows_on_tile_boundaries():
+    from minitensor_b200.sharded import row_chunks
+    for M, chunks in [(8192, 4), (8192, 2), (1000, 4), (300, 4), (256, 3), (1, 4), (8192, 1)]:
+        parts = row_chunks(M, chunks)
+        assert parts[0][0] == 0 and parts[-1][1] == M
+        for (a0, a1), (b0, b1) in zip(parts, parts[1:]):
+            assert a1 == b0
+        assert all(r0 < r1 for r0, r1 in parts)
+        assert all(r0 % 256 == 0 for r0, _ in parts)
+        assert len(parts) == min(chunks, (M + 255) // 256)
