@@ -302,15 +302,20 @@ int launch_umma(const GemmProblem& p, bool x3, cudaStream_t st, float* const* ex
     else if ((p.sb_k == 1 || p.K == 1) && (p.N == 1 || mult4(p.sb_n))) b_mn = 0;
     if (a_mn < 0 || b_mn < 0) return fail(MT_EUNSUPPORTED, "umma: operand strides not TMA-expressible");
 
-    const uint32_t bke = x3 ? 16 : 32;        // k elements per stage
-    const int kswz = (int)bke * 4;             // K-major swizzle span (bytes)
-    const uint32_t chunk = 32;                 // MN-major box width (elements)
     const int64_t tiles_m1 = (p.M + 127) / 128;
     const bool small = tiles_m1 * ((p.N + 255) / 256) * p.batch < (int64_t)di.sms || p.N <= 128;
     const int bn = small ? 128 : 256;
     // CTA pairs: 256 x 256 tiles, at least one per pair of SMs.
     const bool pair = pair_enabled() && !small && p.M > 128 &&
                       ((p.M + 255) / 256) * ((p.N + 255) / 256) * p.batch >= (int64_t)(di.sms / 2);
+    // k elements per stage: 32 (a 128-byte swizzled row); the one-CTA TF32X3 kernel takes
+    // 16 to keep 4-6 stages of hi + lo in shared memory, the pair kernel 32 with 3 stages
+    // (half the stage hand-offs per MMA; measured +5% on 8192^3 and a higher clock under
+    // the power cap).
+    const bool x3_wide = pair && x3;
+    const uint32_t bke = (x3 && !x3_wide) ? 16 : 32;
+    const int kswz = (int)bke * 4;             // K-major swizzle span (bytes)
+    const uint32_t chunk = 32;                 // MN-major box width (elements)
     const int64_t tiles_m = pair ? (p.M + 255) / 256 : tiles_m1;
     const uint32_t b_rows = pair ? (uint32_t)bn / 2 : (uint32_t)bn;   // B tile rows one CTA loads
 
@@ -411,6 +416,7 @@ int launch_umma(const GemmProblem& p, bool x3, cudaStream_t st, float* const* ex
     else rc = launch_pair_inst<256, BKE_, true, true, X3_, ST_>(ta, tb, dm, up, di.sms, st);
     if (pair) {
         if (!x3) { MT_PAIR_DISPATCH(32, false, 6) }
+        else if (x3_wide) { MT_PAIR_DISPATCH(32, true, 3) }
         else { MT_PAIR_DISPATCH(16, true, 6) }
     } else if (!x3) {
         if (bn == 256) { MT_UMMA_DISPATCH(256, 32, false, 4) }
