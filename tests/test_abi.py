@@ -91,3 +91,33 @@ def test_view_carries_offset_and_strides():
     assert list(v.shape)[:2] == [6, 3] and list(v.strides)[:2] == [1, 8]
     e = engine.view(torch.zeros(1, 4, 5).expand(3, 4, 5))
     assert list(e.strides)[:3] == [0, 5, 1]
+
+
+def test_sum_rows_argument_errors():
+    lib = engine.lib()
+    x3, out = engine.view(_t(2, 3, 4)), engine.view(_t(4))
+    assert lib.mt_sum_rows_gpu(ctypes.byref(x3), ctypes.byref(out), None) == engine.MT_EINVAL
+    assert b"2-D" in lib.mt_last_error()
+    x, wrong = engine.view(_t(5, 4)), engine.view(_t(3))
+    assert lib.mt_sum_rows_gpu(ctypes.byref(x), ctypes.byref(wrong), None) == engine.MT_EINVAL
+    assert b"columns" in lib.mt_last_error()
+    two_rows = engine.view(_t(2, 4))
+    assert lib.mt_sum_rows_gpu(ctypes.byref(x), ctypes.byref(two_rows), None) == engine.MT_EINVAL
+    assert lib.mt_sum_rows_gpu(None, ctypes.byref(out), None) == engine.MT_EINVAL
+
+
+def test_copy_rows_and_multi_gpu_argument_errors():
+    lib = engine.lib()
+    assert lib.mt_copy_rows_async(None, 64, None, 64, 16, 4, None) == engine.MT_EINVAL
+    buf = ctypes.create_string_buffer(64)
+    p = ctypes.cast(buf, ctypes.c_void_p)
+    assert lib.mt_copy_rows_async(p, 8, p, 64, 16, 4, None) == engine.MT_EINVAL   # pitch < width
+    assert lib.mt_copy_rows_async(p, 64, p, 64, 16, 0, None) == engine.MT_OK      # nothing to copy
+    a, b, c = engine.view(_t(2, 3)), engine.view(_t(3, 2)), engine.view(_t(2, 2))
+    rc = lib.mt_gemm_multi(ctypes.byref(a), ctypes.byref(b), ctypes.byref(c), None, 2, None, 0, 0, None)
+    assert rc == engine.MT_EINVAL and b"extra_dst" in lib.mt_last_error()
+    rc = lib.mt_gemm_multi(ctypes.byref(a), ctypes.byref(b), ctypes.byref(c), None, 9, None, 0, 0, None)
+    assert rc == engine.MT_EINVAL
+    flags = (ctypes.c_void_p * 2)(None, None)
+    rc = lib.mt_peer_barrier(flags, 0, 9, 1, 1000, None)
+    assert rc == engine.MT_EINVAL
