@@ -63,6 +63,25 @@ def test_multi_destination_epilogue_pair_kernel(eng, port, mode):
         assert np.array_equal(host(e), c)
 
 
+def test_multi_destination_ragged_columns_clipped(eng, port):
+    """N = 2340 (not a multiple of 32): the last column block of each tile is partial and
+    the TMA stores must clip it; every destination is a window of a wider buffer whose
+    guard columns must stay untouched."""
+    M, K, N = 2304, 96, 2340
+    A = inputs.uniform((M, K), -1, 1, 77)
+    B = inputs.uniform((K, N), -1, 1, 78)
+    bufs = [torch.full((M, N + 12), 3.0, device="cuda") for _ in range(4)]
+    views = [b[:, :N] for b in bufs]
+    _multi(dev(A), dev(B), views[0], views[1:], "tf32x3")
+    assert eng.last_path().startswith("umma_pair_tf32x3"), eng.last_path()
+    c0 = host(views[0])
+    rows = [0, 255, 256, 1151, M - 1]
+    check("tf32x3", c0[rows], port.matmul_strided(A[rows], B), absmm(A[rows], B), K, "ragged local")
+    for b, v in zip(bufs, views):
+        assert np.array_equal(host(v), c0)
+        assert np.all(host(b)[:, N:] == 3.0)
+
+
 def test_column_shard_into_wide_buffers(eng, port):
     # The sharded layout on one GPU: 4 "ranks" write their column blocks into 4 full-width Cs.
     M, K, N, world = 256, 192, 512, 4
