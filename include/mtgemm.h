@@ -7,7 +7,8 @@
  * mt_*_gpu function below replaces one of them for T = float, with the same argument
  * meaning, so a binding only maps a Tensor<float> to an mt_tensor (storage pointer,
  * view offset, shape, strides -- exactly the fields of include/TensorImpl.hpp) and
- * turns a non-zero status into the reference's exception (INTEGRATION.md shows it).
+ * turns a non-zero status into the reference's exception (std::runtime_error carrying
+ * mt_last_error()).
  *
  * Conventions (the reference's, include/TensorOps.hpp:993-1149, include/GpuUtils.hpp):
  *   - All pointers are device pointers. The caller allocates every output with its final

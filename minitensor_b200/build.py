@@ -15,6 +15,9 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 LIB = os.path.join(PKG, "libmtgemm.so")
+# The reference checkout: $MT_REFERENCE_ROOT, else a "reference" directory beside the repo.
+REF_ROOT = os.environ.get("MT_REFERENCE_ROOT",
+                          os.path.join(os.path.dirname(ROOT), "reference"))
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -70,7 +73,7 @@ def _run(cmd):
     subprocess.check_call(cmd)
 
 
-def build_dropin(ref_root: str = "/root/reference") -> str | None:
+def build_dropin(ref_root: str = REF_ROOT) -> str | None:
     """Builds overlay/_build/dropin_test: the reference's own dispatchers, autograd and
     modules (headers unmodified; src/gpu_ops.cpp compiled from where it lies) with the
     GEMM/conv entry points served by gpu_ops_b200.cpp + libmtgemm.so. Needs the reference

@@ -43,7 +43,10 @@ def _p(a):
 def build(ref_include: str | None = None) -> None:
     """Compile liboracle.so (and _ref/libref_cpu.so when the reference headers exist)."""
     subprocess.check_call(["make", "-s", "-C", HERE, "all"])
-    inc = ref_include or "/root/reference/include"
+    # The reference checkout: $MT_REFERENCE_ROOT, else a "reference" directory beside the repo.
+    root = os.environ.get("MT_REFERENCE_ROOT",
+                          os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference"))
+    inc = ref_include or os.path.join(root, "include")
     if os.path.isdir(inc):
         subprocess.check_call(["make", "-s", "-C", HERE, "ref", f"REF_INCLUDE={inc}"])
 
