@@ -18,7 +18,8 @@ CUDA IPC, then pushes its columns into every peer's C in one of two ways:
   shard rows are narrow strided runs: 4 KB at 8 ranks); kept as an option.
 
 A stream-ordered flag barrier (bounded wait, device status on timeout) then makes all
-ranks' writes visible.
+ranks' writes visible. An optional host-side step gate (``PeerLiveness``) finds a peer
+that left, died or fell behind before the next step is launched.
 
 Baseline (``allgather_shards``): local GEMM into a shard buffer, then an NCCL (or gloo on
 CPU) all-gather and a relayout into row-major C.
@@ -28,6 +29,7 @@ torch.distributed is only the plumbing: it exchanges IPC handles and runs the ba
 from __future__ import annotations
 
 import ctypes
+import time
 
 import torch
 import torch.distributed as dist
@@ -85,8 +87,10 @@ class ShardedGemm:
     ends with the full C. Call collectively (same order on every rank)."""
 
     def __init__(self, M: int, N: int, K: int, rank: int | None = None, world: int | None = None, group=None,
-                 timeout_s: float = 10.0, gather: str | None = None, chunks: int | None = None):
+                 timeout_s: float = 10.0, gather: str | None = None, chunks: int | None = None,
+                 liveness: "PeerLiveness | None" = None):
         self.M, self.N, self.K = M, N, K
+        self.liveness = liveness
         self.rank = dist.get_rank(group) if rank is None else rank
         self.world = dist.get_world_size(group) if world is None else world
         if self.world > 8:
@@ -126,6 +130,8 @@ class ShardedGemm:
             raise ValueError("C must be a contiguous [M, N] tensor")
         if B_shard.shape != (self.K, self.n1 - self.n0) or A.shape != (self.M, self.K):
             raise ValueError("A must be [M, K] and B_shard [K, n1 - n0]")
+        if self.liveness is not None:
+            self.liveness.step()   # raises PeerLost before anything is launched
         pt = self._peers(C)
         es = C.element_size()
         s = engine._stream(stream)
@@ -164,6 +170,69 @@ class ShardedGemm:
             pt.close()
         self._bound = {}
         self._flag_peers.close()
+
+
+class PeerLost(RuntimeError):
+    """A peer rank left, aborted or missed a step deadline; no further step may launch."""
+
+
+class PeerLiveness:
+    """Host-side step gate over the process group's key-value store.
+
+    Before step e every rank publishes ``ready/e/<rank>`` and waits, polling, until all
+    peers have published theirs. A rank that leaves between steps (``leave()``), dies, or
+    is slower than ``timeout_s`` is therefore noticed on the host BEFORE the next launch,
+    so no kernel is started that would write into, or wait on, a departed peer's memory.
+    A rank that gives up marks itself ``gone/<rank>`` so that late peers stop too instead
+    of launching a step nobody else joins. One store round trip per peer per step: meant
+    for eager steps, not for inside a captured graph (the gate runs at capture time only).
+    """
+
+    def __init__(self, rank: int, world: int, store=None, timeout_s: float = 10.0,
+                 prefix: str = "mt_live", poll_s: float = 0.002):
+        if store is None:
+            store = dist.distributed_c10d._get_default_store()
+        self.rank, self.world, self.store = rank, world, store
+        self.timeout_s, self.poll_s, self.prefix = timeout_s, poll_s, prefix
+        self.epoch = 0
+
+    def _gone(self, r: int) -> str:
+        return f"{self.prefix}/gone/{r}"
+
+    def _ready(self, e: int, r: int) -> str:
+        return f"{self.prefix}/ready/{e}/{r}"
+
+    def gone_peers(self) -> list[int]:
+        return [r for r in range(self.world) if r != self.rank and self.store.check([self._gone(r)])]
+
+    def step(self) -> int:
+        """Gate for the next step. Returns its epoch; raises PeerLost (and marks this rank
+        gone) if a peer has left or does not arrive within the timeout."""
+        self.epoch += 1
+        e = self.epoch
+        self.store.set(self._ready(e, self.rank), b"1")
+        waiting = [r for r in range(self.world) if r != self.rank]
+        deadline = time.monotonic() + self.timeout_s
+        while True:
+            gone = self.gone_peers()
+            if gone:
+                self._give_up()
+                raise PeerLost(f"rank {self.rank}: peer(s) {gone} left before step {e}")
+            waiting = [r for r in waiting if not self.store.check([self._ready(e, r)])]
+            if not waiting:
+                return e
+            if time.monotonic() > deadline:
+                self._give_up()
+                raise PeerLost(f"rank {self.rank}: peer(s) {waiting} missed step {e} "
+                               f"within {self.timeout_s:g} s")
+            time.sleep(self.poll_s)
+
+    def leave(self) -> None:
+        """Announce a departure between steps (call after this rank's stream is idle)."""
+        self._give_up()
+
+    def _give_up(self) -> None:
+        self.store.set(self._gone(self.rank), b"1")
 
 
 def allgather_shards(C_shard: torch.Tensor, world: int, group=None) -> torch.Tensor:

@@ -99,3 +99,125 @@ def test_row_chunks_cover_rows_on_tile_boundaries():
         assert all(r0 < r1 for r0, r1 in parts)
         assert all(r0 % 256 == 0 for r0, _ in parts)
         assert len(parts) == min(chunks, (M + 255) // 256)
+
+
+# --- host-side step gate (PeerLiveness): a departed or late peer is found before a launch ---
+
+def _live_worker(rank, world, port, out, scenario, timeout_s):
+    from minitensor_b200.sharded import PeerLiveness, PeerLost
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
+    gate = PeerLiveness(rank, world, timeout_s=timeout_s)
+    log = []
+    try:
+        log.append(f"step{gate.step()}")
+        dist.barrier()   # stands for the end-of-step device barrier: step 1 finished everywhere
+        if rank == 1 and scenario == "leave":
+            gate.leave()
+            log.append("left")
+            raise SystemExit
+        if rank == 1 and scenario == "die":
+            with open(os.path.join(out, "r1.txt"), "w") as f:
+                f.write(" ".join(log + ["died"]))
+            os._exit(3)
+        if rank == 1 and scenario == "late":
+            time.sleep(3 * timeout_s)
+        for _ in range(2):
+            t0 = time.monotonic()
+            try:
+                log.append(f"step{gate.step()}")
+            except PeerLost:
+                log.append(f"lost@{time.monotonic() - t0:.2f}")
+                break
+    except SystemExit:
+        pass
+    with open(os.path.join(out, f"r{rank}.txt"), "w") as f:
+        f.write(" ".join(log))
+    # Rank 0 hosts the store: keep it up until the peer has written its result.
+    if rank == 0:
+        t0 = time.monotonic()
+        while not os.path.exists(os.path.join(out, "r1.txt")) and time.monotonic() - t0 < 30:
+            time.sleep(0.05)
+    os._exit(0)
+
+
+def _run_live(tmp_path, scenario, timeout_s=1.0):
+    ctx = mp.get_context("spawn")
+    port = free_port()
+    procs = [ctx.Process(target=_live_worker, args=(r, 2, port, str(tmp_path), scenario, timeout_s))
+             for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=90)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    assert not alive, "a rank hung in the step gate"
+    return [open(tmp_path / f"r{r}.txt").read().split() for r in range(2)]
+
+
+def _lost_after(entry):
+    assert entry.startswith("lost@"), entry
+    return float(entry[5:])
+
+
+def test_liveness_gate_all_ranks_step_together(tmp_path):
+    r0, r1 = _run_live(tmp_path, "ok")
+    assert r0 == r1 == ["step1", "step2", "step3"]
+
+
+def test_liveness_peer_that_leaves_is_seen_before_next_step(tmp_path):
+    r0, r1 = _run_live(tmp_path, "leave", timeout_s=5.0)
+    assert r1 == ["step1", "left"]
+    assert r0[0] == "step1" and len(r0) == 2
+    assert _lost_after(r0[1]) < 2.0   # announced departure: no need to wait out the timeout
+
+
+def test_liveness_dead_peer_bounded_by_timeout(tmp_path):
+    r0, r1 = _run_live(tmp_path, "die", timeout_s=1.0)
+    assert r1 == ["step1", "died"]
+    assert r0[0] == "step1"
+    assert 0.9 <= _lost_after(r0[1]) < 5.0
+
+
+def test_liveness_late_peer_stops_too(tmp_path):
+    # Rank 0 gives up after the timeout and marks itself gone; the late rank then finds
+    # that mark at once instead of launching a step that nobody else joins.
+    r0, r1 = _run_live(tmp_path, "late", timeout_s=1.0)
+    assert r0[0] == r1[0] == "step1"
+    assert 0.9 <= _lost_after(r0[1]) < 5.0
+    assert _lost_after(r1[1]) < 1.0
+
+
+def _late_collective_worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=2))
+    if rank == 1:
+        time.sleep(6)   # delayed past the group timeout, between steps
+    t0 = time.time()
+    try:
+        allgather_shards(torch.ones(4, 2), world)
+        status = "completed"
+    except Exception as e:
+        status = f"error:{type(e).__name__}"
+    with open(os.path.join(out, f"r{rank}.txt"), "w") as f:
+        f.write(f"{status} {time.time() - t0:.2f}")
+    os._exit(0)
+
+
+def test_rank_delayed_past_timeout_fails_collective_not_hangs(tmp_path):
+    ctx = mp.get_context("spawn")
+    port = free_port()
+    procs = [ctx.Process(target=_late_collective_worker, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=60)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    assert not alive, "a rank hung past the process-group timeout"
+    status, secs = open(tmp_path / "r0.txt").read().split()
+    assert status.startswith("error"), status
+    assert float(secs) < 20
