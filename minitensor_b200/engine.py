@@ -112,14 +112,31 @@ def lib() -> ctypes.CDLL:
     return L
 
 
+_cuda_present = None
+
+
+def _gpu_present() -> bool:
+    global _cuda_present
+    if _cuda_present is None:
+        _cuda_present = torch.cuda.is_available()
+    return _cuda_present
+
+
 def view(t: torch.Tensor | None) -> MtTensor | None:
-    """A torch tensor as an mt_tensor: storage base + element offset + shape + strides."""
+    """A torch tensor as an mt_tensor: storage base + element offset + shape + strides.
+
+    The C ABI takes device pointers only. Where a GPU is present a host tensor is refused
+    here, before any kernel could read a host address (the reference's dispatchers refuse
+    mixed devices the same way, include/TensorOps.hpp:995-997). Without a GPU no kernel
+    can launch, so host tensors still reach the library's argument checks."""
     if t is None:
         return None
     if t.dtype != torch.float32:
         raise ValueError(f"expected float32, got {t.dtype}")
     if t.dim() > MAX_DIMS:
         raise ValueError("Exceeded MAX_DIMS")
+    if t.device.type != "cuda" and _gpu_present():
+        raise ValueError(f"expected a CUDA tensor, got one on {t.device}")
     v = MtTensor()
     v.data = t.untyped_storage().data_ptr() if t.numel() else 0
     v.offset = t.storage_offset()
@@ -195,8 +212,26 @@ def gemm(A, B, C, bias=None, epi=EPI_NONE, mode=MODE_DEFAULT, stream=None):
     if isinstance(mode, str):
         mode = MODES[mode]
     a, b, c = view(A), view(B), view(C)
-    bp = bias.data_ptr() if bias is not None else None
-    _check(lib().mt_gemm(_ref(a), _ref(b), _ref(c), bp, int(epi), int(mode), _stream(stream)))
+    _check(lib().mt_gemm(_ref(a), _ref(b), _ref(c), _bias_ptr(bias, epi, C), int(epi), int(mode),
+                         _stream(stream)))
+
+
+def _bias_ptr(bias, epi, C):
+    """The raw bias pointer of mt_gemm, after checking what the C ABI cannot: a dense
+    float32 vector of M (EPI_BIAS_ROW) or N (EPI_BIAS_COL) elements on C's device."""
+    if bias is None:
+        return None
+    if not epi & (EPI_BIAS_ROW | EPI_BIAS_COL):
+        raise ValueError("bias given without a bias epilogue (EPI_BIAS_ROW or EPI_BIAS_COL)")
+    view(bias)   # dtype and device
+    want = C.shape[-2] if epi & EPI_BIAS_ROW else C.shape[-1]
+    if bias.numel() != want:
+        raise ValueError(f"bias must have {want} elements, got {bias.numel()}")
+    if not bias.is_contiguous():
+        raise ValueError("bias must be contiguous")
+    if bias.device != C.device:
+        raise ValueError("bias and C must be on the same device")
+    return bias.data_ptr()
 
 
 # ---- allocating dispatchers (include/TensorOps.hpp:933-1045, include/Module.hpp) ------
@@ -330,11 +365,14 @@ def conv2d_backward(dy, x, w, stride=1, padding=0, need=("input", "weight", "bia
 
 
 def conv2d_wgrad_workspace_bytes(dy, x, w_shape, stride, padding, mode=MODE_DEFAULT):
-    dw = torch.empty(0)
-    v = view(dw)
+    # dW is described by shape alone (contiguous, no storage): only its sizes are read.
+    v = MtTensor()
     v.ndim = 4
-    for i, d in enumerate(w_shape):
-        v.shape[i] = d
+    stride = 1
+    for i in reversed(range(4)):
+        v.shape[i] = w_shape[i]
+        v.strides[i] = stride
+        stride *= w_shape[i]
     return int(lib().mt_conv2d_wgrad_workspace_bytes(_ref(view(dy)), _ref(view(x)), _ref(v), stride, padding,
                                                      _mode(mode)))
 

@@ -121,3 +121,24 @@ def test_copy_rows_and_multi_gpu_argument_errors():
     flags = (ctypes.c_void_p * 2)(None, None)
     rc = lib.mt_peer_barrier(flags, 0, 9, 1, 1000, None)
     assert rc == engine.MT_EINVAL
+
+
+def test_gemm_bias_is_checked_before_the_call():
+    # The C ABI takes a raw bias pointer: its length, type and layout are checked above it.
+    A, B, C = _t(4, 3), _t(3, 5), _t(4, 5)
+    with pytest.raises(ValueError, match="5 elements"):
+        engine.gemm(A, B, C, bias=_t(4), epi=engine.EPI_BIAS_COL)
+    with pytest.raises(ValueError, match="4 elements"):
+        engine.gemm(A, B, C, bias=_t(5), epi=engine.EPI_BIAS_ROW)
+    with pytest.raises(ValueError, match="without a bias epilogue"):
+        engine.gemm(A, B, C, bias=_t(5), epi=engine.EPI_RELU)
+    with pytest.raises(ValueError, match="float32"):
+        engine.gemm(A, B, C, bias=torch.zeros(5, dtype=torch.float64), epi=engine.EPI_BIAS_COL)
+    with pytest.raises(ValueError, match="contiguous"):
+        engine.gemm(A, B, C, bias=_t(5, 2)[:, 0], epi=engine.EPI_BIAS_COL)
+
+
+def test_workspace_query_describes_dw_by_shape():
+    # Host-only: the query reads sizes; a bad shape comes back as 0 bytes, not a crash.
+    n = engine.conv2d_wgrad_workspace_bytes(_t(2, 4, 6, 6), _t(2, 3, 6, 6), (4, 3, 3, 3), 1, 1, "tf32")
+    assert n >= 0
