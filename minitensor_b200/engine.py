@@ -135,7 +135,7 @@ def view(t: torch.Tensor | None) -> MtTensor | None:
         raise ValueError(f"expected float32, got {t.dtype}")
     if t.dim() > MAX_DIMS:
         raise ValueError("Exceeded MAX_DIMS")
-    if t.device.type != "cuda" and _gpu_present():
+    if not t.is_cuda and _gpu_present():
         raise ValueError(f"expected a CUDA tensor, got one on {t.device}")
     v = MtTensor()
     v.data = t.untyped_storage().data_ptr() if t.numel() else 0
