@@ -177,3 +177,55 @@ def test_port_matches_reference_build(port, ref):
     assert np.array_equal(port.conv2d_bwd_input(dy, w, x.shape, 2, 1), dx)
     assert np.array_equal(port.conv2d_bwd_weight(dy, x, w.shape, 2, 1), dw)
     assert np.array_equal(port.conv2d_bwd_bias(dy), db)
+
+
+def test_port_matches_reference_build_sweep(port, ref):
+    """Seeded sweep of small shapes, layouts, strides and paddings: the C restatement and
+    the reference's own CPU code agree bit for bit (same loop order, same fp32 sums)."""
+    rs = np.random.RandomState(2024)
+    for i in range(24):
+        M, K, N = (int(v) for v in rs.randint(1, 40, size=3))
+        ta, tb = int(rs.randint(2)), int(rs.randint(2))
+        A_store = inputs.uniform((K, M) if ta else (M, K), -1, 1, 3000 + i)
+        B_store = inputs.uniform((N, K) if tb else (K, N), -1, 1, 3100 + i)
+        A = A_store.T if ta else A_store
+        B = B_store.T if tb else B_store
+        got = port.matmul_strided(A, B)
+        assert np.array_equal(got, ref.matmul_t(A_store, B_store, M, K, N, ta, tb)), (M, K, N, ta, tb)
+        if not ta and not tb:
+            assert np.array_equal(port.matmul(A, B), ref.matmul(A, B))
+    for i in range(8):
+        bt, M, K, N = (int(v) for v in rs.randint(1, 12, size=4))
+        A = inputs.normal((bt, M, K), 1.0, 3200 + i)
+        bc = bool(i % 2)
+        B = inputs.normal((1 if bc else bt, K, N), 1.0, 3300 + i)
+        Bv = np.broadcast_to(B, (bt, K, N)) if bc else B
+        assert np.array_equal(port.bmm(A, Bv), ref.bmm(A, B, bc)), (bt, M, K, N, bc)
+    for i in range(6):
+        M, K, N = (int(v) for v in rs.randint(1, 30, size=3))
+        X = inputs.normal((M, K), 1.0, 3400 + i)
+        W = inputs.normal((K, N), 0.3, 3500 + i)
+        b = inputs.normal((1, N), 0.1, 3600 + i)
+        dY = inputs.normal((M, N), 1.0, 3700 + i)
+        Y, dX, dW = ref.linear(X, W, b, dY)
+        assert np.array_equal(port.linear_fwd(X, W, b), Y)
+        assert np.array_equal(port.matmul_strided(dY, W.T), dX)
+        assert np.array_equal(port.matmul_strided(X.T, dY), dW)
+    for i in range(24):
+        N, C, Co = (int(v) for v in rs.randint(1, 5, size=3))
+        H, W = (int(v) for v in rs.randint(1, 10, size=2))
+        kh, kw = (int(v) for v in rs.choice([1, 2, 3, 5], size=2))
+        stride, pad = int(rs.randint(1, 4)), int(rs.randint(0, 3))
+        x = inputs.normal((N, C, H, W), 1.0, 3800 + i)
+        w = inputs.normal((Co, C, kh, kw), 0.5, 3900 + i)
+        b = inputs.normal((Co,), 0.1, 4000 + i) if i % 3 else None
+        case = (N, C, H, W, Co, kh, kw, stride, pad)
+        y = port.conv2d(x, w, b, stride, pad)
+        assert np.array_equal(y, ref.conv2d(x, w, b, stride, pad)), case
+        if y.size == 0:
+            continue
+        dy = inputs.normal(y.shape, 1.0, 4100 + i)
+        dx, dw, db = ref.conv2d_backward(dy, x, w, stride, pad)
+        assert np.array_equal(port.conv2d_bwd_input(dy, w, x.shape, stride, pad), dx), case
+        assert np.array_equal(port.conv2d_bwd_weight(dy, x, w.shape, stride, pad), dw), case
+        assert np.array_equal(port.conv2d_bwd_bias(dy), db), case
