@@ -286,6 +286,53 @@ def linear_backward(x, W, dY, mode=MODE_DEFAULT, stream=None):
     return dX, dW, db
 
 
+def bmm_backward(A, B, dC, mode=MODE_DEFAULT, stream=None):
+    """Gradients of C = bmm(A, B): dA[i] = dC[i] . B[i]^T and dB[i] = A[i]^T . dC[i], read
+    through transposed views (no copies).
+
+    The reference's MatmulBackward transposes dims 0 and 1 (include/Autograd.hpp:133,139),
+    which is only right for 2-D operands; this is the batched form. An operand that is a
+    broadcast view (batch stride 0, the expand of a [1, ., .] tensor) gets the batch sum
+    of its gradient as [1, ., .], which is what accumulating into the expanded source means.
+    For a broadcast B with batch-contiguous A and dC that sum is ONE GEMM whose k runs over
+    (batch, row). Otherwise the per-batch gradients go to a scratch tensor and
+    mt_sum_rows_gpu adds them in batch order."""
+    if A.dim() != 3 or B.dim() != 3 or dC.dim() != 3:
+        raise ValueError("bmm_backward requires 3D tensors.")
+    bt, M, K = A.shape
+    N = B.shape[2]
+    if B.shape[0] != bt or dC.shape[0] != bt:
+        raise ValueError("bmm_backward: batch dimension mismatch.")
+    if B.shape[1] != K or tuple(dC.shape[1:]) != (M, N):
+        raise ValueError("bmm_backward: dC must be [batch, M, N] for A [batch, M, K] and B [batch, K, N].")
+    dev = A.device
+
+    def grad(X, Y, rows, cols, reduce, fold):
+        """X [bt, rows, k] . Y [bt, k, cols], batch-summed to [1, rows, cols] if `reduce`."""
+        if not reduce or bt == 1:
+            out = torch.empty((bt, rows, cols), dtype=torch.float32, device=dev)
+            gemm(X, Y, out, mode=mode, stream=stream)
+            return out
+        out = torch.empty((1, rows, cols), dtype=torch.float32, device=dev)
+        if fold is not None:
+            gemm(fold[0], fold[1], out[0], mode=mode, stream=stream)
+            return out
+        part = torch.empty((bt, rows, cols), dtype=torch.float32, device=dev)
+        gemm(X, Y, part, mode=mode, stream=stream)
+        sum_rows(part.view(bt, rows * cols), out.view(rows * cols), stream=stream)
+        return out
+
+    a_bcast = bt > 1 and A.stride(0) == 0
+    b_bcast = bt > 1 and B.stride(0) == 0
+    fold_b = None
+    if b_bcast and A.is_contiguous() and dC.is_contiguous():
+        # sum_i A[i]^T dC[i] = (A as [bt*M, K])^T . (dC as [bt*M, N])
+        fold_b = (A.reshape(bt * M, K).t(), dC.reshape(bt * M, N))
+    dA = grad(dC, B.transpose(1, 2), M, K, a_bcast, None)
+    dB = grad(A.transpose(1, 2), dC, K, N, b_bcast, fold_b)
+    return dA, dB
+
+
 def sum_rows(X, out, stream=None):
     """out[n] = sum over m of X[m, n] (X 2-D, out [N] or [1, N])."""
     _check(lib().mt_sum_rows_gpu(_ref(view(X)), _ref(view(out)), _stream(stream)))

@@ -142,3 +142,14 @@ def test_workspace_query_describes_dw_by_shape():
     # Host-only: the query reads sizes; a bad shape comes back as 0 bytes, not a crash.
     n = engine.conv2d_wgrad_workspace_bytes(_t(2, 4, 6, 6), _t(2, 3, 6, 6), (4, 3, 3, 3), 1, 1, "tf32")
     assert n >= 0
+
+
+def test_bmm_backward_shape_errors():
+    with pytest.raises(ValueError, match="3D"):
+        engine.bmm_backward(_t(3, 4), _t(4, 5), _t(3, 5))
+    with pytest.raises(ValueError, match="batch dimension mismatch"):
+        engine.bmm_backward(_t(2, 3, 4), _t(3, 4, 5), _t(2, 3, 5))
+    with pytest.raises(ValueError, match="dC must be"):
+        engine.bmm_backward(_t(2, 3, 4), _t(2, 4, 5), _t(2, 3, 4))
+    with pytest.raises(ValueError, match="dC must be"):
+        engine.bmm_backward(_t(2, 3, 4), _t(2, 5, 5), _t(2, 3, 5))

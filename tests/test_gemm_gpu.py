@@ -309,3 +309,44 @@ def test_pair_kernel_batched_bias_row(eng, port, mode):
         R = port.matmul_strided(A[b][rows], B[b])
         check(mode, Ch[b][rows], R + bm[rows][:, None], absmm(A[b][rows], B[b]) + np.abs(bm[rows])[:, None], K,
               f"pair batch {b}")
+
+
+def _bmm_grads_ref(port, A, B, dC):
+    """Per-batch oracle gradients of C = bmm(A, B) (A, B may be numpy broadcast views)."""
+    dA = np.stack([port.matmul_strided(dC[i], B[i].T) for i in range(A.shape[0])])
+    dB = np.stack([port.matmul_strided(A[i].T, dC[i]) for i in range(A.shape[0])])
+    return dA, dB
+
+
+@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("case", ["batched", "b_broadcast", "a_broadcast", "config3"])
+def test_bmm_backward(eng, port, mode, case):
+    """Batched NT/TN gradients through transposed 3-D views; a broadcast operand's gradient
+    is the batch sum (one folded GEMM for B, per-batch GEMMs + ordered row sums for A)."""
+    if case == "config3":
+        A, B0 = inputs.config3()
+        bt, M, K = A.shape
+        N = B0.shape[2]
+    else:
+        bt, M, K, N = 6, 200, 48, 136
+        A = inputs.uniform((1 if case == "a_broadcast" else bt, M, K), -1, 1, 120)
+        B0 = inputs.uniform((1 if case in ("b_broadcast",) else bt, K, N), -1, 1, 121)
+    dC = inputs.normal((bt, M, N), 1.0, 122)
+    Ab = np.broadcast_to(A, (bt, M, K))
+    Bb = np.broadcast_to(B0, (bt, K, N))
+    Ad = dev(A).expand(bt, M, K) if A.shape[0] == 1 else dev(A)
+    Bd = dev(B0).expand(bt, K, N) if B0.shape[0] == 1 else dev(B0)
+    dA, dB = eng.bmm_backward(Ad, Bd, dev(dC), mode=mode)
+    dA_ref, dB_ref = _bmm_grads_ref(port, Ab, Bb, dC)
+    DA = absmm(dC, np.swapaxes(np.abs(Bb), 1, 2))
+    DB = absmm(np.swapaxes(np.abs(Ab), 1, 2), dC)
+    if A.shape[0] == 1:
+        assert tuple(dA.shape) == (1, M, K)
+        check(mode, host(dA)[0], dA_ref.astype(np.float64).sum(0), DA.sum(0), bt * N, f"{case} dA (summed)")
+    else:
+        check(mode, host(dA), dA_ref, DA, N, f"{case} dA")
+    if B0.shape[0] == 1:
+        assert tuple(dB.shape) == (1, K, N)
+        check(mode, host(dB)[0], dB_ref.astype(np.float64).sum(0), DB.sum(0), bt * M, f"{case} dB (summed)")
+    else:
+        check(mode, host(dB), dB_ref, DB, M, f"{case} dB")
