@@ -10,6 +10,14 @@ if ROOT not in sys.path:
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200, sm_100a)")
+    config.addinivalue_line("markers", "first_gpu_run: GPU test that has not yet passed on hardware")
+
+
+def pytest_collection_modifyitems(config, items):
+    # Tests still waiting for their first pass on a GPU run after the established suite, so
+    # that a failure among them (under -x) cannot hide the results of the others. They
+    # still run and still fail the suite.
+    items.sort(key=lambda it: it.get_closest_marker("first_gpu_run") is not None)
 
 
 @pytest.fixture(scope="session")

@@ -318,6 +318,7 @@ def _bmm_grads_ref(port, A, B, dC):
     return dA, dB
 
 
+@pytest.mark.first_gpu_run
 @pytest.mark.parametrize("mode", MODES)
 @pytest.mark.parametrize("case", ["batched", "b_broadcast", "a_broadcast", "config3"])
 def test_bmm_backward(eng, port, mode, case):
