@@ -183,6 +183,25 @@ MT_API int mt_conv2d_wgrad_noalloc(const mt_tensor* dy, const mt_tensor* x, cons
 MT_API int mt_gemm(const mt_tensor* A, const mt_tensor* B, const mt_tensor* C,
                    const float* bias, int epi, int mode, void* stream);
 
+/* C[M,N] = A[M,K] * B[K,N] for row-major HOST buffers. Replaces the reference's sequence for
+ * host data: A.to(cuda), B.to(cuda), matmul(), C.to(cpu). There, each to() is a synchronous
+ * cudaMemcpy of the whole storage (include/TensorImpl.hpp:245-275) and matmul() runs in
+ * between (include/TensorOps.hpp:993-1045). Here the three overlap. B goes to the device
+ * first, then A in `panels` row panels on a library copy stream. The GEMM of panel i starts
+ * on `stream` once its rows have landed, and C's panel i returns on a second copy stream
+ * while later panels still arrive. The PCIe directions are independent, so the step costs
+ * about the host-to-device transfer plus one panel.
+ *   - Host buffers should be pinned (cudaHostAlloc / cudaHostRegister) for the copies to
+ *     overlap; pageable buffers work, serialised. They must stay valid, and C unread,
+ *     until `stream` has completed: the call only queues the work.
+ *   - `workspace` (device, 256-byte aligned, >= mt_matmul_host_workspace_bytes) holds A, B
+ *     and C on the device; NULL takes a stream-ordered allocation on `stream`.
+ *   - panels <= 0 picks the default (8, fewer for short A); panels are whole 256-row tiles.
+ *   - The two copy streams are per device and shared by all calls on that device. */
+MT_API int mt_matmul_host(const float* A, const float* B, float* C, uint64_t M, uint64_t K, uint64_t N,
+                          int mode, int panels, void* workspace, size_t ws_bytes, void* stream);
+MT_API size_t mt_matmul_host_workspace_bytes(uint64_t M, uint64_t K, uint64_t N);
+
 /* ---- multi-GPU: a column-sharded GEMM whose epilogue all-gathers C ------------------
  * The reference is single-GPU (README.md:273); these entry points have no counterpart
  * there. One process per GPU: rank r holds A and the column shard B[:, n0:n1], computes

@@ -9,6 +9,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "mtgemm.h"
 #include "mt_common.cuh"
@@ -1336,6 +1337,156 @@ MT_API int mt_gemm(const mt_tensor* A, const mt_tensor* B, const mt_tensor* C, c
     if (c.d[1] != a.d[1] || c.d[2] != b.d[2]) return fail(MT_EINVAL, "gemm: C shape mismatch");
     if (c.d[0] == 1) { a.s[0] = 0; b.s[0] = 0; c.s[0] = 0; }
     return gemm_from_views(a, b, c, bias, epi, mode, stream);
+}
+
+
+// ---- GEMM on host buffers: copies in, GEMM and copies out overlapped by row panels ----
+namespace {
+
+// Device-side layout of mt_matmul_host's workspace: A [M,K], B [K,N], C [M,N], each on a
+// 256-byte boundary.
+struct HostGemmLayout {
+    uint64_t a_off, b_off, c_off, bytes;
+};
+
+HostGemmLayout host_gemm_layout(uint64_t M, uint64_t K, uint64_t N) {
+    auto up = [](uint64_t x) { return (x + 255) & ~uint64_t(255); };
+    HostGemmLayout l;
+    l.a_off = 0;
+    l.b_off = up(M * K * 4);
+    l.c_off = l.b_off + up(K * N * 4);
+    l.bytes = l.c_off + M * N * 4;
+    return l;
+}
+
+// Copy streams of the current device, created on first use and kept for the process.
+int host_copy_streams(cudaStream_t& h2d, cudaStream_t& d2h) {
+    static std::mutex mu;
+    static cudaStream_t streams[64][2] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "matmul_host: cudaGetDevice");
+    std::lock_guard<std::mutex> g(mu);
+    cudaStream_t* s = streams[dev & 63];
+    for (int i = 0; i < 2; ++i)
+        if (!s[i] && (e = cudaStreamCreateWithFlags(&s[i], cudaStreamNonBlocking)) != cudaSuccess)
+            return cuda_fail(e, "matmul_host: copy stream");
+    h2d = s[0];
+    d2h = s[1];
+    return MT_OK;
+}
+
+}  // namespace
+
+MT_API size_t mt_matmul_host_workspace_bytes(uint64_t M, uint64_t K, uint64_t N) {
+    return (size_t)host_gemm_layout(M, K, N).bytes;
+}
+
+MT_API int mt_matmul_host(const float* A, const float* B, float* C, uint64_t M, uint64_t K, uint64_t N, int mode,
+                          int panels, void* workspace, size_t ws_bytes, void* stream) {
+    if (mode < MT_MODE_DEFAULT || mode > MT_TF32X3) return fail(MT_EINVAL, "matmul_host: bad mode %d", mode);
+    if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)
+        return fail(MT_EINVAL, "matmul_host: extent beyond 2^31 (M=%llu K=%llu N=%llu)", (unsigned long long)M,
+                    (unsigned long long)K, (unsigned long long)N);
+    if (M == 0 || N == 0) { t_path = "empty"; return MT_OK; }
+    if (!C || (K > 0 && (!A || !B))) return fail(MT_EINVAL, "matmul_host: null buffer");
+    const HostGemmLayout lay = host_gemm_layout(M, K, N);
+    if (workspace && ws_bytes < lay.bytes)
+        return fail(MT_EINVAL, "matmul_host: workspace of %zu bytes < %llu needed", ws_bytes,
+                    (unsigned long long)lay.bytes);
+    if (workspace && (reinterpret_cast<uintptr_t>(workspace) & 255))
+        return fail(MT_EINVAL, "matmul_host: workspace must be 256-byte aligned");
+    cudaStream_t st = static_cast<cudaStream_t>(stream), h2d = nullptr, d2h = nullptr;
+    int rc = host_copy_streams(h2d, d2h);
+    if (rc) return rc;
+
+    // Row panels on 256-row boundaries (a CTA pair's tile height), at most 8 by default.
+    const int64_t tiles = ((int64_t)M + 255) / 256;
+    const int P = (int)std::max<int64_t>(1, std::min<int64_t>(panels > 0 ? panels : 8, tiles));
+    auto row = [&](int p) -> int64_t { return p >= P ? (int64_t)M : 256 * (tiles * p / P); };
+
+    char* ws = static_cast<char*>(workspace);
+    bool owned = false;
+    cudaError_t e;
+    if (!ws) {
+        if ((e = cudaMallocAsync(reinterpret_cast<void**>(&ws), lay.bytes, st)) != cudaSuccess)
+            return cuda_fail(e, "matmul_host: workspace");
+        owned = true;
+    }
+    float* Ad = reinterpret_cast<float*>(ws + lay.a_off);
+    float* Bd = reinterpret_cast<float*>(ws + lay.b_off);
+    float* Cd = reinterpret_cast<float*>(ws + lay.c_off);
+
+    // Events: start (on st), one per A panel landed (h2d), one per C panel computed (st),
+    // and the two copy streams' tails, which st waits for before it returns or frees.
+    std::vector<cudaEvent_t> ev(2 * P + 3, nullptr);
+    for (auto& x : ev)
+        if ((e = cudaEventCreateWithFlags(&x, cudaEventDisableTiming)) != cudaSuccess) {
+            rc = cuda_fail(e, "matmul_host: event");
+            break;
+        }
+    cudaEvent_t ev_start = ev[0], ev_h2d_tail = ev[2 * P + 1], ev_d2h_tail = ev[2 * P + 2];
+    auto ev_a = [&](int p) { return ev[1 + p]; };
+    auto ev_c = [&](int p) { return ev[1 + P + p]; };
+    auto ck = [&](cudaError_t err, const char* what) {
+        if (err != cudaSuccess && rc == MT_OK) rc = cuda_fail(err, what);
+        return rc == MT_OK;
+    };
+    bool joined = false;
+    if (rc == MT_OK && ck(cudaEventRecord(ev_start, st), "matmul_host: record") &&
+        ck(cudaStreamWaitEvent(h2d, ev_start, 0), "matmul_host: wait") &&
+        ck(cudaStreamWaitEvent(d2h, ev_start, 0), "matmul_host: wait")) {
+        joined = true;
+        // B whole, then A panel by panel (cudaMemcpyDefault: pinned, pageable or device).
+        // (K == 0: nothing to copy in; the GEMM then writes zeros.)
+        if (K > 0) ck(cudaMemcpyAsync(Bd, B, K * N * 4, cudaMemcpyDefault, h2d), "matmul_host: copy B");
+        for (int p = 0; p < P && rc == MT_OK; ++p) {
+            const int64_t r0 = row(p), r1 = row(p + 1);
+            if (K == 0 || ck(cudaMemcpyAsync(Ad + r0 * K, A + r0 * K, (r1 - r0) * K * 4, cudaMemcpyDefault, h2d),
+                             "matmul_host: copy A panel"))
+                ck(cudaEventRecord(ev_a(p), h2d), "matmul_host: record");
+        }
+        for (int p = 0; p < P && rc == MT_OK; ++p) {
+            const int64_t r0 = row(p), r1 = row(p + 1);
+            if (!ck(cudaStreamWaitEvent(st, ev_a(p), 0), "matmul_host: wait")) break;
+            GemmProblem gp;
+            gp.A = Ad + r0 * K; gp.sa_b = 0; gp.sa_m = (int64_t)K; gp.sa_k = 1;
+            gp.B = Bd;          gp.sb_b = 0; gp.sb_k = (int64_t)N; gp.sb_n = 1;
+            gp.C = Cd + r0 * N; gp.sc_b = 0; gp.sc_m = (int64_t)N; gp.sc_n = 1;
+            gp.M = r1 - r0; gp.N = (int64_t)N; gp.K = (int64_t)K; gp.batch = 1;
+            gp.bias = nullptr; gp.epi = 0;
+            if ((rc = run_gemm(gp, mode, st)) != MT_OK) break;
+            ck(cudaEventRecord(ev_c(p), st), "matmul_host: record");
+        }
+        // Copies out after every GEMM is queued: a copy into pageable host memory returns
+        // only when it is done, which must not hold back the queueing of later panels.
+        for (int p = 0; p < P && rc == MT_OK; ++p) {
+            const int64_t r0 = row(p), r1 = row(p + 1);
+            if (ck(cudaStreamWaitEvent(d2h, ev_c(p), 0), "matmul_host: wait"))
+                ck(cudaMemcpyAsync(C + r0 * N, Cd + r0 * N, (r1 - r0) * N * 4, cudaMemcpyDefault, d2h),
+                   "matmul_host: copy C panel");
+        }
+    }
+    // Join: whatever was queued on the copy streams completes before st moves on, on the
+    // error paths too, so the workspace is never released under a copy in flight.
+    if (joined) {
+        cudaError_t e1 = cudaEventRecord(ev_h2d_tail, h2d);
+        cudaError_t e2 = cudaEventRecord(ev_d2h_tail, d2h);
+        cudaError_t e3 = e1 == cudaSuccess ? cudaStreamWaitEvent(st, ev_h2d_tail, 0) : e1;
+        cudaError_t e4 = e2 == cudaSuccess ? cudaStreamWaitEvent(st, ev_d2h_tail, 0) : e2;
+        if (e3 != cudaSuccess || e4 != cudaSuccess) {
+            // The copy streams could not be joined to st: wait for them here rather than free
+            // or return while they may still touch the workspace.
+            cudaStreamSynchronize(h2d);
+            cudaStreamSynchronize(d2h);
+            ck(e3 != cudaSuccess ? e3 : e4, "matmul_host: join");
+        }
+    }
+    if (owned) cudaFreeAsync(ws, st);
+    for (auto x : ev)
+        if (x) cudaEventDestroy(x);
+    if (rc == MT_OK) t_path = "matmul_host " + std::to_string(P) + " panels, last " + t_path;
+    return rc;
 }
 
 

@@ -99,6 +99,10 @@ def lib() -> ctypes.CDLL:
     L.mt_peer_barrier.restype = ctypes.c_int
     L.mt_copy_rows_async.argtypes = [vp, u64, vp, u64, u64, u64, vp]
     L.mt_copy_rows_async.restype = ctypes.c_int
+    L.mt_matmul_host.argtypes = [vp, vp, vp, u64, u64, u64, ctypes.c_int, ctypes.c_int, vp, ctypes.c_size_t, vp]
+    L.mt_matmul_host.restype = ctypes.c_int
+    L.mt_matmul_host_workspace_bytes.argtypes = [u64, u64, u64]
+    L.mt_matmul_host_workspace_bytes.restype = ctypes.c_size_t
     L.mt_set_default_mode.argtypes = [ctypes.c_int]
     L.mt_set_default_mode.restype = ctypes.c_int
     L.mt_get_default_mode.restype = ctypes.c_int
@@ -284,6 +288,47 @@ def linear_backward(x, W, dY, mode=MODE_DEFAULT, stream=None):
     db = torch.empty((1, dY.shape[1]), dtype=torch.float32, device=dY.device)
     sum_rows(dY, db, stream=stream)
     return dX, dW, db
+
+
+def matmul_host(A, B, C=None, mode=MODE_DEFAULT, panels=0, workspace=None, stream=None, sync=True):
+    """C = A @ B for host (CPU) float32 tensors through mt_matmul_host: the copies in, the
+    GEMM and the copies out overlap by row panels (pin A, B and C for the overlap). With
+    sync=True (the reference's to() is blocking) the call waits for `stream`; with
+    sync=False C is valid once the stream has completed."""
+    for name, t in (("A", A), ("B", B)):
+        if t.dim() != 2:
+            raise ValueError(f"matmul_host: {name} must be 2-D")
+    M, K = A.shape
+    if B.shape[0] != K:
+        raise ValueError("Dimension mismatch: A columns must match B rows.")
+    N = B.shape[1]
+    if C is None:
+        pin = A.is_pinned() and B.is_pinned()
+        C = torch.empty((M, N), dtype=torch.float32, pin_memory=pin)
+    for name, t in (("A", A), ("B", B), ("C", C)):
+        if t.dtype != torch.float32 or t.is_cuda or not t.is_contiguous():
+            raise ValueError(f"matmul_host: {name} must be a contiguous float32 host tensor")
+    if tuple(C.shape) != (M, N):
+        raise ValueError(f"matmul_host: C must be [{M}, {N}]")
+    ws, ws_bytes = None, 0
+    if workspace is not None:
+        if not workspace.is_cuda or not workspace.is_contiguous():
+            raise ValueError("matmul_host: workspace must be a contiguous CUDA tensor")
+        ws, ws_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
+    s = _stream(stream)
+    _check(lib().mt_matmul_host(A.data_ptr() if A.numel() else None, B.data_ptr() if B.numel() else None,
+                                C.data_ptr() if C.numel() else None, M, K, N, _mode(mode), int(panels), ws,
+                                ws_bytes, s))
+    if sync and torch.cuda.is_available():
+        if stream is None:
+            torch.cuda.current_stream().synchronize()
+        else:
+            torch.cuda.ExternalStream(s).synchronize()
+    return C
+
+
+def matmul_host_workspace_bytes(M, K, N) -> int:
+    return int(lib().mt_matmul_host_workspace_bytes(M, K, N))
 
 
 def bmm_backward(A, B, dC, mode=MODE_DEFAULT, stream=None):

@@ -153,3 +153,40 @@ def test_bmm_backward_shape_errors():
         engine.bmm_backward(_t(2, 3, 4), _t(2, 4, 5), _t(2, 3, 4))
     with pytest.raises(ValueError, match="dC must be"):
         engine.bmm_backward(_t(2, 3, 4), _t(2, 5, 5), _t(2, 3, 5))
+
+
+def test_matmul_host_argument_errors():
+    # Checked before any device call, so these run without a GPU.
+    lib = engine.lib()
+    buf = ctypes.create_string_buffer(4096)
+    p = ctypes.cast(buf, ctypes.c_void_p)
+    assert lib.mt_matmul_host(p, p, p, 4, 4, 4, 7, 0, None, 0, None) == engine.MT_EINVAL   # mode
+    assert b"bad mode" in lib.mt_last_error()
+    assert lib.mt_matmul_host(None, p, p, 4, 4, 4, 0, 0, None, 0, None) == engine.MT_EINVAL
+    assert lib.mt_matmul_host(p, p, None, 4, 4, 4, 0, 0, None, 0, None) == engine.MT_EINVAL
+    assert lib.mt_matmul_host(p, p, p, 1 << 31, 4, 4, 0, 0, None, 0, None) == engine.MT_EINVAL
+    need = lib.mt_matmul_host_workspace_bytes(4, 4, 4)
+    assert need >= 3 * 4 * 4 * 4
+    assert lib.mt_matmul_host(p, p, p, 4, 4, 4, 0, 0, p, need - 1, None) == engine.MT_EINVAL
+    assert b"workspace" in lib.mt_last_error()
+    assert lib.mt_matmul_host(p, p, p, 0, 4, 4, 0, 0, None, 0, None) == engine.MT_OK   # empty C
+    assert lib.mt_matmul_host(None, None, p, 4, 0, 0, 0, 0, None, 0, None) == engine.MT_OK
+
+
+def test_matmul_host_workspace_layout():
+    # A, B and C each start on a 256-byte boundary; the total covers all three.
+    for M, K, N in [(1, 1, 1), (1000, 520, 1200), (8192, 8192, 8192), (3, 0, 5)]:
+        n = engine.matmul_host_workspace_bytes(M, K, N)
+        up = lambda x: (x + 255) // 256 * 256
+        assert n == up(M * K * 4) + up(K * N * 4) + M * N * 4
+
+
+def test_matmul_host_python_checks():
+    with pytest.raises(ValueError, match="Dimension mismatch"):
+        engine.matmul_host(_t(3, 4), _t(5, 2))
+    with pytest.raises(ValueError, match="2-D"):
+        engine.matmul_host(_t(3, 4, 1), _t(4, 2))
+    with pytest.raises(ValueError, match="C must be"):
+        engine.matmul_host(_t(3, 4), _t(4, 2), C=_t(2, 3))
+    with pytest.raises(ValueError, match="host tensor"):
+        engine.matmul_host(_t(3, 4).t(), _t(3, 2))
