@@ -19,7 +19,7 @@
  *   - Launches are asynchronous on `stream` (NULL = legacy default stream, the
  *     reference's active_stream() default); nothing synchronises inside a call, so calls
  *     can be captured in CUDA graphs.
- *   - Device memory: three paths take stream-ordered scratch (cudaMallocAsync and
+ *   - Device memory: four paths take stream-ordered scratch (cudaMallocAsync and
  *     cudaFreeAsync on `stream`; inside a capture these become graph memory nodes):
  *       . a GEMM whose output has too few tiles to fill the GPU (batch 1, no extra
  *         destinations, at least 8 k-blocks): its k range is split, the fp32 partials go
@@ -27,7 +27,8 @@
  *       . a stride-1 tensor-core conv forward or input gradient: an NHWC copy of the
  *         activation (or of dY) and the weights reordered tap by tap;
  *       . the conv weight gradient, stated below (mt_conv2d_wgrad can take a caller
- *         workspace, mt_conv2d_wgrad_noalloc a fixed library array).
+ *         workspace, mt_conv2d_wgrad_noalloc a fixed library array);
+ *       . mt_matmul_host without a workspace: the device copies of A, B and C.
  *     Strict-fp32 calls and every other path allocate nothing.
  *   - Every function returns an mt_status and never throws; mt_last_error() gives the
  *     thread-local message of the last failure.
