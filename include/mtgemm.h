@@ -11,8 +11,9 @@
  * mt_last_error()).
  *
  * Conventions (the reference's, include/TensorOps.hpp:993-1149, include/GpuUtils.hpp):
- *   - All pointers are device pointers. The caller allocates every output with its final
- *     shape; the callee overwrites it (gradient accumulation stays with the caller).
+ *   - All pointers are device pointers (except the A, B and C of mt_matmul_host, which are
+ *     host buffers). The caller allocates every output with its final shape; the callee
+ *     overwrites it (gradient accumulation stays with the caller).
  *   - Inputs are borrowed views: data + offset is element (0,...,0); strides are in
  *     elements; stride 0 marks a broadcast (expand) dimension. Unlike the reference's
  *     matmul_gpu (src/gpu_ops.cpp:1125-1127), view offsets are always honoured.
