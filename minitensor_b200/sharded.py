@@ -220,6 +220,13 @@ class PeerLiveness:
                 raise PeerLost(f"rank {self.rank}: peer(s) {gone} left before step {e}")
             waiting = [r for r in waiting if not self.store.check([self._ready(e, r)])]
             if not waiting:
+                # Every peer has published step e, so each has left gate e - 1 and no longer
+                # reads this rank's key of that step: drop it (the store stays bounded).
+                if e > 1:
+                    try:
+                        self.store.delete_key(self._ready(e - 1, self.rank))
+                    except Exception:   # a store without deletion: the keys just remain
+                        pass
                 return e
             if time.monotonic() > deadline:
                 self._give_up()

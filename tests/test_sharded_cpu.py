@@ -122,6 +122,12 @@ def _live_worker(rank, world, port, out, scenario, timeout_s):
             os._exit(3)
         if rank == 1 and scenario == "late":
             time.sleep(3 * timeout_s)
+        if scenario == "ok":
+            log.append(f"step{gate.step()}")
+            dist.barrier()
+            # Keys of finished steps are dropped: only the latest step's remain.
+            stale = [k for k in (gate._ready(1, 0), gate._ready(1, 1)) if gate.store.check([k])]
+            log.append(f"stale{len(stale)}")
         for _ in range(2):
             t0 = time.monotonic()
             try:
@@ -164,7 +170,7 @@ def _lost_after(entry):
 
 def test_liveness_gate_all_ranks_step_together(tmp_path):
     r0, r1 = _run_live(tmp_path, "ok")
-    assert r0 == r1 == ["step1", "step2", "step3"]
+    assert r0 == r1 == ["step1", "step2", "stale0", "step3", "step4"]
 
 
 def test_liveness_peer_that_leaves_is_seen_before_next_step(tmp_path):
