@@ -30,6 +30,7 @@ from __future__ import annotations
 
 import ctypes
 import time
+import warnings
 
 import torch
 import torch.distributed as dist
@@ -115,17 +116,26 @@ class ShardedGemm:
         self.row_chunks = row_chunks(M, chunks)
         self._copy_streams = [torch.cuda.Stream() for _ in range(self.world - 1)] if gather == "copy" else []
 
+    # Distinct C tensors kept mapped before the caller is warned (see _peers).
+    MAX_BOUND_QUIET = 16
+
     def _peers(self, C: torch.Tensor) -> PeerTensor:
+        """Peer pointers of C. Every distinct C stays mapped on every rank (and alive) until
+        close(): unmapping earlier would need all ranks' in-flight steps to be finished."""
         key = (C.data_ptr(), C.numel())
         pt = self._bound.get(key)
         if pt is None:
             pt = PeerTensor(C, self.rank, self.world, self.group)
             self._bound[key] = pt
+            if len(self._bound) == self.MAX_BOUND_QUIET + 1:
+                warnings.warn("ShardedGemm keeps every distinct C tensor mapped on all ranks until close(); "
+                              "pass the same C each step", RuntimeWarning, stacklevel=3)
         return pt
 
     def run(self, A: torch.Tensor, B_shard: torch.Tensor, C: torch.Tensor, mode="tf32x3", stream=None):
-        """A [M,K] and B_shard [K, n1-n0] on this GPU; C [M,N] row-major on every rank
-        (the same C tensor across calls reuses the IPC mappings)."""
+        """A [M,K] and B_shard [K, n1-n0] on this GPU; C [M,N] row-major on every rank.
+        Pass the same C tensor each step: its IPC mappings are made once and reused, and
+        each new C adds mappings that last until close()."""
         if C.shape != (self.M, self.N) or not C.is_contiguous():
             raise ValueError("C must be a contiguous [M, N] tensor")
         if B_shard.shape != (self.K, self.n1 - self.n0) or A.shape != (self.M, self.K):
