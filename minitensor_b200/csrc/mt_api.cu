@@ -986,9 +986,12 @@ int conv_dgrad(const mt_tensor* dy, const mt_tensor* w, const mt_tensor* dx, uin
         return direct_launch(mt::conv::direct_dgrad_kernel, cp, total, st, who);
     }
     const bool x3 = mode == MT_TF32X3;
-    if (s.stride == 1 && s.Ho > 0 && s.Wo > 0 && s.kh - 1 - s.pad >= 0 && s.kw - 1 - s.pad >= 0) {
+    if (s.stride == 1 && s.kh == s.kw && s.Ho > 0 && s.Wo > 0 && s.kh - 1 - s.pad >= 0) {
         // Stride 1: dx = forward conv of NHWC dy with W flipped and transposed, padding
-        // kh-1-pad (the dy positions an input pixel receives from).
+        // kh-1-pad (the dy positions an input pixel receives from). The forward kernels take
+        // one padding for both dimensions, as the reference's conv does, so this mapping
+        // needs a square filter: kh != kw would need kw-1-pad across. Non-square filters
+        // take the gather kernel below, which indexes dy per dimension.
         const size_t bytes = fwd_tma_scratch(s.N, s.Ho, s.Wo, s.Co, s.C, s.kh * s.kw);
         float* scratch = nullptr;
         cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&scratch), bytes, st);

@@ -162,3 +162,31 @@ def test_conv_errors_and_empty(eng):
 
 def test_device_status_clean_after_conv(eng):
     assert eng.device_status(reset=True) == 0
+
+
+@pytest.mark.first_gpu_run
+@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("shape", [
+    # N, C, H, W, Co, kh, kw, stride, pad
+    (2, 6, 9, 11, 10, 3, 5, 1, 1),
+    (1, 33, 8, 12, 20, 1, 3, 1, 0),
+    (1, 64, 10, 10, 64, 3, 1, 1, 0),
+    (2, 4, 10, 7, 6, 5, 2, 2, 1),
+])
+def test_conv_non_square_filters(eng, port, mode, shape):
+    """kh != kw with the reference's single padding: the stride-1 input gradient cannot be
+    the forward kernel on flipped weights (that needs kh-1-pad down and kw-1-pad across)."""
+    N, C, H, W, Co, kh, kw, s, p = shape
+    x = inputs.normal((N, C, H, W), 1.0, 1400 + C)
+    w = inputs.normal((Co, C, kh, kw), float(np.sqrt(2.0 / (C * kh * kw))), 1500 + Co)
+    b = inputs.normal((Co,), 0.1, 1600)
+    Ho, Wo = (H + 2 * p - kh) // s + 1, (W + 2 * p - kw) // s + 1
+    dy = inputs.normal((N, Co, Ho, Wo), 1.0, 1700)
+    y, dx, dw, db = run_all(eng, x, w, b, dy, s, p, mode)
+    check(mode, y, port.conv2d(x, w, b, s, p), d_fwd(x, w, s, p) + np.abs(b)[None, :, None, None], C * kh * kw,
+          f"{shape} fwd")
+    check(mode, dx, port.conv2d_bwd_input(dy, w, x.shape, s, p), d_dgrad(dy, w, x.shape, s, p), Co * kh * kw,
+          f"{shape} dgrad")
+    check(mode, dw, port.conv2d_bwd_weight(dy, x, w.shape, s, p), d_wgrad(dy, x, w.shape, s, p), N * Ho * Wo,
+          f"{shape} wgrad")
+    assert np.allclose(db, port.conv2d_bwd_bias(dy), rtol=1e-5, atol=1e-5)
