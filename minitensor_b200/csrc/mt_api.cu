@@ -1316,8 +1316,15 @@ MT_API int mt_linear_fwd_gpu(const mt_tensor* X, const mt_tensor* W, const mt_te
         uint64_t n = 1;
         for (uint32_t i = 0; i < bias->ndim; ++i) n *= bias->shape[i];
         if ((int64_t)n != w.d[2]) return fail(MT_EINVAL, "linear: bias must hold out_features elements");
-        if (bias->ndim >= 1 && bias->strides[bias->ndim - 1] != 1 && n > 1)
-            return fail(MT_EINVAL, "linear: bias must be contiguous");
+        // The epilogue reads bias[0..n) densely: every dimension longer than 1 must have the
+        // stride of a contiguous layout ([1,out], [out] and [out,1] all qualify).
+        uint64_t expect = 1;
+        for (int i = (int)bias->ndim - 1; i >= 0; --i) {
+            if (bias->shape[i] > 1 && bias->strides[i] != expect)
+                return fail(MT_EINVAL, "linear: bias must be contiguous");
+            expect *= bias->shape[i];
+        }
+        if (n > 0 && !bias->data) return fail(MT_EINVAL, "linear: null bias data");
         bp = bias->data + bias->offset;
     }
     int epi = (bp ? MT_EPI_BIAS_COL : 0) | (relu ? MT_EPI_RELU : 0);

@@ -190,3 +190,21 @@ def test_matmul_host_python_checks():
         engine.matmul_host(_t(3, 4), _t(4, 2), C=_t(2, 3))
     with pytest.raises(ValueError, match="host tensor"):
         engine.matmul_host(_t(3, 4).t(), _t(3, 2))
+
+
+def test_linear_bias_layout_checked_before_the_call():
+    # The fused epilogue reads the bias densely; a strided bias view is refused up front.
+    lib = engine.lib()
+    X, W, Y = engine.view(_t(2, 3)), engine.view(_t(3, 4)), engine.view(_t(2, 4))
+    base = torch.zeros(4, 2)
+    col_strided = engine.view(base[:, :1])          # [4, 1] with row stride 2
+    assert lib.mt_linear_fwd_gpu(ctypes.byref(X), ctypes.byref(W), ctypes.byref(col_strided),
+                                 ctypes.byref(Y), 0, None) == engine.MT_EINVAL
+    assert b"contiguous" in lib.mt_last_error()
+    row_strided = engine.view(torch.zeros(1, 8)[:, ::2])   # [1, 4] with stride 2
+    assert lib.mt_linear_fwd_gpu(ctypes.byref(X), ctypes.byref(W), ctypes.byref(row_strided),
+                                 ctypes.byref(Y), 0, None) == engine.MT_EINVAL
+    short = engine.view(_t(1, 3))
+    assert lib.mt_linear_fwd_gpu(ctypes.byref(X), ctypes.byref(W), ctypes.byref(short),
+                                 ctypes.byref(Y), 0, None) == engine.MT_EINVAL
+    assert b"out_features" in lib.mt_last_error()
