@@ -190,3 +190,25 @@ def test_conv_non_square_filters(eng, port, mode, shape):
     check(mode, dw, port.conv2d_bwd_weight(dy, x, w.shape, s, p), d_wgrad(dy, x, w.shape, s, p), N * Ho * Wo,
           f"{shape} wgrad")
     assert np.allclose(db, port.conv2d_bwd_bias(dy), rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.first_gpu_run
+@pytest.mark.parametrize("mode", ["tf32", "tf32x3"])
+def test_conv_per_tap_fallback(eng, port, mode):
+    """A 7x7 filter over 200-pixel rows: two halo slots (128-pixel pitch x 7 rows) exceed the
+    227 KB of shared memory, so the forward and the input-grad take the per-tap TMA kernel."""
+    N, C, H, W, Co, k, s, p = 1, 32, 9, 200, 16, 7, 1, 3
+    x = inputs.normal((N, C, H, W), 1.0, 1800)
+    w = inputs.normal((Co, C, k, k), float(np.sqrt(2.0 / (C * k * k))), 1801)
+    b = inputs.normal((Co,), 0.1, 1802)
+    dy = inputs.normal((N, Co, H, W), 1.0, 1803)
+    xd, wd = dev(x), dev(w)
+    y = eng.conv2d(xd, wd, dev(b), s, p, mode=mode)
+    assert "tma bn=" in eng.last_path(), eng.last_path()
+    dx, dw, _ = eng.conv2d_backward(dev(dy), xd, wd, s, p, need=("input", "weight"), mode=mode)
+    check(mode, host(y), port.conv2d(x, w, b, s, p), d_fwd(x, w, s, p) + np.abs(b)[None, :, None, None],
+          C * k * k, "per-tap fwd")
+    check(mode, host(dx), port.conv2d_bwd_input(dy, w, x.shape, s, p), d_dgrad(dy, w, x.shape, s, p), Co * k * k,
+          "per-tap dgrad")
+    check(mode, host(dw), port.conv2d_bwd_weight(dy, x, w.shape, s, p), d_wgrad(dy, x, w.shape, s, p), N * H * W,
+          "per-tap shape wgrad")
