@@ -351,3 +351,18 @@ def test_bmm_backward(eng, port, mode, case):
         check(mode, host(dB)[0], dB_ref.astype(np.float64).sum(0), DB.sum(0), bt * M, f"{case} dB (summed)")
     else:
         check(mode, host(dB), dB_ref, DB, M, f"{case} dB")
+
+
+@pytest.mark.first_gpu_run
+@pytest.mark.parametrize("mode", ["tf32", "tf32x3"])
+def test_one_cta_wide_tiles_batched_short_rows(eng, port, mode):
+    """Batched outputs with M <= 128 and enough 128x256 tiles to fill the GPU: too short for
+    CTA pairs, too many tiles for the small-output path, so the one-CTA 256-wide kernel."""
+    Bt, M, N, K = 40, 100, 1000, 72
+    A = inputs.uniform((Bt, M, K), -1, 1, 140)
+    B = inputs.uniform((Bt, K, N), -1, 1, 141)
+    C = torch.empty(Bt, M, N, device="cuda")
+    eng.gemm(dev(A), dev(B), C, mode=mode)
+    path = eng.last_path()
+    assert path.startswith(f"umma_{mode} bn=256"), path
+    check(mode, host(C), port.bmm(A, B), absmm(A, B), K, "one-CTA bn=256 batched")
