@@ -132,6 +132,31 @@ def _cuda(a):
     return torch.from_numpy(np.ascontiguousarray(a)).cuda()
 
 
+# Parity bound of north_star: strict fp32 and 3xTF32 within 1e-5 sqrt(K), TF32 within 2e-3 sqrt(K)
+# of the reference CPU result, with the error of each element scaled by (|A|.|B|) there.
+PARITY_TOL = {"strict": 1e-5, "tf32x3": 1e-5, "tf32": 2e-3}
+
+
+def _rel_err(C, C_ref, D):
+    C, C_ref, D = (np.asarray(a, np.float64) for a in (C, C_ref, D))
+    if C.size == 0:
+        return 0.0
+    return float(np.max(np.abs(C - C_ref) / np.maximum(D, 1e-30)))
+
+
+def _parity(mode, parts, sample):
+    """parts: (name, C_gpu, C_ref, D, K). One entry per output, worst ratio to the bound."""
+    out = {"sample": sample, "checker": "oracle (C restatement of the reference CPU path)", "outputs": {}}
+    worst = 0.0
+    for name, C, C_ref, D, K in parts:
+        r, t = _rel_err(C, C_ref, D), PARITY_TOL[mode] * np.sqrt(max(K, 1))
+        out["outputs"][name] = {"rel_err": r, "tol": float(t), "K": int(K)}
+        worst = max(worst, r / t)
+    out["worst_err_over_tol"] = worst
+    out["ok"] = bool(worst <= 1.0 and all(np.isfinite(C).all() for _, C, _, _, _ in parts))
+    return out
+
+
 # ------------------------------------------------------------------ workloads --------
 class Workload:
     """One configuration. Host inputs always exist; gpu=True also builds device buffers.
@@ -153,6 +178,10 @@ class Workload:
 
     def cpu_sample(self, threads):
         """(TFLOP/s, seconds, kind, sample description) of the reference CPU path."""
+        raise NotImplementedError
+
+    def parity(self, mode, threads):
+        """Compares the outputs of the last step (run in `mode`) with the oracle on a sample."""
         raise NotImplementedError
 
 
@@ -200,6 +229,19 @@ class C5(Workload):
         return (2.0 * rows * self.n * self.n / dt / 1e12, dt, kind,
                 f"C rows 0..{rows - 1} of config5 ({rows} x {self.n} x {self.n}), {threads} threads")
 
+    def parity(self, mode, threads):
+        import oracle
+        n = self.n
+        # First and last rows, both sides of the 128- and 256-row tile edges, the middle.
+        rows = sorted({r for r in (0, 1, 127, 128, 255, 256, n // 2 - 1, n // 2, n - 257, n - 256, n - 2, n - 1)
+                       if 0 <= r < n})
+        A_s = np.ascontiguousarray(self.A_h[rows])
+        C_ref = oracle.Port().matmul_rows(A_s, self.B_h, 0, len(rows), min(threads, len(rows)))
+        D = np.abs(A_s.astype(np.float64)) @ np.abs(self.B_h.astype(np.float64))
+        C = self.C[rows].cpu().numpy()
+        return _parity(mode, [("C", C, C_ref, D, n)],
+                       f"{len(rows)} full rows of C (every column, so every rank's shard): {rows}")
+
 
 class C1(Workload):
     name = "c1"
@@ -230,6 +272,12 @@ class C1(Workload):
         impl.matmul(self.A_h, self.B_h)
         dt = time.perf_counter() - t0
         return self.flops / dt / 1e12, dt, kind, "the whole 512^3 matmul, 1 thread (matmul_cpu is serial)"
+
+    def parity(self, mode, threads):
+        import oracle
+        C_ref = oracle.Port().matmul(self.A_h, self.B_h)
+        D = np.abs(self.A_h.astype(np.float64)) @ np.abs(self.B_h.astype(np.float64))
+        return _parity(mode, [("C", self.C.cpu().numpy(), C_ref, D, 512)], "the whole C")
 
 
 class C2(Workload):
@@ -281,6 +329,25 @@ class C2(Workload):
         return (3 * 2.0 * rows * 1024 * 4096 / dt / 1e12, dt, kind,
                 f"Linear fwd+bwd on {rows} of 256 batch rows, 1 thread (the reference CPU path is serial)")
 
+    def parity(self, mode, threads):
+        import oracle
+        P = oracle.Port()
+        X, W, b, dY = self.host
+        f64 = lambda a: np.abs(a.astype(np.float64))   # noqa: E731
+        ry = [0, 1, 127, 128, 254, 255]        # rows of Y and dX
+        rw = [0, 1, 511, 512, 1022, 1023]      # rows of dW
+        Xs, dYs = np.ascontiguousarray(X[ry]), np.ascontiguousarray(dY[ry])
+        Y_ref = P.linear_fwd(Xs, W, b)
+        dX_ref = P.matmul_strided(dYs, W.T)
+        XT = np.ascontiguousarray(X.T[rw])
+        dW_ref = P.matmul_strided(XT, dY)
+        db_ref = dY.astype(np.float64).sum(axis=0)
+        parts = [("Y", self.Y[ry].cpu().numpy(), Y_ref, f64(Xs) @ f64(W) + np.abs(b), 1024),
+                 ("dX", self.dX[ry].cpu().numpy(), dX_ref, f64(dYs) @ f64(W.T), 4096),
+                 ("dW", self.dW[rw].cpu().numpy(), dW_ref, f64(XT) @ f64(dY), 256),
+                 ("db", self.db.cpu().numpy().reshape(-1), db_ref, f64(dY).sum(axis=0), 256)]
+        return _parity(mode, parts, f"Y and dX rows {ry}, dW rows {rw}, all of db")
+
 
 class C3(Workload):
     name = "c3"
@@ -316,6 +383,14 @@ class C3(Workload):
             impl.bmm(self.A_h[:nb], np.broadcast_to(self.B0_h, (nb, 64, 512)))
         dt = time.perf_counter() - t0
         return 2.0 * nb * 512 * 512 * 64 / dt / 1e12, dt, kind, f"bmm on {nb} of 64 batches, 1 thread"
+
+    def parity(self, mode, threads):
+        import oracle
+        bs = [0, 1, 31, 63]
+        A_s = np.ascontiguousarray(self.A_h[bs])
+        C_ref = oracle.Port().bmm(A_s, np.broadcast_to(self.B0_h, (len(bs), 64, 512)))
+        D = np.abs(A_s.astype(np.float64)) @ np.abs(self.B0_h.astype(np.float64))
+        return _parity(mode, [("C", self.C[bs].cpu().numpy(), C_ref, D, 64)], f"batches {bs} of 64, whole")
 
 
 class C4(Workload):
@@ -369,6 +444,20 @@ class C4(Workload):
         dt = time.perf_counter() - t0
         return (2 * 2.0 * n * 56 * 56 * 64 * 576 / dt / 1e12, dt, kind,
                 f"conv forward + backward on {n} of 32 images, 1 thread")
+
+    def parity(self, mode, threads):
+        import oracle
+        P = oracle.Port()
+        x, w, b, dy = self.host
+        ims = [0, 31]
+        xs = np.ascontiguousarray(x[ims])
+        y_ref = P.conv2d(xs, w, b, 1, 1, threads)
+        D_y = P.conv2d(np.abs(xs), np.abs(w), np.abs(b), 1, 1, threads)
+        dw_ref = P.conv2d_bwd_weight(dy, x, w.shape, 1, 1, threads)
+        D_w = P.conv2d_bwd_weight(np.abs(dy), np.abs(x), w.shape, 1, 1, threads)
+        parts = [("y", self.y[ims].cpu().numpy(), y_ref, D_y, 576),
+                 ("dW", self.dw.cpu().numpy(), dw_ref, D_w, 32 * 56 * 56)]
+        return _parity(mode, parts, f"y of images {ims}; the whole dW (a sum over all 32 images)")
 
 
 def make_workload(args, rank, world, gpu=True):
@@ -485,6 +574,16 @@ def run_gpu(args, rank, world, local_rank):
     path = engine.last_path()
     tflops = wl.flops * args.steps / t / 1e12
     ms = t / args.steps * 1e3
+
+    # Output parity of the timed mode (rank 0 holds the whole C at every N), before the
+    # other modes overwrite the outputs. Outside the timed region.
+    par = None
+    if rank == 0:
+        try:
+            torch.cuda.synchronize()
+            par = wl.parity(args.mode, cpu_threads())
+        except Exception as exc:
+            par = {"error": f"{type(exc).__name__}: {exc}"[:200], "ok": False}
 
     extras, e2e, cpu, e2e_ov = {}, None, None, None
     if not args.no_extras:
@@ -615,7 +714,7 @@ def run_gpu(args, rank, world, local_rank):
                                   if world > 1 else "single GPU",
                    "l2": "inputs larger than the 126 MB L2, no flush" if wl.name == "c5" else
                          "steps back to back without an L2 flush (working set fits L2)"},
-        "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "e2e_overlapped": e2e_ov, "modes": extras,
+        "roofline": roofline, "parity": par, "cpu_baseline": cpu, "e2e": e2e, "e2e_overlapped": e2e_ov, "modes": extras,
         "clocks": clk.summary(), "gpu_launches": launches,
     }
     print(json.dumps(line), flush=True)

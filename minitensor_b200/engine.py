@@ -460,11 +460,11 @@ def conv2d_wgrad_workspace_bytes(dy, x, w_shape, stride, padding, mode=MODE_DEFA
     # dW is described by shape alone (contiguous, no storage): only its sizes are read.
     v = MtTensor()
     v.ndim = 4
-    stride = 1
+    elem_stride = 1
     for i in reversed(range(4)):
         v.shape[i] = w_shape[i]
-        v.strides[i] = stride
-        stride *= w_shape[i]
+        v.strides[i] = elem_stride
+        elem_stride *= w_shape[i]
     return int(lib().mt_conv2d_wgrad_workspace_bytes(_ref(view(dy)), _ref(view(x)), _ref(v), stride, padding,
                                                      _mode(mode)))
 

@@ -16,8 +16,10 @@ def pytest_configure(config):
 def pytest_collection_modifyitems(config, items):
     # Tests still waiting for their first pass on a GPU run after the established suite, so
     # that a failure among them (under -x) cannot hide the results of the others. They
-    # still run and still fail the suite.
-    items.sort(key=lambda it: it.get_closest_marker("first_gpu_run") is not None)
+    # still run and still fail the suite. The no-allocation entry point's file
+    # (test_zz_no_alloc.py) always runs last of all.
+    items.sort(key=lambda it: (os.path.basename(str(it.fspath)).startswith("test_zz_"),
+                               it.get_closest_marker("first_gpu_run") is not None))
 
 
 @pytest.fixture(scope="session")

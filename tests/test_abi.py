@@ -138,10 +138,26 @@ def test_gemm_bias_is_checked_before_the_call():
         engine.gemm(A, B, C, bias=_t(5, 2)[:, 0], epi=engine.EPI_BIAS_COL)
 
 
-def test_workspace_query_describes_dw_by_shape():
-    # Host-only: the query reads sizes; a bad shape comes back as 0 bytes, not a crash.
-    n = engine.conv2d_wgrad_workspace_bytes(_t(2, 4, 6, 6), _t(2, 3, 6, 6), (4, 3, 3, 3), 1, 1, "tf32")
-    assert n >= 0
+def _sms():
+    return torch.cuda.get_device_properties(0).multi_processor_count if torch.cuda.is_available() else 0
+
+
+@pytest.mark.parametrize("mode,x3", [("tf32", False), ("tf32x3", True)])
+def test_workspace_query_describes_dw_by_shape(mode, x3):
+    # Host-only: dW is described by its shape alone; the conv stride and padding pass through.
+    from wgrad_plan import tma_bytes
+    N, C, H, W, Co, k = 2, 32, 8, 8, 32, 3
+    n = engine.conv2d_wgrad_workspace_bytes(_t(N, Co, H, W), _t(N, C, H, W), (Co, C, k, k), 1, 1, mode)
+    want, _ = tma_bytes(N, C, H, W, Co, k, k, H, W, _sms(), x3)
+    assert n == want > 0
+    # Stride 2: the gather plan, whose only scratch is the split-K partials.
+    n2 = engine.conv2d_wgrad_workspace_bytes(_t(N, Co, 4, 4), _t(N, C, H, W), (Co, C, k, k), 2, 1, mode)
+    from wgrad_plan import gather_bytes
+    assert n2 == gather_bytes(N, C, Co, k, k, 4, 4, _sms())[0]
+    # A stride or padding that does not produce dy's shape: 0 bytes, not a crash.
+    assert engine.conv2d_wgrad_workspace_bytes(_t(N, Co, H, W), _t(N, C, H, W), (Co, C, k, k), 2, 1, mode) == 0
+    assert engine.conv2d_wgrad_workspace_bytes(_t(N, Co, H, W), _t(N, C, H, W), (Co, C, k, k), 1, 0, mode) == 0
+    assert engine.conv2d_wgrad_workspace_bytes(_t(N, Co, H, W), _t(N, C, H, W), (Co, C, k, k), 1, 1, "strict") == 0
 
 
 def test_bmm_backward_shape_errors():
