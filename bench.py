@@ -157,6 +157,46 @@ def _parity(mode, parts, sample):
     return out
 
 
+class RefGpu:
+    """The reference's own GPU kernels (src/gpu_ops.cpp compiled unmodified for sm_100a)
+    behind baseline/ref_gpu.cpp: the same-hardware baseline. Not the product, not an oracle."""
+    PATH = os.path.join(ROOT, "baseline", "_ref", "libref_gpu.so")
+
+    def __init__(self):
+        f, i64, ci = ctypes.POINTER(ctypes.c_float), ctypes.c_int64, ctypes.c_int
+        fo = ctypes.POINTER(ctypes.c_float)
+        self.L = L = ctypes.CDLL(self.PATH)
+        L.ref_gpu_error.restype = ctypes.c_char_p
+        L.ref_gpu_matmul.argtypes = [f, f, f, i64, i64, i64, ci, ci, fo]
+        L.ref_gpu_linear_step.argtypes = [f, f, f, f, f, f, i64, i64, i64, ci, ci, fo]
+        L.ref_gpu_bmm_bcast.argtypes = [f, f, f, i64, i64, i64, i64, ci, ci, fo]
+        L.ref_gpu_conv_step.argtypes = [f, f, f, f, f, f] + [i64] * 8 + [ci, ci, fo]
+
+    def call(self, name, *args):
+        ms = ctypes.c_float(0.0)
+        rc = getattr(self.L, name)(*args, ctypes.byref(ms))
+        if rc != 0:
+            raise RuntimeError(f"{name}: {self.L.ref_gpu_error().decode()}")
+        return ms.value
+
+
+def _fp(a):
+    return a.ctypes.data_as(ctypes.POINTER(ctypes.c_float)) if a is not None else None
+
+
+def ref_gpu_line(wl, warmup=1, iters=3):
+    """Times the reference's GPU kernels on wl's configuration (rank 0, N = 1)."""
+    if not os.path.exists(RefGpu.PATH):
+        return {"unavailable": "baseline/_ref/libref_gpu.so not built (needs the reference checkout at build time)"}
+    try:
+        out = wl.ref_gpu(RefGpu(), warmup, iters)
+        out["what"] = ("the reference's own GPU kernels (src/gpu_ops.cpp, unmodified) compiled for sm_100a, "
+                       "timed with CUDA events on this GPU")
+        return out
+    except Exception as exc:
+        return {"error": f"{type(exc).__name__}: {exc}"[:200]}
+
+
 # ------------------------------------------------------------------ workloads --------
 class Workload:
     """One configuration. Host inputs always exist; gpu=True also builds device buffers.
@@ -242,6 +282,19 @@ class C5(Workload):
         return _parity(mode, [("C", C, C_ref, D, n)],
                        f"{len(rows)} full rows of C (every column, so every rank's shard): {rows}")
 
+    def ref_gpu(self, R, warmup, iters):
+        import oracle
+        n = self.n
+        C = np.empty((n, n), np.float32)
+        ms = R.call("ref_gpu_matmul", _fp(self.A_h), _fp(self.B_h), _fp(C), n, n, n, warmup, iters)
+        rows = [0, n // 2, n - 1]
+        A_s = np.ascontiguousarray(self.A_h[rows])
+        C_ref = oracle.Port().matmul_rows(A_s, self.B_h, 0, len(rows), len(rows))
+        D = np.abs(A_s.astype(np.float64)) @ np.abs(self.B_h.astype(np.float64))
+        return {"value": self.flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms,
+                "kernels": "matmul_gpu -> sgemm_kernel_v2 (src/gpu_ops.cpp:932-1101)",
+                "rel_err_vs_cpu": _rel_err(C[rows], C_ref, D)}
+
 
 class C1(Workload):
     name = "c1"
@@ -278,6 +331,15 @@ class C1(Workload):
         C_ref = oracle.Port().matmul(self.A_h, self.B_h)
         D = np.abs(self.A_h.astype(np.float64)) @ np.abs(self.B_h.astype(np.float64))
         return _parity(mode, [("C", self.C.cpu().numpy(), C_ref, D, 512)], "the whole C")
+
+    def ref_gpu(self, R, warmup, iters):
+        import oracle
+        C = np.empty((512, 512), np.float32)
+        ms = R.call("ref_gpu_matmul", _fp(self.A_h), _fp(self.B_h), _fp(C), 512, 512, 512, 5, 50)
+        D = np.abs(self.A_h.astype(np.float64)) @ np.abs(self.B_h.astype(np.float64))
+        return {"value": self.flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms,
+                "kernels": "matmul_gpu -> sgemm_kernel_v2 (src/gpu_ops.cpp:932-1101)",
+                "rel_err_vs_cpu": _rel_err(C, oracle.Port().matmul(self.A_h, self.B_h), D)}
 
 
 class C2(Workload):
@@ -348,6 +410,15 @@ class C2(Workload):
                  ("db", self.db.cpu().numpy().reshape(-1), db_ref, f64(dY).sum(axis=0), 256)]
         return _parity(mode, parts, f"Y and dX rows {ry}, dW rows {rw}, all of db")
 
+    def ref_gpu(self, R, warmup, iters):
+        X, W, b, dY = self.host
+        Y, dX, dW = (np.empty(s, np.float32) for s in ((256, 4096), (256, 1024), (1024, 4096)))
+        ms = R.call("ref_gpu_linear_step", _fp(X), _fp(W), _fp(dY), _fp(Y), _fp(dX), _fp(dW), 256, 1024, 4096,
+                    2, 10)
+        return {"value": 3 * 2.0 * 256 * 1024 * 4096 / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms,
+                "kernels": "Y: matmul_gpu (sgemm_kernel_v2); dX, dW: matmul_gpu_strided -> matmul_kernel_strided "
+                           "(src/gpu_ops.cpp:909-930) on transposed views; bias add and db not included"}
+
 
 class C3(Workload):
     name = "c3"
@@ -391,6 +462,18 @@ class C3(Workload):
         C_ref = oracle.Port().bmm(A_s, np.broadcast_to(self.B0_h, (len(bs), 64, 512)))
         D = np.abs(A_s.astype(np.float64)) @ np.abs(self.B0_h.astype(np.float64))
         return _parity(mode, [("C", self.C[bs].cpu().numpy(), C_ref, D, 64)], f"batches {bs} of 64, whole")
+
+    def ref_gpu(self, R, warmup, iters):
+        import oracle
+        C = np.empty((64, 512, 512), np.float32)
+        ms = R.call("ref_gpu_bmm_bcast", _fp(self.A_h), _fp(self.B0_h), _fp(C), 64, 512, 64, 512, 2, 10)
+        C_ref = oracle.Port().bmm(self.A_h[:2], np.broadcast_to(self.B0_h, (2, 64, 512)))
+        D = np.abs(self.A_h[:2].astype(np.float64)) @ np.abs(self.B0_h.astype(np.float64))
+        return {"value": self.flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms,
+                "kernels": "expand().contiguous() + 64 x matmul_gpu (sgemm_kernel_v2) on batch slices",
+                "note": "timed, output incorrect: matmul_gpu ignores the slice offset (src/gpu_ops.cpp:1125-1127)",
+                "rel_err_vs_cpu_batch0": _rel_err(C[0], C_ref[0], D[0]),
+                "rel_err_vs_cpu_batch1": _rel_err(C[1], C_ref[1], D[1])}
 
 
 class C4(Workload):
@@ -458,6 +541,15 @@ class C4(Workload):
         parts = [("y", self.y[ims].cpu().numpy(), y_ref, D_y, 576),
                  ("dW", self.dw.cpu().numpy(), dw_ref, D_w, 32 * 56 * 56)]
         return _parity(mode, parts, f"y of images {ims}; the whole dW (a sum over all 32 images)")
+
+    def ref_gpu(self, R, warmup, iters):
+        x, w, b, dy = self.host
+        y, dw = np.empty(x.shape, np.float32), np.empty(w.shape, np.float32)
+        ms = R.call("ref_gpu_conv_step", _fp(x), _fp(w), _fp(b), _fp(dy), _fp(y), _fp(dw), 32, 64, 56, 56, 64, 3,
+                    1, 1, 2, 10)
+        return {"value": self.flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms,
+                "kernels": "conv2d_gpu (im2col + batched_sgemm_kernel_v2, src/gpu_ops.cpp:2237-2325) + "
+                           "conv2d_backward_weight_gpu (src/gpu_ops.cpp:2623-2713)"}
 
 
 def make_workload(args, rank, world, gpu=True):
@@ -585,7 +677,7 @@ def run_gpu(args, rank, world, local_rank):
         except Exception as exc:
             par = {"error": f"{type(exc).__name__}: {exc}"[:200], "ok": False}
 
-    extras, e2e, cpu, e2e_ov = {}, None, None, None
+    extras, e2e, cpu, e2e_ov, ref_gpu = {}, None, None, None, None
     if not args.no_extras:
         for m in ("tf32", "tf32x3", "strict"):
             if m == args.mode:
@@ -638,6 +730,9 @@ def run_gpu(args, rank, world, local_rank):
                "h2d_bytes_per_step": int(sum(h.numel() * h.element_size() for h, _ in wl.h2d)),
                "d2h_bytes_per_step": int(sum(h.numel() * h.element_size() for _, h in wl.d2h))}
         if rank == 0 and world == 1:
+            torch.cuda.synchronize()
+            ref_gpu = ref_gpu_line(wl)
+            torch.cuda.synchronize()
             v, dt, kind, sample = wl.cpu_sample(cpu_threads())
             cpu = {"value": v, "unit": "TFLOP/s", "cores": cpu_threads() if wl.name == "c5" else 1,
                    "kind": kind, "sample": f"{sample} ({dt:.2f} s)"}
@@ -714,7 +809,7 @@ def run_gpu(args, rank, world, local_rank):
                                   if world > 1 else "single GPU",
                    "l2": "inputs larger than the 126 MB L2, no flush" if wl.name == "c5" else
                          "steps back to back without an L2 flush (working set fits L2)"},
-        "roofline": roofline, "parity": par, "cpu_baseline": cpu, "e2e": e2e, "e2e_overlapped": e2e_ov, "modes": extras,
+        "roofline": roofline, "parity": par, "cpu_baseline": cpu, "ref_gpu_baseline": ref_gpu, "e2e": e2e, "e2e_overlapped": e2e_ov, "modes": extras,
         "clocks": clk.summary(), "gpu_launches": launches,
     }
     print(json.dumps(line), flush=True)

@@ -172,9 +172,11 @@ MT_API size_t mt_conv2d_wgrad_workspace_bytes(const mt_tensor* dy, const mt_tens
  * computes what mt_conv2d_wgrad computes, with the split-K partials in a fixed 8 MiB
  * array inside the library (one per GPU, held until the process exits); problems whose
  * partials need more get MT_EINVAL with the size in the message. The first call on a
- * device looks up that array's device address, so make it before any stream capture.
- * All calls on a device share the array: calls that overlap on the GPU (other streams,
- * other host threads) race and must be serialised by the caller. */
+ * device looks up that array's device address, so make it before any stream capture
+ * (after a device reset, the first call looks it up again). It always takes the gather
+ * kernel, whose only scratch is those partials. All calls on a device share the array:
+ * calls that overlap on the GPU (other streams, other host threads) race and must be
+ * serialised by the caller. */
 MT_API int mt_conv2d_wgrad_noalloc(const mt_tensor* dy, const mt_tensor* x, const mt_tensor* dw, uint64_t stride,
                                    uint64_t padding, int mode, void* stream);
 
@@ -224,7 +226,8 @@ MT_API int mt_gemm_multi(const mt_tensor* A, const mt_tensor* B, const mt_tensor
 /* Stream-ordered cross-GPU barrier: flags[d] is rank d's array of `world` ints (peer-mapped,
  * zero-initialised). Rank `rank` stores `epoch` into flags[d][rank] for every d, then waits
  * until flags[rank][*] == epoch. The wait gives up after timeout_ns and records status 6 in
- * the device status word (mt_device_status) instead of hanging. */
+ * the device status word (mt_device_status) instead of hanging. timeout_ns above 60 s
+ * (60e9) is refused with MT_EINVAL, so that every device-side wait stays bounded. */
 MT_API int mt_peer_barrier(int* const* flags, int rank, int world, int epoch, uint64_t timeout_ns, void* stream);
 
 /* Stream-ordered 2-D copy of `rows` rows of `width_bytes` bytes (row pitches dpitch /

@@ -46,7 +46,22 @@ def up_to_date() -> bool:
     return all(os.path.getmtime(d) <= t for d in deps())
 
 
+INPUTS_SRC = os.path.join(PKG, "inputs_gen.c")
+INPUTS_LIB = os.path.join(PKG, "libmtinputs.so")
+
+
+def build_inputs(force: bool = False) -> str:
+    """libmtinputs.so: the seeded synthetic-input generator (host C, no FMA contraction)."""
+    if not force and os.path.exists(INPUTS_LIB) and os.path.getmtime(INPUTS_LIB) >= os.path.getmtime(INPUTS_SRC):
+        return INPUTS_LIB
+    subprocess.check_call(["gcc", "-O2", "-ffp-contract=off", "-fPIC", "-shared", "-o", INPUTS_LIB + ".tmp",
+                           INPUTS_SRC, "-lm"])
+    os.replace(INPUTS_LIB + ".tmp", INPUTS_LIB)
+    return INPUTS_LIB
+
+
 def build(verbose: bool = False, force: bool = False) -> str:
+    build_inputs(force)
     if not force and up_to_date():
         return LIB
     cmd = [nvcc(), *ARCH, "-lineinfo", "-O3", "-std=c++17", "--expt-relaxed-constexpr",
@@ -105,7 +120,35 @@ def build_dropin(ref_root: str = REF_ROOT) -> str | None:
     return DROPIN_BIN
 
 
+REFGPU_SRC = os.path.join(ROOT, "baseline", "ref_gpu.cpp")
+REFGPU_LIB = os.path.join(ROOT, "baseline", "_ref", "libref_gpu.so")
+
+
+def build_refgpu(ref_root: str = REF_ROOT) -> str | None:
+    """baseline/_ref/libref_gpu.so: the reference's own GPU kernels (src/gpu_ops.cpp compiled
+    unmodified for sm_100a, its headers unmodified) behind the timing shim
+    baseline/ref_gpu.cpp -- the same-hardware baseline bench.py reports. Needs the
+    reference checkout; returns None without it (the built library travels)."""
+    src = os.path.join(ref_root, "src", "gpu_ops.cpp")
+    if not os.path.exists(src):
+        return None
+    os.makedirs(DROPIN_OUT, exist_ok=True)
+    os.makedirs(os.path.dirname(REFGPU_LIB), exist_ok=True)
+    ref_inc = os.path.join(ref_root, "include")
+    cuda_inc = os.path.join(os.path.dirname(os.path.dirname(nvcc())), "include")
+    ref_obj = os.path.join(DROPIN_OUT, "ref_gpu_ops.o")
+    if not os.path.exists(ref_obj) or os.path.getmtime(ref_obj) < os.path.getmtime(src):
+        _run([nvcc(), "-x", "cu", "-std=c++20", "-DUSE_CUDA", *ARCH, "-O3", "-w", "-Xcompiler", "-fPIC",
+              "-I", ref_inc, "-c", src, "-o", ref_obj])
+    shim_obj = os.path.join(DROPIN_OUT, "ref_gpu_shim.o")
+    _run(["g++", "-std=c++20", "-O2", "-fPIC", "-DUSE_CUDA", "-I", ref_inc, "-I", cuda_inc, "-c", REFGPU_SRC,
+          "-o", shim_obj])
+    _run([nvcc(), *ARCH, "-shared", "-Xcompiler", "-fPIC", "-o", REFGPU_LIB, shim_obj, ref_obj])
+    return REFGPU_LIB
+
+
 if __name__ == "__main__":
     print(build(verbose="--verbose" in sys.argv, force=True))
     if "--dropin" in sys.argv:
         print(build_dropin())
+        print(build_refgpu())

@@ -1574,22 +1574,50 @@ MT_API int mt_conv2d_wgrad(const mt_tensor* dy, const mt_tensor* x, const mt_ten
 constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;   // 8 MiB of partials per GPU
 static __device__ __align__(256) float g_wgrad_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
 
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+
+CtxGetCurrentFn ctx_current_fn() {
+    static CtxGetCurrentFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<CtxGetCurrentFn>(p);
+    });
+    return fn;
+}
+
 // Device address of the array on the current device. On the host the array's name is
 // only a stand-in symbol, so the address is looked up once per device (with that device
-// current) and cached.
+// current) and cached together with the context it belongs to: after a device reset the
+// runtime makes a new context and loads the module again, and the next call looks the
+// address up afresh.
 int noalloc_scratch(float** out) {
     static std::mutex mu;
     static float* cache[64] = {};
+    static CUcontext cache_ctx[64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cuda_fail(e, "conv2d_wgrad_noalloc: cudaGetDevice");
     if (dev < 0 || dev >= 64) return fail(MT_EUNSUPPORTED, "conv2d_wgrad_noalloc: device index %d", dev);
+    CtxGetCurrentFn cur = ctx_current_fn();
+    auto current = [cur]() {
+        CUcontext c = nullptr;
+        if (!cur || cur(&c) != CUDA_SUCCESS) c = nullptr;
+        return c;
+    };
+    // A thread whose context the runtime has not set up yet reads null here; the lookup
+    // below sets it up, and the context is read again after it.
+    CUcontext ctx = current();
     std::lock_guard<std::mutex> g(mu);
-    if (!cache[dev]) {
+    if (!cache[dev] || !ctx || cache_ctx[dev] != ctx) {
         void* ptr = nullptr;
         e = cudaGetSymbolAddress(&ptr, g_wgrad_noalloc_scratch);
         if (e != cudaSuccess) return cuda_fail(e, "conv2d_wgrad_noalloc: cudaGetSymbolAddress");
         cache[dev] = static_cast<float*>(ptr);
+        cache_ctx[dev] = current();
     }
     *out = cache[dev];
     return MT_OK;
@@ -1633,6 +1661,9 @@ MT_API size_t mt_conv2d_wgrad_workspace_bytes(const mt_tensor* dy, const mt_tens
 
 
 // ---- multi-GPU: peer memory and the GEMM that writes every rank's output -------------
+
+// Longest wait mt_peer_barrier accepts (60 s): every device-side wait has a bound.
+constexpr uint64_t kMaxPeerWaitNs = 60ull * 1000 * 1000 * 1000;
 
 MT_API int mt_ipc_get_handle(const void* dptr, void* handle_out, uint64_t* offset_out) {
     if (!dptr || !handle_out || !offset_out) return fail(MT_EINVAL, "ipc_get_handle: null argument");
@@ -1710,6 +1741,10 @@ MT_API int mt_gemm_multi(const mt_tensor* A, const mt_tensor* B, const mt_tensor
 }
 
 MT_API int mt_peer_barrier(int* const* flags, int rank, int world, int epoch, uint64_t timeout_ns, void* stream) {
+    // Every device-side wait stays bounded: a longer limit is refused, not clamped.
+    if (timeout_ns > kMaxPeerWaitNs)
+        return fail(MT_EINVAL, "peer_barrier: timeout_ns %llu above the %llu ns maximum",
+                    (unsigned long long)timeout_ns, (unsigned long long)kMaxPeerWaitNs);
     if (world < 1 || world > mt::umma::kMaxDst || rank < 0 || rank >= world || !flags)
         return fail(MT_EINVAL, "peer_barrier: bad rank/world");
     peer::Flags fl;

@@ -169,6 +169,8 @@ class Ref:
         L.ref_conv2d_backward.argtypes = [_f, _f, _f, _f, _f, _f] + [_i64] * 9
         L.ref_matmul_rows_mt.argtypes = [_f, _f, _f, _i64, _i64, _i64, _i64, _i64, ctypes.c_int,
                                          ctypes.POINTER(ctypes.c_double)]
+        L.ref_normal.argtypes = [ctypes.c_uint32, ctypes.c_float, ctypes.c_float, _f, _i64]
+        L.ref_conv2d_first_weight.argtypes = [_i64, _i64, _i64, _f]
 
     @staticmethod
     def _ok(rc):
@@ -228,6 +230,18 @@ class Ref:
         self._ok(self.lib.ref_conv2d(_p(x), _p(w), _p(bias) if bias is not None else None, _p(y),
                                      N, C, H, W, Co, kh, kw, stride, pad))
         return y
+
+    def normal(self, n, mean, stddev, seed):
+        """The first n draws of std::normal_distribution<float>(mean, stddev) on std::mt19937(seed)."""
+        out = np.empty(n, np.float32)
+        self._ok(self.lib.ref_normal(seed, mean, stddev, _p(out), n))
+        return out
+
+    def conv2d_first_weight(self, out_ch, in_ch, k):
+        """Weights of the first Conv2D<float> constructed in this process (seed 42)."""
+        out = np.empty((out_ch, in_ch, k, k), np.float32)
+        self._ok(self.lib.ref_conv2d_first_weight(out_ch, in_ch, k, _p(out)))
+        return out
 
     def conv2d_backward(self, dy, x, w, stride, pad):
         N, C, H, W = x.shape

@@ -13,6 +13,7 @@
 #include <cstring>
 #include <exception>
 #include <memory>
+#include <random>
 #include <thread>
 #include <vector>
 
@@ -204,6 +205,34 @@ int ref_matmul_rows_mt(const float* A, const float* B, float* C,
             to_host(outs[(size_t)t], C + row * (size_t)N);
             row += outs[(size_t)t].shape()[0];
         }
+        return 0;
+    } catch (const std::exception&) { return 1; }
+}
+
+// The first n draws of std::normal_distribution<float>(mean, stddev) on std::mt19937(seed),
+// filled in order as the reference fills its weights (include/Module.hpp:99-105, :226-232).
+// Pins the synthetic-input generator to this C++ standard library.
+int ref_normal(uint32_t seed, float mean, float stddev, float* out, int64_t n) {
+    std::mt19937 gen(seed);
+    std::normal_distribution<float> dist(mean, stddev);
+    for (int64_t i = 0; i < n; ++i) out[i] = dist(gen);
+    return 0;
+}
+
+// The weights of the FIRST Conv2D<float> this process constructs (include/Module.hpp:
+// 199-233: its static init_seed starts at 42 and counts up per instance). Built once and
+// cached, so every call returns that first instance's weights, which must have the
+// requested shape.
+int ref_conv2d_first_weight(int64_t out_ch, int64_t in_ch, int64_t k, float* out) {
+    try {
+        static std::unique_ptr<Conv2D<float>> first;
+        static int64_t shape[3];
+        if (!first) {
+            first = std::make_unique<Conv2D<float>>((size_t)in_ch, (size_t)out_ch, (size_t)k, 1, 0, false);
+            shape[0] = out_ch; shape[1] = in_ch; shape[2] = k;
+        }
+        if (shape[0] != out_ch || shape[1] != in_ch || shape[2] != k) return 2;
+        to_host(first->weight_, out);
         return 0;
     } catch (const std::exception&) { return 1; }
 }

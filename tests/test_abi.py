@@ -224,3 +224,12 @@ def test_linear_bias_layout_checked_before_the_call():
     assert lib.mt_linear_fwd_gpu(ctypes.byref(X), ctypes.byref(W), ctypes.byref(short),
                                  ctypes.byref(Y), 0, None) == engine.MT_EINVAL
     assert b"out_features" in lib.mt_last_error()
+
+
+def test_peer_barrier_refuses_unbounded_timeout():
+    # Checked before any device call: a limit above 60 s is refused, so no wait is unbounded.
+    lib = engine.lib()
+    flags = (ctypes.c_void_p * 1)(None)
+    rc = lib.mt_peer_barrier(flags, 0, 1, 1, 2**64 - 1, None)
+    assert rc == engine.MT_EINVAL
+    assert b"timeout" in lib.mt_last_error()

@@ -229,3 +229,34 @@ def test_port_matches_reference_build_sweep(port, ref):
         assert np.array_equal(port.conv2d_bwd_input(dy, w, x.shape, stride, pad), dx), case
         assert np.array_equal(port.conv2d_bwd_weight(dy, x, w.shape, stride, pad), dw), case
         assert np.array_equal(port.conv2d_bwd_bias(dy), db), case
+
+
+def test_normal_inputs_match_libstdcxx(ref):
+    # The synthetic normals are libstdc++'s normal_distribution<float> on mt19937(seed), bit
+    # for bit: odd and even lengths (the polar method makes values in pairs), the stds the
+    # configurations use, and seeds 0..7 and 42.
+    for seed, std, n in [(0, 1.0, 1), (1, 1.0, 2), (2, 1.0, 7), (3, 1.0, 4097), (4, 0.125, 131072),
+                         (5, 0.125, 32768), (6, 1.0, 100001), (7, 1.0, 65536),
+                         (42, inputs.he_std_conv(576), 36864), (42, inputs.he_std_linear(1024), 50000)]:
+        got = inputs.normal((n,), std, seed)
+        want = ref.normal(n, 0.0, float(np.float32(std)), seed)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), (seed, std, n)
+
+
+def test_config4_weight_is_the_reference_first_conv2d(ref):
+    # include/Module.hpp:226-232: the first Conv2D<float> draws He-normal weights from mt19937(42).
+    W = inputs.config4()[1]
+    assert np.array_equal(W.view(np.uint32), ref.conv2d_first_weight(64, 64, 3).view(np.uint32))
+
+
+def test_uniform_inputs_match_libstdcxx_canonical(port):
+    # uniform() restates generate_canonical<float> + uniform_real_distribution<float>;
+    # the C generator (inputs_gen.c) does the same from its own MT19937, so both agree.
+    import ctypes
+    L = inputs._gen()
+    L.mtin_uniform_f32.argtypes = [ctypes.c_uint32, ctypes.c_float, ctypes.c_float,
+                                   ctypes.POINTER(ctypes.c_float), ctypes.c_size_t]
+    for seed, n in [(0, 5), (1, 100003)]:
+        out = np.empty(n, np.float32)
+        L.mtin_uniform_f32(seed, -1.0, 1.0, out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), n)
+        assert np.array_equal(out, inputs.uniform((n,), -1.0, 1.0, seed))
