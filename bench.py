@@ -262,6 +262,10 @@ class C5(Workload):
         else:
             self.plan.run(self.A, self.B, self.C, mode=mode)
 
+    def local_step(self, mode):
+        """This rank's column shard into its own C only (no peer stores, no barrier)."""
+        self.engine.gemm(self.A, self.B, self.C[:, self.plan.n0:self.plan.n1], mode=mode)
+
     def cpu_sample(self, threads):
         impl, kind = _ref()
         rows = threads
@@ -426,8 +430,9 @@ class C3(Workload):
     flops = 2.0 * 64 * 512 * 512 * 64
     bytes = 4.0 * (64 * 512 * 64 + 64 * 512 + 64 * 512 * 512)
 
-    def __init__(self, gpu=True):
+    def __init__(self, gpu=True, rank=0, world=1):
         from minitensor_b200 import inputs
+        self.rank, self.world = rank, world
         self.A_h, self.B0_h = inputs.config3()
         super().__init__(gpu)
 
@@ -435,14 +440,28 @@ class C3(Workload):
         import torch
         from minitensor_b200 import engine
         self.engine = engine
-        self.A, self.B0 = _cuda(self.A_h), _cuda(self.B0_h)
-        self.Bx = self.B0.expand(64, 64, 512)
+        b0, b1 = 0, 64
+        if self.world > 1:
+            # Batch shards: this rank's block of A, B0 broadcast, the whole C on every rank.
+            from minitensor_b200 import sharded
+            self.plan = sharded.ShardedBmm(64, 512, 512, 64, self.rank, self.world)
+            b0, b1 = self.plan.b0, self.plan.b1
+        A_src = np.ascontiguousarray(self.A_h[b0:b1])
+        self.A, self.B0 = _cuda(A_src), _cuda(self.B0_h)
+        self.Bx = self.B0.expand(b1 - b0, 64, 512)
         self.C = torch.empty(64, 512, 512, device="cuda")
-        self.h2d = [(_pin(self.A_h), self.A), (_pin(self.B0_h), self.B0)]
+        self.h2d = [(_pin(A_src), self.A), (_pin(self.B0_h), self.B0)]
         self.d2h = [(self.C, torch.empty(64, 512, 512).pin_memory())]
 
     def step(self, mode):
-        self.engine.gemm(self.A, self.Bx, self.C, mode=mode)
+        if self.world == 1:
+            self.engine.gemm(self.A, self.Bx, self.C, mode=mode)
+        else:
+            self.plan.run(self.A, self.Bx, self.C, mode=mode)
+
+    def local_step(self, mode):
+        """This rank's batch block into its own C only (no peer stores, no barrier)."""
+        self.engine.gemm(self.A, self.Bx, self.C[self.plan.b0:self.plan.b1], mode=mode)
 
     def cpu_sample(self, threads):
         impl, kind = _ref()
@@ -555,9 +574,11 @@ class C4(Workload):
 def make_workload(args, rank, world, gpu=True):
     if args.workload == "c5":
         return C5(gpu, args.size, rank, world, getattr(args, "gather", "auto"))
+    if args.workload == "c3":
+        return C3(gpu, rank, world)
     if world > 1 and gpu:
-        raise SystemExit("workloads c1-c4 are single-GPU problems (replicas only)")
-    return {"c1": C1, "c2": C2, "c3": C3, "c4": C4}[args.workload](gpu)
+        raise SystemExit("workloads c1, c2 and c4 are single-GPU problems (replicas only)")
+    return {"c1": C1, "c2": C2, "c4": C4}[args.workload](gpu)
 
 
 # ------------------------------------------------------------------ reference arm ----
@@ -700,16 +721,15 @@ def run_gpu(args, rank, world, local_rank):
         if world > 1 and hasattr(wl, "plan"):
             s, tl, err = max(3, min(args.steps, 10)), float("inf"), None
             try:
-                Cv = wl.C[:, wl.plan.n0:wl.plan.n1]
-                engine.gemm(wl.A, wl.B, Cv, mode=args.mode)
+                wl.local_step(args.mode)
                 torch.cuda.synchronize()
-                tl = time_steps(lambda: engine.gemm(wl.A, wl.B, Cv, mode=args.mode), s, stream)
+                tl = time_steps(lambda: wl.local_step(args.mode), s, stream)
             except Exception as exc:
                 err = f"{type(exc).__name__}: {exc}"[:200]
             tl = max_over_ranks(tl)
             extras["shard_gemm_only"] = (
                 {"value": wl.flops * s / tl / 1e12, "ms_per_step": tl / s * 1e3,
-                 "note": "column-shard GEMMs only, no all-gather (not the metric)"}
+                 "note": "each rank's shard product only, no all-gather (not the metric)"}
                 if err is None and tl != float("inf") else {"error": err or "failed on another rank"})
 
         # End to end through the public API from pinned host buffers: H2D of this rank's
@@ -804,9 +824,10 @@ def run_gpu(args, rank, world, local_rank):
         "config": {"workload": wl.desc, "mode": args.mode,
                    "timing": "one CUDA-graph replay of the K captured steps" if graph is not None
                              else "K eager steps",
-                   "parallelism": (f"N-column shards x{world}, all-gather by "
-                                   + ("epilogue peer stores" if wl.plan.gather == "epilogue" else "copy engines"))
-                                  if world > 1 else "single GPU",
+                   "parallelism": ("single GPU" if world == 1 else
+                                   f"batch shards x{world}, all-gather by epilogue peer stores" if wl.name == "c3" else
+                                   f"N-column shards x{world}, all-gather by "
+                                   + ("epilogue peer stores" if wl.plan.gather == "epilogue" else "copy engines")),
                    "l2": "inputs larger than the 126 MB L2, no flush" if wl.name == "c5" else
                          "steps back to back without an L2 flush (working set fits L2)"},
         "roofline": roofline, "parity": par, "cpu_baseline": cpu, "ref_gpu_baseline": ref_gpu, "e2e": e2e, "e2e_overlapped": e2e_ov, "modes": extras,

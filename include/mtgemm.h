@@ -219,7 +219,10 @@ MT_API int mt_ipc_open(const void* handle, uint64_t offset, void** dptr_out);
 MT_API int mt_ipc_close(void* dptr, uint64_t offset);
 
 /* C = epi(A * B) written to C and to extra_dst[0..nextra) (nextra < 8), each a device
- * pointer (peer-mapped allowed) laid out with C's row stride. */
+ * pointer (peer-mapped allowed) laid out with C's row (and batch) strides. A, B and C are
+ * 2-D, or 3-D with a common batch (batch stride 0 = an operand broadcast over the batch):
+ * a batch-sharded bmm passes its block of batches, and the epilogue writes every finished
+ * tile to every rank's C. */
 MT_API int mt_gemm_multi(const mt_tensor* A, const mt_tensor* B, const mt_tensor* C, float* const* extra_dst,
                          int nextra, const float* bias, int epi, int mode, void* stream);
 

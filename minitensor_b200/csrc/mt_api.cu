@@ -222,10 +222,57 @@ int launch_umma_inst(const CUtensorMap& ta, const CUtensorMap& tb, const mt::umm
     return MT_OK;
 }
 
-// CTA-pair kernel: grid = 2 x (clusters that fit at once, capped by the tile count).
+// Stream-K remainder of a pair launch with `clusters` clusters (see umma::Params). When
+// the tiles do not divide into whole rounds over the clusters, the last num_tiles %
+// clusters tiles are cut into equal k-block ranges, one per cluster, as long as every range
+// gets at least 8 k-blocks. *ws_out receives the stream-ordered workspace (partial slots and
+// arrival counters, the counters zeroed on the stream) that the caller frees after the launch.
+bool streamk_enabled() {
+    static int v = [] {
+        const char* e = std::getenv("MT_GEMM_STREAMK");
+        return (e && e[0] == '0') ? 0 : 1;
+    }();
+    return v != 0;
+}
+
+int pair_streamk_plan(mt::umma::Params& up, int clusters, int kblocks, int bn, cudaStream_t st, void** ws_out) {
+    *ws_out = nullptr;
+    up.sk_dp = up.num_tiles;
+    up.sk_clusters = clusters;
+    up.sk_maxseg = 0;
+    up.sk_ws = nullptr;
+    up.sk_cnt = nullptr;
+    if (!streamk_enabled() || clusters <= 0 || up.num_tiles <= clusters) return MT_OK;
+    const long long rem = up.num_tiles % clusters;
+    const long long W = rem * (long long)kblocks;
+    if (rem == 0 || W < 8LL * clusters) return MT_OK;
+    // A range holds at least floor(W / C) k-blocks, so a tile meets at most this many.
+    const long long minr = W / clusters;
+    const int maxseg = (int)((kblocks + minr - 1) / minr + 1);
+    const size_t ws_bytes = (size_t)rem * maxseg * mt::umma2::BM * bn * sizeof(float);
+    const size_t cnt_bytes = (size_t)rem * 8 * sizeof(int);
+    void* ws = nullptr;
+    cudaError_t e = cudaMallocAsync(&ws, ws_bytes + cnt_bytes, st);
+    if (e != cudaSuccess) return cuda_fail(e, "stream-K workspace");
+    int* cnt = reinterpret_cast<int*>(static_cast<char*>(ws) + ws_bytes);
+    e = cudaMemsetAsync(cnt, 0, cnt_bytes, st);
+    if (e != cudaSuccess) {
+        cudaFreeAsync(ws, st);
+        return cuda_fail(e, "stream-K counters");
+    }
+    up.sk_dp = up.num_tiles - rem;
+    up.sk_maxseg = maxseg;
+    up.sk_ws = static_cast<float*>(ws);
+    up.sk_cnt = cnt;
+    *ws_out = ws;
+    return MT_OK;
+}
+
+// CTA-pair kernel: grid = 2 x (clusters that fit at once, capped by the tile count), with
+// the stream-K remainder planned for exactly that many clusters.
 template <int BN, int BKE, bool AMN, bool BMN, bool X3, int STAGES>
 int launch_pair_inst(const CUtensorMap& ta, const CUtensorMap& tb, const mt::umma::DstMaps& dm,
-                     const mt::umma::Params& up, int sms, cudaStream_t st) {
+                     mt::umma::Params up, int sms, cudaStream_t st) {
     using G = mt::umma2::Cfg<BN, BKE, X3, STAGES>;
     auto kern = mt::umma2::gemm_pair_kernel<BN, BKE, AMN, BMN, X3, STAGES>;
     static std::atomic<uint64_t> attr_set_mask{0};
@@ -253,9 +300,13 @@ int launch_pair_inst(const CUtensorMap& ta, const CUtensorMap& tb, const mt::umm
         max_clusters[dev & 63].store(std::min(n, sms / 2));
         attr_set_mask.fetch_or(bit);
     }
-    const int clusters = (int)std::min<long long>(up.num_units, (long long)max_clusters[dev & 63].load());
+    const int clusters = (int)std::min<long long>(up.num_tiles, (long long)max_clusters[dev & 63].load());
+    void* ws = nullptr;
+    int rc = pair_streamk_plan(up, clusters, (up.K + BKE - 1) / BKE, BN, st, &ws);
+    if (rc) return rc;
     kern<<<2 * clusters, G::THREADS, G::SMEM_BYTES, st>>>(ta, tb, dm, up);
     cudaError_t e = cudaGetLastError();
+    if (ws) cudaFreeAsync(ws, st);
     if (e != cudaSuccess && e != cudaErrorStreamCaptureUnsupported) return cuda_fail(e, "umma pair gemm launch");
     g_launches.fetch_add(1);
     return MT_OK;
@@ -266,6 +317,16 @@ int launch_pair_inst(const CUtensorMap& ta, const CUtensorMap& tb, const mt::umm
 bool pair_enabled() {
     static int v = [] {
         const char* e = std::getenv("MT_GEMM_PAIR");
+        return (e && e[0] == '0') ? 0 : 1;
+    }();
+    return v != 0;
+}
+
+// 256 x 128 pair tiles for outputs with fewer than two rounds of 256 x 256 tiles;
+// MT_GEMM_PAIR_BN128=0 keeps 256 x 256.
+bool pair_bn128_enabled() {
+    static int v = [] {
+        const char* e = std::getenv("MT_GEMM_PAIR_BN128");
         return (e && e[0] == '0') ? 0 : 1;
     }();
     return v != 0;
@@ -305,10 +366,15 @@ int launch_umma(const GemmProblem& p, bool x3, cudaStream_t st, float* const* ex
 
     const int64_t tiles_m1 = (p.M + 127) / 128;
     const bool small = tiles_m1 * ((p.N + 255) / 256) * p.batch < (int64_t)di.sms || p.N <= 128;
-    const int bn = small ? 128 : 256;
+    int bn = small ? 128 : 256;
     // CTA pairs: 256 x 256 tiles, at least one per pair of SMs.
-    const bool pair = pair_enabled() && !small && p.M > 128 &&
-                      ((p.M + 255) / 256) * ((p.N + 255) / 256) * p.batch >= (int64_t)(di.sms / 2);
+    const int64_t tiles256 = ((p.M + 255) / 256) * ((p.N + 255) / 256) * p.batch;
+    const bool pair = pair_enabled() && !small && p.M > 128 && tiles256 >= (int64_t)(di.sms / 2);
+    // Fewer than two rounds of 256 x 256 pair tiles (e.g. one rank's 1024-column shard of
+    // an 8192^3 GEMM over 8 GPUs): 256 x 128 tiles. Each tile then takes half as long, so the
+    // first finished tiles (and, in a sharded GEMM, their stores to the peers) come twice
+    // as early and the last round's stores are half as large.
+    if (pair && tiles256 < (int64_t)di.sms && pair_bn128_enabled()) bn = 128;
     // k elements per stage: 32 (a 128-byte swizzled row); the one-CTA TF32X3 kernel takes
     // 16 to keep 4-6 stages of hi + lo in shared memory, the pair kernel 32 with 3 stages
     // (half the stage hand-offs per MMA; measured +5% on 8192^3 and a higher clock under
@@ -410,15 +476,20 @@ int launch_umma(const GemmProblem& p, bool x3, cudaStream_t st, float* const* ex
     else if (a_mn == 0 && b_mn == 1) rc = launch_umma_inst<BN_, BKE_, false, true, X3_, ST_>(ta, tb, dm, up, grid, st); \
     else if (a_mn == 1 && b_mn == 0) rc = launch_umma_inst<BN_, BKE_, true, false, X3_, ST_>(ta, tb, dm, up, grid, st); \
     else rc = launch_umma_inst<BN_, BKE_, true, true, X3_, ST_>(ta, tb, dm, up, grid, st);
-#define MT_PAIR_DISPATCH(BKE_, X3_, ST_)                                                                   \
-    if (a_mn == 0 && b_mn == 0) rc = launch_pair_inst<256, BKE_, false, false, X3_, ST_>(ta, tb, dm, up, di.sms, st); \
-    else if (a_mn == 0 && b_mn == 1) rc = launch_pair_inst<256, BKE_, false, true, X3_, ST_>(ta, tb, dm, up, di.sms, st); \
-    else if (a_mn == 1 && b_mn == 0) rc = launch_pair_inst<256, BKE_, true, false, X3_, ST_>(ta, tb, dm, up, di.sms, st); \
-    else rc = launch_pair_inst<256, BKE_, true, true, X3_, ST_>(ta, tb, dm, up, di.sms, st);
+#define MT_PAIR_DISPATCH(BN_, BKE_, X3_, ST_)                                                               \
+    if (a_mn == 0 && b_mn == 0) rc = launch_pair_inst<BN_, BKE_, false, false, X3_, ST_>(ta, tb, dm, up, di.sms, st); \
+    else if (a_mn == 0 && b_mn == 1) rc = launch_pair_inst<BN_, BKE_, false, true, X3_, ST_>(ta, tb, dm, up, di.sms, st); \
+    else if (a_mn == 1 && b_mn == 0) rc = launch_pair_inst<BN_, BKE_, true, false, X3_, ST_>(ta, tb, dm, up, di.sms, st); \
+    else rc = launch_pair_inst<BN_, BKE_, true, true, X3_, ST_>(ta, tb, dm, up, di.sms, st);
     if (pair) {
-        if (!x3) { MT_PAIR_DISPATCH(32, false, 6) }
-        else if (x3_wide) { MT_PAIR_DISPATCH(32, true, 3) }
-        else { MT_PAIR_DISPATCH(16, true, 6) }
+        // Stages: as many as fit in 227 KB with the 32 KB epilogue staging.
+        if (bn == 256) {
+            if (!x3) { MT_PAIR_DISPATCH(256, 32, false, 6) }
+            else { MT_PAIR_DISPATCH(256, 32, true, 3) }
+        } else {
+            if (!x3) { MT_PAIR_DISPATCH(128, 32, false, 8) }
+            else { MT_PAIR_DISPATCH(128, 32, true, 4) }
+        }
     } else if (!x3) {
         if (bn == 256) { MT_UMMA_DISPATCH(256, 32, false, 4) }
         else { MT_UMMA_DISPATCH(128, 32, false, 6) }
@@ -1705,21 +1776,26 @@ MT_API int mt_gemm_multi(const mt_tensor* A, const mt_tensor* B, const mt_tensor
         if (!extra_dst[i]) return fail(MT_EINVAL, "gemm_multi: extra_dst[%d] is null", i);
     if (mode < MT_MODE_DEFAULT || mode > MT_TF32X3) return fail(MT_EINVAL, "gemm_multi: bad mode %d", mode);
     if (epi & ~7) return fail(MT_EINVAL, "gemm_multi: bad epilogue flags %d", epi);
+    if (!A || !B || !C) return fail(MT_EINVAL, "gemm_multi: null tensor");
+    const int nd = (int)C->ndim;
+    if (nd != 2 && nd != 3) return fail(MT_EINVAL, "gemm_multi: 2-D or 3-D views only");
     View a, b, c;
     int rc;
-    if ((rc = to_view(A, 2, "gemm_multi A", a)) || (rc = to_view(B, 2, "gemm_multi B", b)) ||
-        (rc = to_view(C, 2, "gemm_multi C", c)))
+    if ((rc = to_view(A, nd, "gemm_multi A", a)) || (rc = to_view(B, nd, "gemm_multi B", b)) ||
+        (rc = to_view(C, nd, "gemm_multi C", c)))
         return rc;
+    if (a.d[0] != c.d[0] || b.d[0] != c.d[0]) return fail(MT_EINVAL, "gemm_multi: batch mismatch");
     if (a.d[2] != b.d[1]) return fail(MT_EINVAL, "gemm_multi: inner dimension mismatch (A.K != B.K)");
     if (c.d[1] != a.d[1] || c.d[2] != b.d[2]) return fail(MT_EINVAL, "gemm_multi: C shape mismatch");
     if (c.s[2] != 1 && c.d[2] > 1) return fail(MT_EINVAL, "gemm_multi: C rows must be contiguous");
+    if (c.d[0] == 1) { a.s[0] = 0; b.s[0] = 0; c.s[0] = 0; }
     GemmProblem p;
-    p.A = a.ptr; p.sa_b = 0; p.sa_m = a.s[1]; p.sa_k = a.s[2];
-    p.B = b.ptr; p.sb_b = 0; p.sb_k = b.s[1]; p.sb_n = b.s[2];
-    p.C = const_cast<float*>(c.ptr); p.sc_b = 0; p.sc_m = c.s[1]; p.sc_n = 1;
-    p.M = a.d[1]; p.K = a.d[2]; p.N = b.d[2]; p.batch = 1;
+    p.A = a.ptr; p.sa_b = a.s[0]; p.sa_m = a.s[1]; p.sa_k = a.s[2];
+    p.B = b.ptr; p.sb_b = b.s[0]; p.sb_k = b.s[1]; p.sb_n = b.s[2];
+    p.C = const_cast<float*>(c.ptr); p.sc_b = c.s[0]; p.sc_m = c.s[1]; p.sc_n = 1;
+    p.M = a.d[1]; p.K = a.d[2]; p.N = b.d[2]; p.batch = c.d[0];
     p.bias = bias; p.epi = epi;
-    if (p.M == 0 || p.N == 0) return MT_OK;
+    if (p.M == 0 || p.N == 0 || p.batch == 0) return MT_OK;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const int m = resolve_mode(mode);
     if (m != MT_STRICT_FP32 && p.K > 0) {
@@ -1729,12 +1805,14 @@ MT_API int mt_gemm_multi(const mt_tensor* A, const mt_tensor* B, const mt_tensor
         if (rc != MT_EUNSUPPORTED) return rc;
         t_err = saved;
     }
-    // Local product, then one 2-D copy per peer (stream-ordered, over NVLink).
+    // Local product, then one 2-D copy per peer and batch (stream-ordered, over NVLink).
     if ((rc = run_gemm(p, m, st))) return rc;
     for (int i = 0; i < nextra; ++i) {
-        cudaError_t e = cudaMemcpy2DAsync(extra_dst[i], p.sc_m * 4, p.C, p.sc_m * 4, p.N * 4, p.M,
-                                          cudaMemcpyDeviceToDevice, st);
-        if (e != cudaSuccess) return cuda_fail(e, "gemm_multi peer copy");
+        for (int64_t bi = 0; bi < p.batch; ++bi) {
+            cudaError_t e = cudaMemcpy2DAsync(extra_dst[i] + bi * p.sc_b, p.sc_m * 4, p.C + bi * p.sc_b, p.sc_m * 4,
+                                              p.N * 4, p.M, cudaMemcpyDeviceToDevice, st);
+            if (e != cudaSuccess) return cuda_fail(e, "gemm_multi peer copy");
+        }
     }
     t_path += " +" + std::to_string(nextra) + " peer copies";
     return MT_OK;

@@ -22,6 +22,7 @@ enum DevStatus : int {
     kDevTimeoutAccEmpty = 4,  // MMA issuer waited too long for a drained accumulator
     kDevTimeoutMisc = 5,
     kDevTimeoutPeer = 6,      // a peer GPU never raised its flag in mt_peer_barrier
+    kDevBadLaunch = 7,        // launch shape disagrees with the kernel's parameters (no work done)
 };
 
 // Defined here: every kernel of the library is compiled in the single translation unit

@@ -55,6 +55,19 @@ struct Params {
     // one tensor store per destination (maps in DstMaps, C as {N, M, batch}, box {32, 32, 1},
     // 128-byte swizzle). SM stores to peer memory top out far below the link rate.
     int tma_multi;
+    // Stream-K remainder (CTA-pair kernel only; splits == 1 there). Tiles [0, sk_dp) run
+    // whole, round-robin over the clusters. The k-blocks of tiles [sk_dp, num_tiles),
+    // taken tile after tile, are cut into one contiguous range per cluster, so that every
+    // cluster ends at the same time instead of some running one tile more than others.
+    // A tile cut between clusters: every contributing warp writes its raw partial to
+    // sk_ws and counts itself in sk_cnt; the last to arrive sums the partials in k order
+    // (a fixed order, so the result does not depend on timing) and runs the epilogue.
+    // sk_dp == num_tiles turns it off.
+    long long sk_dp;
+    int sk_clusters;            // clusters in the launch
+    int sk_maxseg;              // partial slots per stream-K tile
+    float* sk_ws;               // [tile - sk_dp][sk_maxseg][256 rows][BN] partial sums
+    int* sk_cnt;                // [tile - sk_dp][2 CTAs][4 warps] arrivals, zero at launch
 };
 
 // Tensor maps of the ndst destinations (same view, different base pointers).

@@ -64,6 +64,51 @@ __device__ __forceinline__ void drain_pause() {
     while (globaltimer_ns() - t0 < 2000000ull) __nanosleep(1000);
 }
 
+// One piece of a cluster's work: k-blocks [kb0, kb1) of output tile `tile`. nseg > 1: the
+// tile is cut between nseg clusters and this piece is the seg-th in k order.
+struct Item {
+    long long tile;
+    int kb0, kb1, seg, nseg;
+};
+
+// The work of cluster c of C, in order: whole tiles c, c + C, ... below p.sk_dp, then the
+// cluster's contiguous range [W c / C, W (c+1) / C) of the W = (num_tiles - sk_dp) * kblocks
+// k-blocks of the stream-K tiles, cut at tile boundaries. Every role of the kernel walks
+// the same sequence.
+struct Sched {
+    long long u, x, hi, c, C, W;
+    int kblocks;
+    __device__ Sched(const Params& p, int kblocks_, long long cluster, long long clusters)
+        : u(cluster), c(cluster), C(clusters), kblocks(kblocks_) {
+        W = (p.num_tiles - p.sk_dp) * (long long)kblocks;
+        x = W * c / C;
+        hi = W * (c + 1) / C;
+    }
+    // The cluster whose range holds stream-K k-block y: the largest c with W c / C <= y.
+    __device__ long long owner(long long y) const { return ((y + 1) * C + W - 1) / W - 1; }
+    __device__ bool next(const Params& p, Item& it) {
+        if (u < p.sk_dp) {
+            it.tile = u;
+            it.kb0 = 0;
+            it.kb1 = kblocks;
+            it.seg = 0;
+            it.nseg = 1;
+            u += C;
+            return true;
+        }
+        if (x >= hi) return false;
+        const long long t = x / kblocks;
+        it.tile = p.sk_dp + t;
+        it.kb0 = (int)(x - t * kblocks);
+        it.kb1 = (int)min((long long)kblocks, (long long)it.kb0 + (hi - x));
+        const long long cf = owner(t * kblocks);
+        it.nseg = (int)(owner(t * kblocks + kblocks - 1) - cf + 1);
+        it.seg = (int)(c - cf);
+        x += it.kb1 - it.kb0;
+        return true;
+    }
+};
+
 template <int BN, int BKE, bool A_MN, bool B_MN, bool X3, int STAGES>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg<BN, BKE, X3, STAGES>::THREADS, 1)
 gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -91,6 +136,15 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     const long long first = blockIdx.x >> 1, step = gridDim.x >> 1;
     const int kblocks = (p.K + G::BKE - 1) / G::BKE;
 
+    // The stream-K split is planned on the host for this many clusters and at least one
+    // k-block per cluster; any other launch does no work and says so (both CTAs return
+    // before touching a barrier, so neither waits for the other).
+    if (p.sk_dp < p.num_tiles &&
+        (p.sk_clusters != (int)step || (p.num_tiles - p.sk_dp) * (long long)kblocks < step)) {
+        if (threadIdx.x == 0) atomicCAS(&g_dev_status, 0, (int)kDevBadLaunch);
+        return;
+    }
+
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(smem_u32(&full[s]), 1);
@@ -117,19 +171,19 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
+    Item item;
     if (warp == 0) {
         // ------------------------------ TMA producer ------------------------------
         if (lane == 0) {
             int s = 0;
             uint32_t ph = 0;
-            for (long long u = first; u < p.num_units; u += step) {
-                int b, mb, nb, kb0, kb1;
-                umma::tile_coords(p, u / p.splits, b, mb, nb);
-                umma::split_range(p, kblocks, (int)(u % p.splits), kb0, kb1);
+            for (Sched sc(p, kblocks, first, step); sc.next(p, item);) {
+                int b, mb, nb;
+                umma::tile_coords(p, item.tile, b, mb, nb);
                 const int m0 = mb * BM + (int)rank * BMC;
                 const int n0 = nb * BN + (int)rank * G::BH;
                 const int ab = p.a_batched ? b : 0, bb = p.b_batched ? b : 0;
-                for (int kb = kb0; kb < kb1; ++kb) {
+                for (int kb = item.kb0; kb < item.kb1; ++kb) {
                     if (!mbar_wait_cl(smem_u32(&empty[s]), ph ^ 1, abort_flag, kDevTimeoutEmpty)) goto done;
                     const uint32_t sa = smem_u32(ring + s * G::STAGE_BYTES);
                     const uint32_t sb = sa + G::A_BYTES;
@@ -171,15 +225,13 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             int s = 0;
             uint32_t ph = 0;
             int it = 0;
-            for (long long u = first; u < p.num_units; u += step, ++it) {
-                int kb0, kb1;
-                umma::split_range(p, kblocks, (int)(u % p.splits), kb0, kb1);
+            for (Sched sc(p, kblocks, first, step); sc.next(p, item); ++it) {
                 const int a = it & 1;
                 const uint32_t aph = (it >> 1) & 1;
                 if (!mbar_wait_cl(smem_u32(&acc_empty[a]), aph ^ 1, abort_flag, kDevTimeoutAccEmpty)) goto done;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + a * BN;
-                for (int kb = kb0; kb < kb1; ++kb) {
+                for (int kb = item.kb0; kb < item.kb1; ++kb) {
                     const uint32_t wbar = X3 ? smem_u32(&conv[s]) : smem_u32(&full[s]);
                     if (!mbar_wait_cl(wbar, ph, abort_flag, kDevTimeoutFull)) goto done;
                     tc_fence_after();
@@ -189,7 +241,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                     for (int k = 0; k < G::KSTEPS; ++k) {
                         const uint64_t ad = umma::operand_desc<A_MN, BKE>(sa, k);
                         const uint64_t bd = umma::operand_desc<B_MN, BKE>(sb, k);
-                        const uint32_t acc = (kb > kb0 || k > 0) ? 1u : 0u;
+                        const uint32_t acc = (kb > item.kb0 || k > 0) ? 1u : 0u;
                         if (X3) {
                             const uint32_t la = smem_u32(ring_lo + s * G::STAGE_BYTES);
                             const uint32_t lb = la + G::A_BYTES;
@@ -212,47 +264,33 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         // ------------------------------ epilogue ----------------------------------
         const int q = warp & 3;
         int it = 0, seq = 0;
-        for (long long u = first; u < p.num_units; u += step, ++it) {
-            int b, mb, nb, kb0, kb1;
-            umma::tile_coords(p, u / p.splits, b, mb, nb);
-            const int sp = (int)(u % p.splits);
-            umma::split_range(p, kblocks, sp, kb0, kb1);
-            const bool no_k = kb1 <= kb0;
+        for (Sched sc(p, kblocks, first, step); sc.next(p, item); ++it) {
+            int b, mb, nb;
+            umma::tile_coords(p, item.tile, b, mb, nb);
             const int a = it & 1;
             const uint32_t aph = (it >> 1) & 1;
             if (!mbar_wait_cl(smem_u32(&acc_full[a]), aph, abort_flag, kDevTimeoutAccFull)) goto done;
             __syncwarp();
             tc_fence_after();
-            const int m = mb * BM + (int)rank * BMC + q * 32 + lane;
-            const int64_t row_off = (int64_t)b * p.sc_b + (int64_t)m * p.sc_m + (int64_t)sp * p.split_stride;
+            const int m0w = mb * BM + (int)rank * BMC + q * 32;   // this warp's first row
+            const int m = m0w + lane;
+            const int64_t row_off = (int64_t)b * p.sc_b + (int64_t)m * p.sc_m;
             const float bias_row = (p.epi & 1) && m < p.M ? __ldg(p.bias + m) : 0.f;
-#pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + a * BN + c * 32, r);
-                tmem_ld_wait();
-                if (c == BN / 32 - 1) {
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[a]), 0));
-                }
+            // Epilogue of one finished 32-column chunk c: bias / ReLU, then the stores.
+            auto finish = [&](float (&v)[32], int c) {
                 const int n0 = nb * BN + c * 32;
-                float v[32];
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
-                    float x = (no_k ? 0.f : __uint_as_float(r[j])) + bias_row;
+                    float x = v[j] + bias_row;
                     if (p.epi & 2) x = x + ((n0 + j < p.N) ? __ldg(p.bias + n0 + j) : 0.f);
                     if (p.epi & 4) x = x > 0.f ? x : 0.f;
                     v[j] = x;
                 }
                 if (p.tma_multi) {
-                    umma::store_block_tma(dm, p.ndst, epi_stage + q * 512, seq, v, lane, n0,
-                                          mb * BM + (int)rank * BMC + q * 32, b, p.M, p.N);
+                    umma::store_block_tma(dm, p.ndst, epi_stage + q * 512, seq, v, lane, n0, m0w, b, p.M, p.N);
                 } else if (p.vec_store && n0 + 32 <= p.N && p.ndst > 1) {
                     // several destinations (peers over NVLink): whole-row stores
-                    umma::store_block_lines(epi_stage + q * 512, v, lane, p,
-                                            (int64_t)b * p.sc_b + (int64_t)sp * p.split_stride,
-                                            mb * BM + (int)rank * BMC + q * 32, n0);
+                    umma::store_block_lines(epi_stage + q * 512, v, lane, p, (int64_t)b * p.sc_b, m0w, n0);
                 } else if (p.vec_store && n0 + 32 <= p.N) {
                     // one local destination: straight from registers (the shared-memory
                     // round trip costs more than it saves when the epilogue is the bound)
@@ -272,6 +310,66 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                             if (n0 + j < p.N) crow[n0 + j] = v[j];
                     }
                 }
+            };
+            const bool part = item.nseg > 1;
+            const long long skt = item.tile - p.sk_dp;
+            // This warp's row of the partial slots of a cut tile (slot stride 256 x BN).
+            const long long slot_row = ((skt * p.sk_maxseg) * BM + (int)rank * BMC + q * 32 + lane) * (long long)BN;
+            const long long slot_stride = (long long)BM * BN;
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + a * BN + c * 32, r);
+                tmem_ld_wait();
+                if (c == BN / 32 - 1) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[a]), 0));
+                }
+                if (part) {
+                    // Raw partial sum to this piece's slot (L2; other SMs read it).
+                    float4* w = reinterpret_cast<float4*>(p.sk_ws + slot_row + item.seg * slot_stride + c * 32);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        __stcg(w + j, make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                                  __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])));
+                    continue;
+                }
+                float v[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+                finish(v, c);
+            }
+            if (part) {
+                // Count this piece; the last of the tile's pieces to arrive sums all of
+                // them in k order (slot 0 first) and writes the tile. No one waits.
+                __threadfence();
+                __syncwarp();
+                int old = 0;
+                if (lane == 0) old = atomicAdd(p.sk_cnt + (skt * 2 + (long long)rank) * 4 + q, 1);
+                old = __shfl_sync(0xffffffffu, old, 0);
+                if (old == item.nseg - 1) {
+                    __threadfence();
+#pragma unroll 1
+                    for (int c = 0; c < BN / 32; ++c) {
+                        float v[32];
+                        const float4* r0 = reinterpret_cast<const float4*>(p.sk_ws + slot_row + c * 32);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            const float4 x = __ldcg(r0 + j);
+                            v[4 * j] = x.x; v[4 * j + 1] = x.y; v[4 * j + 2] = x.z; v[4 * j + 3] = x.w;
+                        }
+                        for (int sg = 1; sg < item.nseg; ++sg) {
+                            const float4* rs = reinterpret_cast<const float4*>(p.sk_ws + slot_row + sg * slot_stride + c * 32);
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) {
+                                const float4 x = __ldcg(rs + j);
+                                v[4 * j] += x.x; v[4 * j + 1] += x.y; v[4 * j + 2] += x.z; v[4 * j + 3] += x.w;
+                            }
+                        }
+                        finish(v, c);
+                    }
+                }
             }
         }
     } else if (X3) {
@@ -279,10 +377,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         const int ct = threadIdx.x - 6 * 32;
         int s = 0;
         uint32_t ph = 0;
-        for (long long u = first; u < p.num_units; u += step) {
-            int kb0, kb1;
-            umma::split_range(p, kblocks, (int)(u % p.splits), kb0, kb1);
-            for (int kb = kb0; kb < kb1; ++kb) {
+        for (Sched sc(p, kblocks, first, step); sc.next(p, item);) {
+            for (int kb = item.kb0; kb < item.kb1; ++kb) {
                 if (!mbar_wait(smem_u32(&full[s]), ph, abort_flag, kDevTimeoutMisc)) goto done;
                 float4* hi = reinterpret_cast<float4*>(ring + s * G::STAGE_BYTES);
                 float4* lo = reinterpret_cast<float4*>(ring_lo + s * G::STAGE_BYTES);

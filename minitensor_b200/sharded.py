@@ -24,6 +24,10 @@ that left, died or fell behind before the next step is launched.
 Baseline (``allgather_shards``): local GEMM into a shard buffer, then an NCCL (or gloo on
 CPU) all-gather and a relayout into row-major C.
 
+Batched matmuls (``ShardedBmm``) split the batch instead: rank r computes C[b0:b1] from
+A[b0:b1] and its B batches (or the one broadcast B), and the same multi-destination
+epilogue stores that contiguous block of batches into every rank's C.
+
 torch.distributed is only the plumbing: it exchanges IPC handles and runs the baseline.
 """
 from __future__ import annotations
@@ -41,6 +45,11 @@ from . import engine
 def shard_columns(N: int, world: int, rank: int) -> tuple[int, int]:
     """Columns [n0, n1) of rank `rank`: near-equal contiguous blocks covering [0, N)."""
     return N * rank // world, N * (rank + 1) // world
+
+
+def shard_batches(batch: int, world: int, rank: int) -> tuple[int, int]:
+    """Batches [b0, b1) of rank `rank`: near-equal contiguous blocks covering [0, batch)."""
+    return batch * rank // world, batch * (rank + 1) // world
 
 
 def row_chunks(M: int, chunks: int) -> list[tuple[int, int]]:
@@ -83,38 +92,24 @@ class PeerTensor:
         self._opened = []
 
 
-class ShardedGemm:
-    """C[M,N] = A[M,K] . B[K,N] with B's columns sharded over `world` ranks; every rank
-    ends with the full C. Call collectively (same order on every rank)."""
+class _PeerOutput:
+    """What every sharded product shares: the ranks' output buffers mapped into each other
+    (CUDA IPC, made once per distinct output tensor) and the bounded cross-GPU flag
+    barrier that orders every rank's writes before the output is read."""
 
-    def __init__(self, M: int, N: int, K: int, rank: int | None = None, world: int | None = None, group=None,
-                 timeout_s: float = 10.0, gather: str | None = None, chunks: int | None = None,
-                 liveness: "PeerLiveness | None" = None):
-        self.M, self.N, self.K = M, N, K
+    def __init__(self, rank, world, group, timeout_s, liveness):
         self.liveness = liveness
         self.rank = dist.get_rank(group) if rank is None else rank
         self.world = dist.get_world_size(group) if world is None else world
         if self.world > 8:
-            raise ValueError("at most 8 GPUs per sharded GEMM")
+            raise ValueError("at most 8 GPUs per sharded product")
         self.group = group
-        self.n0, self.n1 = shard_columns(N, self.world, self.rank)
         self.timeout_ns = int(timeout_s * 1e9)
         self.epoch = 0
         self.flags = torch.zeros(self.world, dtype=torch.int32, device="cuda")
         self._flag_peers = PeerTensor(self.flags, self.rank, self.world, group)
         self._flag_arr = (ctypes.c_void_p * self.world)(*self._flag_peers.ptrs)
         self._bound = {}
-        if gather is None:
-            gather = "epilogue"
-        if gather not in ("epilogue", "copy"):
-            raise ValueError("gather must be 'epilogue' or 'copy'")
-        self.gather = gather
-        # Row chunks for the copy pipeline: boundaries on 256-row tiles; fewer chunks when
-        # the shard is narrow so that each chunk still has work for most SM pairs.
-        if chunks is None:
-            chunks = 4 if self.world <= 4 else 2
-        self.row_chunks = row_chunks(M, chunks)
-        self._copy_streams = [torch.cuda.Stream() for _ in range(self.world - 1)] if gather == "copy" else []
 
     # Distinct C tensors kept mapped before the caller is warned (see _peers).
     MAX_BOUND_QUIET = 16
@@ -128,9 +123,43 @@ class ShardedGemm:
             pt = PeerTensor(C, self.rank, self.world, self.group)
             self._bound[key] = pt
             if len(self._bound) == self.MAX_BOUND_QUIET + 1:
-                warnings.warn("ShardedGemm keeps every distinct C tensor mapped on all ranks until close(); "
-                              "pass the same C each step", RuntimeWarning, stacklevel=3)
+                warnings.warn(f"{type(self).__name__} keeps every distinct C tensor mapped on all ranks until "
+                              "close(); pass the same C each step", RuntimeWarning, stacklevel=3)
         return pt
+
+    def _barrier(self, s):
+        self.epoch += 1
+        engine._check(engine.lib().mt_peer_barrier(self._flag_arr, self.rank, self.world, self.epoch,
+                                                   self.timeout_ns, s))
+
+    def close(self):
+        for pt in self._bound.values():
+            pt.close()
+        self._bound = {}
+        self._flag_peers.close()
+
+
+class ShardedGemm(_PeerOutput):
+    """C[M,N] = A[M,K] . B[K,N] with B's columns sharded over `world` ranks; every rank
+    ends with the full C. Call collectively (same order on every rank)."""
+
+    def __init__(self, M: int, N: int, K: int, rank: int | None = None, world: int | None = None, group=None,
+                 timeout_s: float = 10.0, gather: str | None = None, chunks: int | None = None,
+                 liveness: "PeerLiveness | None" = None):
+        super().__init__(rank, world, group, timeout_s, liveness)
+        self.M, self.N, self.K = M, N, K
+        self.n0, self.n1 = shard_columns(N, self.world, self.rank)
+        if gather is None:
+            gather = "epilogue"
+        if gather not in ("epilogue", "copy"):
+            raise ValueError("gather must be 'epilogue' or 'copy'")
+        self.gather = gather
+        # Row chunks for the copy pipeline: boundaries on 256-row tiles; fewer chunks when
+        # the shard is narrow so that each chunk still has work for most SM pairs.
+        if chunks is None:
+            chunks = 4 if self.world <= 4 else 2
+        self.row_chunks = row_chunks(M, chunks)
+        self._copy_streams = [torch.cuda.Stream() for _ in range(self.world - 1)] if gather == "copy" else []
 
     def run(self, A: torch.Tensor, B_shard: torch.Tensor, C: torch.Tensor, mode="tf32x3", stream=None):
         """A [M,K] and B_shard [K, n1-n0] on this GPU; C [M,N] row-major on every rank.
@@ -172,14 +201,44 @@ class ShardedGemm:
                 ev = torch.cuda.Event()
                 ev.record(cs)
                 main.wait_event(ev)
-        self.epoch += 1
-        engine._check(L.mt_peer_barrier(self._flag_arr, self.rank, self.world, self.epoch, self.timeout_ns, s))
+        self._barrier(s)
 
-    def close(self):
-        for pt in self._bound.values():
-            pt.close()
-        self._bound = {}
-        self._flag_peers.close()
+
+class ShardedBmm(_PeerOutput):
+    """C[b] = A[b] . B[b] for b in [0, batch) with the batch split over `world` ranks
+    (include/TensorOps.hpp:933-991 is the single-GPU bmm this shards); every rank ends with
+    the full C [batch, M, N]. Rank r computes batches [b0, b1) = shard_batches(batch, world,
+    r) and its multi-destination epilogue stores them into every rank's C, whose block of
+    those batches is contiguous, so nothing is relaid out. Call collectively."""
+
+    def __init__(self, batch: int, M: int, N: int, K: int, rank: int | None = None, world: int | None = None,
+                 group=None, timeout_s: float = 10.0, liveness: "PeerLiveness | None" = None):
+        super().__init__(rank, world, group, timeout_s, liveness)
+        self.batch, self.M, self.N, self.K = batch, M, N, K
+        self.b0, self.b1 = shard_batches(batch, self.world, self.rank)
+
+    def run(self, A_shard: torch.Tensor, B_shard: torch.Tensor, C: torch.Tensor, mode="tf32x3", stream=None):
+        """A_shard [b1-b0, M, K] and B_shard [b1-b0, K, N] (any views: B may be a broadcast
+        operand expanded with batch stride 0) on this GPU; C [batch, M, N] contiguous on
+        every rank. Pass the same C each step (its IPC mappings are made once)."""
+        nb = self.b1 - self.b0
+        if C.shape != (self.batch, self.M, self.N) or not C.is_contiguous():
+            raise ValueError("C must be a contiguous [batch, M, N] tensor")
+        if A_shard.shape != (nb, self.M, self.K) or B_shard.shape != (nb, self.K, self.N):
+            raise ValueError("A_shard must be [b1-b0, M, K] and B_shard [b1-b0, K, N]")
+        if self.liveness is not None:
+            self.liveness.step()
+        pt = self._peers(C)
+        s = engine._stream(stream)
+        if nb > 0:
+            off = self.b0 * self.M * self.N * C.element_size()
+            extra = [pt.ptrs[d] + off for d in range(self.world) if d != self.rank]
+            arr = (ctypes.c_void_p * max(1, len(extra)))(*extra)
+            engine._check(engine.lib().mt_gemm_multi(ctypes.byref(engine.view(A_shard)),
+                                                     ctypes.byref(engine.view(B_shard)),
+                                                     ctypes.byref(engine.view(C[self.b0:self.b1])), arr, len(extra),
+                                                     None, 0, engine._mode(mode), s))
+        self._barrier(s)
 
 
 class PeerLost(RuntimeError):
@@ -259,3 +318,21 @@ def allgather_shards(C_shard: torch.Tensor, world: int, group=None) -> torch.Ten
     parts = [torch.empty_like(C_shard) for _ in range(world)]
     dist.all_gather(parts, C_shard.contiguous(), group=group)
     return torch.cat(parts, dim=1)
+
+
+def allgather_batch_shards(C_block: torch.Tensor, batch: int, world: int, group=None) -> torch.Tensor:
+    """Baseline reassembly of a batch-sharded bmm: all-gather every rank's block of batches
+    (NCCL on GPU, gloo on CPU; blocks padded to the largest so the collective sees equal
+    sizes) into [batch, M, N]. Each block is contiguous in the result: no relayout."""
+    M, N = C_block.shape[1], C_block.shape[2]
+    width = (batch + world - 1) // world
+    pad = torch.zeros((width, M, N), dtype=C_block.dtype, device=C_block.device)
+    pad[:C_block.shape[0]] = C_block
+    parts = [torch.empty_like(pad) for _ in range(world)]
+    dist.all_gather(parts, pad, group=group)
+    blocks = []
+    for r, part in enumerate(parts):
+        b0, b1 = shard_batches(batch, world, r)
+        blocks.append(part[:b1 - b0])
+    return torch.cat(blocks, dim=0)
+

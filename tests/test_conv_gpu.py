@@ -164,7 +164,6 @@ def test_device_status_clean_after_conv(eng):
     assert eng.device_status(reset=True) == 0
 
 
-@pytest.mark.first_gpu_run
 @pytest.mark.parametrize("mode", MODES)
 @pytest.mark.parametrize("shape", [
     # N, C, H, W, Co, kh, kw, stride, pad
@@ -192,7 +191,6 @@ def test_conv_non_square_filters(eng, port, mode, shape):
     assert np.allclose(db, port.conv2d_bwd_bias(dy), rtol=1e-5, atol=1e-5)
 
 
-@pytest.mark.first_gpu_run
 @pytest.mark.parametrize("mode", ["tf32", "tf32x3"])
 def test_conv_per_tap_fallback(eng, port, mode):
     """A 7x7 filter over 200-pixel rows: two halo slots (128-pixel pitch x 7 rows) exceed the

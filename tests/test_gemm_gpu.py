@@ -318,7 +318,6 @@ def _bmm_grads_ref(port, A, B, dC):
     return dA, dB
 
 
-@pytest.mark.first_gpu_run
 @pytest.mark.parametrize("mode", MODES)
 @pytest.mark.parametrize("case", ["batched", "b_broadcast", "a_broadcast", "config3"])
 def test_bmm_backward(eng, port, mode, case):
@@ -353,7 +352,6 @@ def test_bmm_backward(eng, port, mode, case):
         check(mode, host(dB), dB_ref, DB, M, f"{case} dB")
 
 
-@pytest.mark.first_gpu_run
 @pytest.mark.parametrize("mode", ["tf32", "tf32x3"])
 def test_one_cta_wide_tiles_batched_short_rows(eng, port, mode):
     """Batched outputs with M <= 128 and enough 128x256 tiles to fill the GPU: too short for

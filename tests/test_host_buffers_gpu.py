@@ -7,7 +7,7 @@ import torch
 from minitensor_b200 import inputs
 from parity import absmm, check, host
 
-pytestmark = [pytest.mark.gpu, pytest.mark.first_gpu_run]
+pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("mode", ["strict", "tf32", "tf32x3"])

@@ -99,6 +99,26 @@ def test_column_shard_into_wide_buffers(eng, port):
         check("tf32x3", host(C), ref, absmm(A, B), K, "sharded layout")
 
 
+@pytest.mark.parametrize("mode", ["tf32x3", "tf32", "strict"])
+def test_batch_shard_into_full_buffers(eng, port, mode):
+    """The batch-sharded layout on one GPU: 3 "ranks" each compute a block of a broadcast
+    bmm (batch 7 cut 2/2/3, B broadcast with batch stride 0) and write it into all three
+    full-size Cs through the 3-D multi-destination epilogue."""
+    from minitensor_b200.sharded import shard_batches
+    bt, M, K, N, world = 7, 320, 64, 288, 3
+    A = inputs.uniform((bt, M, K), -1, 1, 91)
+    B0 = inputs.uniform((1, K, N), -1, 1, 92)
+    Cs = [torch.full((bt, M, N), -5.0, device="cuda") for _ in range(world)]
+    Ad, Bd = dev(A), dev(B0)
+    for r in range(world):
+        b0, b1 = shard_batches(bt, world, r)
+        others = [Cs[d][b0:] for d in range(world) if d != r]   # element (b0, 0, 0) of each peer C
+        _multi(Ad[b0:b1], Bd.expand(b1 - b0, K, N), Cs[r][b0:b1], others, mode)
+    ref = port.bmm(A, np.broadcast_to(B0, (bt, K, N)))
+    for C in Cs:
+        check(mode, host(C), ref, absmm(A, B0), K, "batch-sharded layout")
+
+
 def test_peer_barrier_timeout_reports_status(eng):
     L = engine.lib()
     L.mt_peer_barrier.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_uint64,
@@ -169,3 +189,44 @@ def test_sharded_gemm_two_gpus(eng, port, tmp_path, mode, shape, gather):
     ref = port.matmul_strided(A[rows], B)
     for r in range(world):
         check(mode, np.load(tmp_path / f"c{r}.npy")[rows], ref, absmm(A[rows], B), K, f"rank {r}")
+
+
+def _bmm_worker(rank, world, port, out, mode, shape):
+    import torch.distributed as dist
+    from minitensor_b200 import sharded
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    bt, M, K, N = shape
+    A = inputs.uniform((bt, M, K), -1, 1, 93)
+    B0 = inputs.uniform((1, K, N), -1, 1, 94)
+    plan = sharded.ShardedBmm(bt, M, N, K, rank, world, timeout_s=5.0)
+    C = torch.zeros(bt, M, N, device="cuda")
+    Ad = dev(np.ascontiguousarray(A[plan.b0:plan.b1]))
+    Bd = dev(B0).expand(plan.b1 - plan.b0, K, N)
+    for _ in range(2):   # the second call reuses the mappings with a new epoch
+        plan.run(Ad, Bd, C, mode=mode)
+    torch.cuda.synchronize()
+    np.save(os.path.join(out, f"c{rank}.npy"), C.cpu().numpy())
+    status = engine.device_status(reset=True)
+    dist.barrier()
+    plan.close()
+    dist.destroy_process_group()
+    assert status == 0, status
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("mode,shape", [("tf32x3", (64, 512, 64, 512)), ("tf32", (7, 300, 96, 520)),
+                                        ("strict", (5, 256, 64, 256))])
+def test_sharded_bmm_two_gpus(eng, port, tmp_path, mode, shape):
+    """Batch shards of a broadcast bmm on two GPUs (config 3's shape, and uneven batches
+    with ragged tiles): every rank ends with the whole C."""
+    import torch.multiprocessing as mp
+    world = 2
+    mp.spawn(_bmm_worker, args=(world, _free_port(), str(tmp_path), mode, shape), nprocs=world, join=True)
+    bt, M, K, N = shape
+    A = inputs.uniform((bt, M, K), -1, 1, 93)
+    B0 = inputs.uniform((1, K, N), -1, 1, 94)
+    ref = port.bmm(A, np.broadcast_to(B0, (bt, K, N)))
+    for r in range(world):
+        check(mode, np.load(tmp_path / f"c{r}.npy"), ref, absmm(A, B0), K, f"rank {r}")

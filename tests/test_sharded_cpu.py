@@ -13,7 +13,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from minitensor_b200.sharded import allgather_shards, shard_columns
+from minitensor_b200.sharded import allgather_batch_shards, allgather_shards, shard_batches, shard_columns
 
 
 def free_port():
@@ -31,6 +31,42 @@ def test_shard_plan_covers_columns():
                 assert 0 <= n0 <= n1 <= N
                 cols.extend(range(n0, n1))
             assert cols == list(range(N))
+
+
+def test_batch_shard_plan_covers_batches():
+    for batch in (1, 2, 7, 64, 65):
+        for world in (1, 2, 3, 4, 8):
+            got = []
+            for r in range(world):
+                b0, b1 = shard_batches(batch, world, r)
+                assert 0 <= b0 <= b1 <= batch and b1 - b0 in (batch // world, batch // world + 1)
+                got.extend(range(b0, b1))
+            assert got == list(range(batch))
+
+
+def _batch_gather_worker(rank, world, port, out, batch):
+    # Each rank computes its block of a broadcast bmm (config 3's shape, batch cut
+    # unevenly) and the baseline all-gather reassembles [batch, M, N] on every rank.
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    rs = np.random.RandomState(1)
+    A = rs.standard_normal((batch, 6, 4)).astype(np.float32)
+    B0 = rs.standard_normal((1, 4, 5)).astype(np.float32)
+    b0, b1 = shard_batches(batch, world, rank)
+    block = torch.from_numpy(np.matmul(A[b0:b1], B0))
+    C = allgather_batch_shards(block, batch, world)
+    np.save(os.path.join(out, f"c{rank}.npy"), C.numpy())
+    np.save(os.path.join(out, "ref.npy"), np.matmul(A, B0))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,batch", [(2, 7), (3, 64)])
+def test_batch_allgather_reassembly_gloo(tmp_path, world, batch):
+    mp.spawn(_batch_gather_worker, args=(world, free_port(), str(tmp_path), batch), nprocs=world, join=True)
+    ref = np.load(tmp_path / "ref.npy")
+    for r in range(world):
+        assert np.array_equal(np.load(tmp_path / f"c{r}.npy"), ref)
 
 
 def _gather_worker(rank, world, port, out):

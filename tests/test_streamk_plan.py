@@ -1,0 +1,98 @@
+"""CPU tests of the CTA-pair kernel's work schedule (whole tiles round-robin, then the
+stream-K remainder), restated from minitensor_b200/csrc/umma_gemm2.cuh (Sched) and
+mt_api.cu (pair_streamk_plan). The kernel's correctness rests on three properties that
+are pure integer arithmetic, checked here over many shapes:
+
+1. every (tile, k-block) is done by exactly one cluster;
+2. the pieces of a cut tile carry seg = 0 .. nseg-1 in k order, each exactly once, and
+   every piece agrees on nseg (the last-arriver count and the partial slots depend on it);
+3. nseg never exceeds the partial slots the host allocates (sk_maxseg).
+"""
+import itertools
+
+import pytest
+
+
+def plan(num_tiles, clusters, kblocks):
+    """(sk_dp, maxseg) as pair_streamk_plan sets them (stream-K on)."""
+    if clusters <= 0 or num_tiles <= clusters:
+        return num_tiles, 0
+    rem = num_tiles % clusters
+    W = rem * kblocks
+    if rem == 0 or W < 8 * clusters:
+        return num_tiles, 0
+    minr = W // clusters
+    return num_tiles - rem, (kblocks + minr - 1) // minr + 1
+
+
+def items(num_tiles, sk_dp, kblocks, c, C):
+    """The Sched sequence of cluster c of C: (tile, kb0, kb1, seg, nseg)."""
+    out = []
+    u = c
+    while u < sk_dp:
+        out.append((u, 0, kblocks, 0, 1))
+        u += C
+    W = (num_tiles - sk_dp) * kblocks
+    if W == 0:
+        return out
+    x, hi = W * c // C, W * (c + 1) // C
+
+    def owner(y):
+        return ((y + 1) * C + W - 1) // W - 1
+
+    while x < hi:
+        t = x // kblocks
+        kb0 = x - t * kblocks
+        kb1 = min(kblocks, kb0 + (hi - x))
+        cf = owner(t * kblocks)
+        nseg = owner(t * kblocks + kblocks - 1) - cf + 1
+        out.append((sk_dp + t, kb0, kb1, c - cf, nseg))
+        x += kb1 - kb0
+    return out
+
+
+def check_schedule(num_tiles, C, kblocks):
+    sk_dp, maxseg = plan(num_tiles, C, kblocks)
+    covered = {}
+    pieces = {}
+    for c in range(C):
+        for tile, kb0, kb1, seg, nseg in items(num_tiles, sk_dp, kblocks, c, C):
+            assert 0 <= kb0 < kb1 <= kblocks
+            for kb in range(kb0, kb1):
+                assert (tile, kb) not in covered, (tile, kb)
+                covered[(tile, kb)] = c
+            pieces.setdefault(tile, []).append((kb0, kb1, seg, nseg, c))
+    assert len(covered) == num_tiles * kblocks
+    for tile, ps in pieces.items():
+        ps.sort()
+        nsegs = {p[3] for p in ps}
+        assert len(nsegs) == 1 and nsegs.pop() == len(ps), (tile, ps)
+        assert [p[2] for p in ps] == list(range(len(ps))), (tile, ps)   # seg in k order
+        if len(ps) > 1:
+            assert tile >= sk_dp and len(ps) <= maxseg, (tile, len(ps), maxseg)
+            clusters = [p[4] for p in ps]
+            assert clusters == list(range(clusters[0], clusters[0] + len(ps)))   # consecutive clusters
+    return sk_dp, maxseg
+
+
+def test_config5_shards():
+    # 8192^3 over 1, 2, 4, 8 GPUs with 74 clusters: 256 x 256 tiles (K = 8192 -> 256 k-blocks),
+    # and 256 x 128 tiles for the 8-GPU shard.
+    for tiles in (1024, 512, 256, 128):
+        sk_dp, maxseg = check_schedule(tiles, 74, 256)
+        assert sk_dp == tiles - tiles % 74 and maxseg >= 2
+    sk_dp, maxseg = check_schedule(256, 74, 256)
+    assert (sk_dp, maxseg) == (222, 4)
+
+
+def test_off_when_ranges_would_be_short_or_rounds_are_whole():
+    assert plan(148, 74, 256) == (148, 0)          # whole rounds
+    assert plan(90, 74, 5) == (90, 0)              # 16 x 5 k-blocks < 8 per cluster
+    assert plan(60, 74, 256) == (60, 0)            # fewer tiles than clusters: not a pair launch
+    check_schedule(90, 74, 5)
+
+
+@pytest.mark.parametrize("C", [1, 2, 3, 7, 37, 74])
+def test_many_shapes(C):
+    for tiles, kblocks in itertools.product([C + 1, 2 * C - 1, 3 * C + 2, 5 * C + C // 2 + 1], [1, 2, 7, 8, 9, 31, 64, 256]):
+        check_schedule(tiles, C, kblocks)
