@@ -239,6 +239,26 @@ MT_API int mt_peer_barrier(int* const* flags, int rank, int world, int epoch, ui
 MT_API int mt_copy_rows_async(void* dst, uint64_t dpitch, const void* src, uint64_t spitch, uint64_t width_bytes,
                               uint64_t rows, void* stream);
 
+/* ---- scratch memory ------------------------------------------------------------------ */
+
+/* Where the library's temporary device buffers come from (split-K and stream-K partials,
+ * the stride-1 conv's NHWC copy and reordered weights, weight-grad partials). The
+ * reference takes scratch from its MemoryPool (include/MemoryPool.hpp:45-99); its drop-in
+ * overlay installs the pool here. With no allocator installed (the default, or after
+ * passing NULL, NULL) every buffer is a stream-ordered cudaMallocAsync / cudaFreeAsync on
+ * the call's stream. With one installed, alloc(bytes, device, ctx) is called before the
+ * kernels are enqueued and free(ptr, bytes, device, ctx) right after: the block may be
+ * handed out again while those kernels still run, so work sharing the allocator must be
+ * ordered on one stream (the reference's active_stream()). A NULL from alloc fails the
+ * call with MT_ENOMEM. Install it once, before other calls; mt_matmul_host keeps its
+ * stream-ordered workspace (it spans several streams) unless given one. */
+typedef void* (*mt_scratch_alloc_fn)(size_t bytes, int device, void* ctx);
+typedef void (*mt_scratch_free_fn)(void* ptr, size_t bytes, int device, void* ctx);
+MT_API int mt_set_scratch_allocator(mt_scratch_alloc_fn alloc, mt_scratch_free_fn free_fn, void* ctx);
+/* Scratch buffers obtained so far (all threads): stream-ordered, and from the installed
+ * allocator. */
+MT_API void mt_scratch_counts(uint64_t* stream_ordered, uint64_t* from_allocator);
+
 /* ---- process settings and diagnostics ---------------------------------------------- */
 
 MT_API int mt_set_default_mode(int mode);   /* returns the previous default */

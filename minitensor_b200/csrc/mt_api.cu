@@ -222,6 +222,58 @@ int launch_umma_inst(const CUtensorMap& ta, const CUtensorMap& tb, const mt::umm
     return MT_OK;
 }
 
+// ---- scratch memory ----------------------------------------------------------------
+// Every temporary buffer of the library (split-K and stream-K partials, the NHWC copy and
+// reordered weights of the stride-1 conv, weight-grad partials, the host-buffer GEMM's
+// device copies) comes from scratch_alloc. By default that is a stream-ordered allocation
+// (cudaMallocAsync / cudaFreeAsync on the call's stream: capturable, freed in stream order).
+// A host that manages device memory itself installs its allocator with
+// mt_set_scratch_allocator; the library then returns each block right after enqueuing the
+// kernels that use it, which is safe for work ordered on one stream.
+struct ScratchHook {
+    mt_scratch_alloc_fn alloc = nullptr;
+    mt_scratch_free_fn free = nullptr;
+    void* ctx = nullptr;
+};
+std::mutex g_scratch_mu;
+ScratchHook g_scratch;
+std::atomic<uint64_t> g_async_allocs{0}, g_hook_allocs{0};
+
+ScratchHook scratch_hook() {
+    std::lock_guard<std::mutex> g(g_scratch_mu);
+    return g_scratch;
+}
+
+int scratch_alloc(void** p, size_t bytes, cudaStream_t st, const char* who) {
+    *p = nullptr;
+    if (bytes == 0) return MT_OK;
+    const ScratchHook h = scratch_hook();
+    if (h.alloc) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        *p = h.alloc(bytes, dev, h.ctx);
+        if (!*p) return fail(MT_ENOMEM, "%s: the scratch allocator returned NULL for %zu bytes", who, bytes);
+        g_hook_allocs.fetch_add(1);
+        return MT_OK;
+    }
+    cudaError_t e = cudaMallocAsync(p, bytes, st);
+    if (e != cudaSuccess) return cuda_fail(e, who);
+    g_async_allocs.fetch_add(1);
+    return MT_OK;
+}
+
+void scratch_free(void* p, size_t bytes, cudaStream_t st) {
+    if (!p) return;
+    const ScratchHook h = scratch_hook();
+    if (h.free) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        h.free(p, bytes, dev, h.ctx);
+    } else {
+        cudaFreeAsync(p, st);
+    }
+}
+
 // Stream-K remainder of a pair launch with `clusters` clusters (see umma::Params). When
 // the tiles do not divide into whole rounds over the clusters, the last num_tiles %
 // clusters tiles are cut into equal k-block ranges, one per cluster, as long as every range
@@ -235,8 +287,10 @@ bool streamk_enabled() {
     return v != 0;
 }
 
-int pair_streamk_plan(mt::umma::Params& up, int clusters, int kblocks, int bn, cudaStream_t st, void** ws_out) {
+int pair_streamk_plan(mt::umma::Params& up, int clusters, int kblocks, int bn, cudaStream_t st, void** ws_out,
+                      size_t* ws_bytes_out) {
     *ws_out = nullptr;
+    *ws_bytes_out = 0;
     up.sk_dp = up.num_tiles;
     up.sk_clusters = clusters;
     up.sk_maxseg = 0;
@@ -252,12 +306,12 @@ int pair_streamk_plan(mt::umma::Params& up, int clusters, int kblocks, int bn, c
     const size_t ws_bytes = (size_t)rem * maxseg * mt::umma2::BM * bn * sizeof(float);
     const size_t cnt_bytes = (size_t)rem * 8 * sizeof(int);
     void* ws = nullptr;
-    cudaError_t e = cudaMallocAsync(&ws, ws_bytes + cnt_bytes, st);
-    if (e != cudaSuccess) return cuda_fail(e, "stream-K workspace");
+    int rc = scratch_alloc(&ws, ws_bytes + cnt_bytes, st, "stream-K workspace");
+    if (rc) return rc;
     int* cnt = reinterpret_cast<int*>(static_cast<char*>(ws) + ws_bytes);
-    e = cudaMemsetAsync(cnt, 0, cnt_bytes, st);
+    cudaError_t e = cudaMemsetAsync(cnt, 0, cnt_bytes, st);
     if (e != cudaSuccess) {
-        cudaFreeAsync(ws, st);
+        scratch_free(ws, ws_bytes + cnt_bytes, st);
         return cuda_fail(e, "stream-K counters");
     }
     up.sk_dp = up.num_tiles - rem;
@@ -265,6 +319,7 @@ int pair_streamk_plan(mt::umma::Params& up, int clusters, int kblocks, int bn, c
     up.sk_ws = static_cast<float*>(ws);
     up.sk_cnt = cnt;
     *ws_out = ws;
+    *ws_bytes_out = ws_bytes + cnt_bytes;
     return MT_OK;
 }
 
@@ -302,11 +357,12 @@ int launch_pair_inst(const CUtensorMap& ta, const CUtensorMap& tb, const mt::umm
     }
     const int clusters = (int)std::min<long long>(up.num_tiles, (long long)max_clusters[dev & 63].load());
     void* ws = nullptr;
-    int rc = pair_streamk_plan(up, clusters, (up.K + BKE - 1) / BKE, BN, st, &ws);
+    size_t ws_bytes = 0;
+    int rc = pair_streamk_plan(up, clusters, (up.K + BKE - 1) / BKE, BN, st, &ws, &ws_bytes);
     if (rc) return rc;
     kern<<<2 * clusters, G::THREADS, G::SMEM_BYTES, st>>>(ta, tb, dm, up);
     cudaError_t e = cudaGetLastError();
-    if (ws) cudaFreeAsync(ws, st);
+    scratch_free(ws, ws_bytes, st);
     if (e != cudaSuccess && e != cudaErrorStreamCaptureUnsupported) return cuda_fail(e, "umma pair gemm launch");
     g_launches.fetch_add(1);
     return MT_OK;
@@ -443,10 +499,10 @@ int launch_umma(const GemmProblem& p, bool x3, cudaStream_t st, float* const* ex
     up.splits = splits;
     up.num_units = up.num_tiles * splits;
     float* ws = nullptr;
+    const size_t splitk_bytes = (size_t)splits * (size_t)p.M * (size_t)p.N * sizeof(float);
     if (splits > 1) {
-        const size_t bytes = (size_t)splits * (size_t)p.M * (size_t)p.N * sizeof(float);
-        cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&ws), bytes, st);
-        if (e != cudaSuccess) return cuda_fail(e, "gemm split-K workspace");
+        const int arc = scratch_alloc(reinterpret_cast<void**>(&ws), splitk_bytes, st, "gemm split-K workspace");
+        if (arc) return arc;
         up.dst[0] = ws;
         up.sc_m = p.N;
         up.split_stride = (int64_t)p.M * p.N;
@@ -508,7 +564,7 @@ int launch_umma(const GemmProblem& p, bool x3, cudaStream_t st, float* const* ex
             if (e != cudaSuccess && e != cudaErrorStreamCaptureUnsupported) rc = cuda_fail(e, "split-K epilogue");
             else g_launches.fetch_add(1);
         }
-        cudaFreeAsync(ws, st);
+        scratch_free(ws, splitk_bytes, st);
     }
     if (rc == MT_OK) {
         char buf[112];
@@ -1007,8 +1063,7 @@ int conv_fwd(const mt_tensor* x, const mt_tensor* w, const mt_tensor* bias, cons
         // TMA path: x -> NHWC and W -> [tap][co][ci] in a stream-ordered scratch buffer.
         const size_t bytes = fwd_tma_scratch(s.N, s.H, s.W, s.C, s.Co, s.kh * s.kw);
         float* scratch = nullptr;
-        cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&scratch), bytes, st);
-        if (e != cudaSuccess) return cuda_fail(e, "conv fwd scratch");
+        if ((rc = scratch_alloc(reinterpret_cast<void**>(&scratch), bytes, st, "conv fwd scratch"))) return rc;
         float* xt = scratch;
         float* wt = scratch + ((s.N * s.H * s.W * ((s.C + 3) & ~3) + 63) & ~int64_t(63));
         std::string path;
@@ -1016,7 +1071,7 @@ int conv_fwd(const mt_tensor* x, const mt_tensor* w, const mt_tensor* bias, cons
         if (!rc) rc = run_fwd_tma(xt, (int)s.N, (int)s.H, (int)s.W, (int)s.C, cp.w, cp.sw, false, wt, (int)s.Co,
                                   (int)s.kh, (int)s.kw,
                                   (int)s.pad, cp.out, (int)s.Ho, (int)s.Wo, bp, x3, st, di.sms, path);
-        cudaFreeAsync(scratch, st);
+        scratch_free(scratch, bytes, st);
         if (rc == MT_OK) t_path = std::string("conv_umma_fwd_") + (x3 ? "tf32x3 " : "tf32 ") + path;
         return rc;
     }
@@ -1065,8 +1120,7 @@ int conv_dgrad(const mt_tensor* dy, const mt_tensor* w, const mt_tensor* dx, uin
         // take the gather kernel below, which indexes dy per dimension.
         const size_t bytes = fwd_tma_scratch(s.N, s.Ho, s.Wo, s.Co, s.C, s.kh * s.kw);
         float* scratch = nullptr;
-        cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&scratch), bytes, st);
-        if (e != cudaSuccess) return cuda_fail(e, "conv dgrad scratch");
+        if ((rc = scratch_alloc(reinterpret_cast<void**>(&scratch), bytes, st, "conv dgrad scratch"))) return rc;
         float* dyt = scratch;
         float* wt = scratch + ((s.N * s.Ho * s.Wo * ((s.Co + 3) & ~3) + 63) & ~int64_t(63));
         std::string path;
@@ -1074,7 +1128,7 @@ int conv_dgrad(const mt_tensor* dy, const mt_tensor* w, const mt_tensor* dx, uin
         if (!rc) rc = run_fwd_tma(dyt, (int)s.N, (int)s.Ho, (int)s.Wo, (int)s.Co, cp.w, cp.sw, true, wt, (int)s.C,
                                   (int)s.kh, (int)s.kw,
                                   (int)(s.kh - 1 - s.pad), cp.out, (int)s.H, (int)s.W, nullptr, x3, st, di.sms, path);
-        cudaFreeAsync(scratch, st);
+        scratch_free(scratch, bytes, st);
         if (rc == MT_OK) t_path = std::string("conv_umma_dgrad_") + (x3 ? "tf32x3 " : "tf32 ") + path;
         return rc;
     }
@@ -1227,12 +1281,11 @@ int conv_wgrad(const mt_tensor* dy, const mt_tensor* x, const mt_tensor* dw, uin
             if (ws_bytes < tp.bytes)
                 return fail(MT_EINVAL, "%s: workspace of %zu bytes < %zu needed", who, ws_bytes, tp.bytes);
         } else {
-            cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&scratch), tp.bytes, st);
-            if (e != cudaSuccess) return cuda_fail(e, "conv wgrad scratch");
+            if ((rc = scratch_alloc(reinterpret_cast<void**>(&scratch), tp.bytes, st, "conv wgrad scratch"))) return rc;
             owned = true;
         }
         rc = conv_wgrad_tma(s, tp, cp, dwp, scratch, x3w, st, di.sms, who);
-        if (owned) cudaFreeAsync(scratch, st);
+        if (owned) scratch_free(scratch, tp.bytes, st);
         if (rc == MT_OK)
             t_path = std::string("conv_umma_wgrad_") + (x3w ? "tf32x3" : "tf32") + " tma bn=" + std::to_string(tp.bn) +
                      " splits=" + std::to_string(tp.splits);
@@ -1251,9 +1304,8 @@ int conv_wgrad(const mt_tensor* dy, const mt_tensor* x, const mt_tensor* dw, uin
                 return fail(MT_EINVAL, "%s: workspace of %zu bytes < %zu needed", who, ws_bytes, wp.ws_bytes);
             part = static_cast<float*>(workspace);
         } else {
-            // Stream-ordered allocation from the device's default pool (capturable).
-            cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&part), wp.ws_bytes, st);
-            if (e != cudaSuccess) return cuda_fail(e, "conv wgrad workspace");
+            if ((rc = scratch_alloc(reinterpret_cast<void**>(&part), wp.ws_bytes, st, "conv wgrad workspace")))
+                return rc;
             owned = true;
         }
     }
@@ -1269,7 +1321,7 @@ int conv_wgrad(const mt_tensor* dy, const mt_tensor* x, const mt_tensor* dw, uin
         if (e != cudaSuccess && e != cudaErrorStreamCaptureUnsupported) rc = cuda_fail(e, "splitk reduce");
         else g_launches.fetch_add(1);
     }
-    if (owned) cudaFreeAsync(part, st);
+    if (owned) scratch_free(part, wp.ws_bytes, st);
     if (rc == MT_OK)
         t_path = std::string("conv_umma_wgrad_") + (x3 ? "tf32x3" : "tf32") + " gather bn=" + std::to_string(bn) +
                  " splits=" + std::to_string(wp.splits);
@@ -1846,6 +1898,21 @@ MT_API int mt_copy_rows_async(void* dst, uint64_t dpitch, const void* src, uint6
                                       static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "copy_rows_async");
     return MT_OK;
+}
+
+MT_API int mt_set_scratch_allocator(mt_scratch_alloc_fn alloc, mt_scratch_free_fn free_fn, void* ctx) {
+    if ((alloc == nullptr) != (free_fn == nullptr))
+        return fail(MT_EINVAL, "set_scratch_allocator: give both functions, or neither");
+    std::lock_guard<std::mutex> g(g_scratch_mu);
+    g_scratch.alloc = alloc;
+    g_scratch.free = free_fn;
+    g_scratch.ctx = ctx;
+    return MT_OK;
+}
+
+MT_API void mt_scratch_counts(uint64_t* stream_ordered, uint64_t* from_allocator) {
+    if (stream_ordered) *stream_ordered = g_async_allocs.load();
+    if (from_allocator) *from_allocator = g_hook_allocs.load();
 }
 
 MT_API int mt_set_default_mode(int mode) {

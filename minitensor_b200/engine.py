@@ -103,6 +103,10 @@ def lib() -> ctypes.CDLL:
     L.mt_matmul_host.restype = ctypes.c_int
     L.mt_matmul_host_workspace_bytes.argtypes = [u64, u64, u64]
     L.mt_matmul_host_workspace_bytes.restype = ctypes.c_size_t
+    L.mt_set_scratch_allocator.argtypes = [vp, vp, vp]
+    L.mt_set_scratch_allocator.restype = ctypes.c_int
+    L.mt_scratch_counts.argtypes = [ctypes.POINTER(u64), ctypes.POINTER(u64)]
+    L.mt_scratch_counts.restype = None
     L.mt_set_default_mode.argtypes = [ctypes.c_int]
     L.mt_set_default_mode.restype = ctypes.c_int
     L.mt_get_default_mode.restype = ctypes.c_int
@@ -487,6 +491,13 @@ def launch_count() -> int:
 
 def device_status(reset: bool = True) -> int:
     return int(lib().mt_device_status(1 if reset else 0))
+
+
+def scratch_counts() -> tuple[int, int]:
+    """(stream-ordered, from the installed allocator) scratch buffers obtained so far."""
+    a, b = ctypes.c_uint64(0), ctypes.c_uint64(0)
+    lib().mt_scratch_counts(ctypes.byref(a), ctypes.byref(b))
+    return int(a.value), int(b.value)
 
 
 def version() -> str:

@@ -172,10 +172,15 @@ int main() {
     }
     {   // include/GraphExecutor.hpp: warm-up, capture (Relaxed, on active_stream()) and replay
         // of a whole training step; the captured GEMMs are this library's kernels. Compared
-        // step by step with eager training of an identical model.
+        // step by step with eager training of an identical model. The first layer's forward
+        // (32 x 1024 . 1024 x 128: one output tile, a long K) runs split-K, whose partials are
+        // scratch; with the overlay's MemoryPool allocator installed, no stream-ordered
+        // allocation may happen anywhere in the step, so the captured graph holds none.
+        uint64_t async0 = 0, pool0 = 0;
+        mt_scratch_counts(&async0, &pool0);
         auto make = [] {
             return std::make_shared<Sequential<float>>(std::initializer_list<std::shared_ptr<Module<float>>>{
-                std::make_shared<Linear<float>>(64, 128), std::make_shared<ReLU<float>>(),
+                std::make_shared<Linear<float>>(1024, 128), std::make_shared<ReLU<float>>(),
                 std::make_shared<Linear<float>>(128, 16)});
         };
         auto eager = make();
@@ -188,7 +193,7 @@ int main() {
         SGD<float> opt_e(eager->parameters(), 0.05f), opt_g(graphed->parameters(), 0.05f);
         GraphExecutor<float> exec(graphed, opt_g,
                                   [](const Tensor<float>& p, const Tensor<float>& t) { return mse_loss(p, t); });
-        Tensor<float> x = filled({32, 64}, 16).to(kGpu), y = filled({32, 16}, 17).to(kGpu);
+        Tensor<float> x = filled({32, 1024}, 16).to(kGpu), y = filled({32, 16}, 17).to(kGpu);
         bool ok = true;
         double worst = 0;
         for (int step = 0; step < 4; ++step) {
@@ -209,6 +214,12 @@ int main() {
             ok = ok && pok;
         }
         report("GraphExecutor capture/replay of a training step", ok, worst);
+        uint64_t async1 = 0, pool1 = 0;
+        mt_scratch_counts(&async1, &pool1);
+        std::printf("scratch during the step: %llu from MemoryPool, %llu stream-ordered (total stream-ordered %llu)\n",
+                    (unsigned long long)(pool1 - pool0), (unsigned long long)(async1 - async0),
+                    (unsigned long long)async1);
+        report("step scratch from MemoryPool, no stream-ordered allocation", pool1 > pool0 && async1 == 0, 0.0);
     }
     std::printf("%s: %d failure(s)\n", failures ? "FAILED" : "ALL PASSED", failures);
     return failures ? 1 : 0;

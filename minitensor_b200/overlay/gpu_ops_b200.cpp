@@ -12,13 +12,15 @@
 // failures (as GPU_CHECK does, include/GpuUtils.hpp:10-18).
 //
 // Also registers the engine in the reference's (otherwise unused) OpRegistry<float>
-// under OpType::Matmul and OpType::Conv2D (include/Dispatch.hpp:12-58).
+// under OpType::Matmul and OpType::Conv2D (include/Dispatch.hpp:12-58), and hands the
+// engine's scratch allocations to the reference's MemoryPool.
 #include <iostream>
 #include <stdexcept>
 #include <type_traits>
 
 #include "Dispatch.hpp"
 #include "GpuUtils.hpp"
+#include "MemoryPool.hpp"
 #include "Tensor.hpp"
 #include "TensorOps.hpp"
 #include "mtgemm.h"
@@ -145,6 +147,29 @@ Tensor<float> mt_linear_forward(const Tensor<float>& x, const Tensor<float>& W, 
     check(mt_linear_fwd_gpu(&xv, &wv, bias.empty() ? nullptr : &bv, &yv, relu ? 1 : 0, stream()));
     return y;
 }
+
+// ---- scratch from the reference's MemoryPool (include/MemoryPool.hpp:45-99) -----------
+// The reference's GPU routines take their temporary buffers from MemoryPool::get() and
+// return them right after enqueuing their kernels on active_stream(); the engine's scratch
+// (split-K / stream-K partials, conv NHWC copies, weight-grad partials) now does the same,
+// so a captured step (GraphExecutor) holds no allocation node of this library and reuses
+// the pool's cached blocks on every replay.
+namespace {
+void* pool_alloc(size_t bytes, int device, void*) {
+    try {
+        return MemoryPool::get().allocate(bytes, Device{DeviceType::CUDA, static_cast<uint8_t>(device)});
+    } catch (const std::exception& e) {
+        std::cerr << "MemoryPool: " << e.what() << std::endl;
+        return nullptr;
+    }
+}
+void pool_free(void* ptr, size_t bytes, int device, void*) {
+    MemoryPool::get().free(ptr, bytes, Device{DeviceType::CUDA, static_cast<uint8_t>(device)});
+}
+struct InstallPool {
+    InstallPool() { mt_set_scratch_allocator(pool_alloc, pool_free, nullptr); }
+} install_pool;
+}  // namespace
 
 // ---- OpRegistry registrations (include/Dispatch.hpp:50-58) ----------------------------
 namespace {

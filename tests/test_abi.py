@@ -233,3 +233,13 @@ def test_peer_barrier_refuses_unbounded_timeout():
     rc = lib.mt_peer_barrier(flags, 0, 1, 1, 2**64 - 1, None)
     assert rc == engine.MT_EINVAL
     assert b"timeout" in lib.mt_last_error()
+
+
+def test_scratch_allocator_needs_both_functions():
+    lib = engine.lib()
+    fn = ctypes.CFUNCTYPE(ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_void_p)(lambda b, d, c: None)
+    assert lib.mt_set_scratch_allocator(ctypes.cast(fn, ctypes.c_void_p), None, None) == engine.MT_EINVAL
+    assert b"both" in lib.mt_last_error()
+    assert lib.mt_set_scratch_allocator(None, None, None) == engine.MT_OK   # back to stream-ordered
+    a, b = engine.scratch_counts()
+    assert a >= 0 and b >= 0
