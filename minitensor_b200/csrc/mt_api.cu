@@ -20,6 +20,7 @@
 #include "conv_tma.cuh"
 #include "conv_halo.cuh"
 #include "conv_wgrad.cuh"
+#include "conv_simt.cuh"
 
 namespace {
 
@@ -287,24 +288,40 @@ bool streamk_enabled() {
     return v != 0;
 }
 
-int pair_streamk_plan(mt::umma::Params& up, int clusters, int kblocks, int bn, cudaStream_t st, void** ws_out,
-                      size_t* ws_bytes_out) {
+int pair_streamk_plan(mt::umma::Params& up, int clusters, int kblocks, int bn, bool split_dp, cudaStream_t st,
+                      void** ws_out, size_t* ws_bytes_out) {
     *ws_out = nullptr;
     *ws_bytes_out = 0;
     up.sk_dp = up.num_tiles;
     up.sk_clusters = clusters;
+    up.sk_split = 1;
     up.sk_maxseg = 0;
+    up.sk_t0 = up.num_tiles;
     up.sk_ws = nullptr;
     up.sk_cnt = nullptr;
-    if (!streamk_enabled() || clusters <= 0 || up.num_tiles <= clusters) return MT_OK;
-    const long long rem = up.num_tiles % clusters;
-    const long long W = rem * (long long)kblocks;
-    if (rem == 0 || W < 8LL * clusters) return MT_OK;
-    // A range holds at least floor(W / C) k-blocks, so a tile meets at most this many.
-    const long long minr = W / clusters;
-    const int maxseg = (int)((kblocks + minr - 1) / minr + 1);
-    const size_t ws_bytes = (size_t)rem * maxseg * mt::umma2::BM * bn * sizeof(float);
-    const size_t cnt_bytes = (size_t)rem * 8 * sizeof(int);
+    if (!streamk_enabled() || clusters <= 0) return MT_OK;
+    // Whole tiles in two k-halves: only where asked (a sharded GEMM with few rounds) and
+    // with at least 8 k-blocks per half.
+    const int S = (split_dp && kblocks >= 16) ? 2 : 1;
+    const long long units = up.num_tiles * S;
+    long long sk_dp = up.num_tiles;
+    int maxseg = 0;
+    if (units > clusters) {
+        const long long dp = (units / clusters) * clusters / S;   // whole tiles in whole rounds
+        const long long rem = up.num_tiles - dp;
+        const long long W = rem * (long long)kblocks;
+        if (rem > 0 && W >= 8LL * clusters) {
+            sk_dp = dp;
+            // A range holds at least floor(W / C) k-blocks, so a tile meets at most this many.
+            const long long minr = W / clusters;
+            maxseg = (int)((kblocks + minr - 1) / minr + 1);
+        }
+    }
+    if (S == 1 && sk_dp == up.num_tiles) return MT_OK;
+    const long long t0 = S > 1 ? 0 : sk_dp;
+    const int slots = std::max(S, maxseg);
+    const size_t ws_bytes = (size_t)(up.num_tiles - t0) * slots * mt::umma2::BM * bn * sizeof(float);
+    const size_t cnt_bytes = (size_t)(up.num_tiles - t0) * 8 * sizeof(int);
     void* ws = nullptr;
     int rc = scratch_alloc(&ws, ws_bytes + cnt_bytes, st, "stream-K workspace");
     if (rc) return rc;
@@ -314,8 +331,10 @@ int pair_streamk_plan(mt::umma::Params& up, int clusters, int kblocks, int bn, c
         scratch_free(ws, ws_bytes + cnt_bytes, st);
         return cuda_fail(e, "stream-K counters");
     }
-    up.sk_dp = up.num_tiles - rem;
-    up.sk_maxseg = maxseg;
+    up.sk_dp = sk_dp;
+    up.sk_split = S;
+    up.sk_maxseg = slots;
+    up.sk_t0 = t0;
     up.sk_ws = static_cast<float*>(ws);
     up.sk_cnt = cnt;
     *ws_out = ws;
@@ -358,7 +377,10 @@ int launch_pair_inst(const CUtensorMap& ta, const CUtensorMap& tb, const mt::umm
     const int clusters = (int)std::min<long long>(up.num_tiles, (long long)max_clusters[dev & 63].load());
     void* ws = nullptr;
     size_t ws_bytes = 0;
-    int rc = pair_streamk_plan(up, clusters, (up.K + BKE - 1) / BKE, BN, st, &ws, &ws_bytes);
+    // A GEMM that stores into peers (ndst > 1) with fewer than two rounds of tiles splits
+    // its whole tiles in two, so that finished tiles (and their stores) come twice as often.
+    const bool split_dp = up.ndst > 1 && up.num_tiles < 2LL * clusters;
+    int rc = pair_streamk_plan(up, clusters, (up.K + BKE - 1) / BKE, BN, split_dp, st, &ws, &ws_bytes);
     if (rc) return rc;
     kern<<<2 * clusters, G::THREADS, G::SMEM_BYTES, st>>>(ta, tb, dm, up);
     cudaError_t e = cudaGetLastError();
@@ -373,16 +395,6 @@ int launch_pair_inst(const CUtensorMap& ta, const CUtensorMap& tb, const mt::umm
 bool pair_enabled() {
     static int v = [] {
         const char* e = std::getenv("MT_GEMM_PAIR");
-        return (e && e[0] == '0') ? 0 : 1;
-    }();
-    return v != 0;
-}
-
-// 256 x 128 pair tiles for outputs with fewer than two rounds of 256 x 256 tiles;
-// MT_GEMM_PAIR_BN128=0 keeps 256 x 256.
-bool pair_bn128_enabled() {
-    static int v = [] {
-        const char* e = std::getenv("MT_GEMM_PAIR_BN128");
         return (e && e[0] == '0') ? 0 : 1;
     }();
     return v != 0;
@@ -422,15 +434,11 @@ int launch_umma(const GemmProblem& p, bool x3, cudaStream_t st, float* const* ex
 
     const int64_t tiles_m1 = (p.M + 127) / 128;
     const bool small = tiles_m1 * ((p.N + 255) / 256) * p.batch < (int64_t)di.sms || p.N <= 128;
-    int bn = small ? 128 : 256;
+    const int bn = small ? 128 : 256;
     // CTA pairs: 256 x 256 tiles, at least one per pair of SMs.
     const int64_t tiles256 = ((p.M + 255) / 256) * ((p.N + 255) / 256) * p.batch;
     const bool pair = pair_enabled() && !small && p.M > 128 && tiles256 >= (int64_t)(di.sms / 2);
-    // Fewer than two rounds of 256 x 256 pair tiles (e.g. one rank's 1024-column shard of
-    // an 8192^3 GEMM over 8 GPUs): 256 x 128 tiles. Each tile then takes half as long, so the
-    // first finished tiles (and, in a sharded GEMM, their stores to the peers) come twice
-    // as early and the last round's stores are half as large.
-    if (pair && tiles256 < (int64_t)di.sms && pair_bn128_enabled()) bn = 128;
+
     // k elements per stage: 32 (a 128-byte swizzled row); the one-CTA TF32X3 kernel takes
     // 16 to keep 4-6 stages of hi + lo in shared memory, the pair kernel 32 with 3 stages
     // (half the stage hand-offs per MMA; measured +5% on 8192^3 and a higher clock under
@@ -538,14 +546,10 @@ int launch_umma(const GemmProblem& p, bool x3, cudaStream_t st, float* const* ex
     else if (a_mn == 1 && b_mn == 0) rc = launch_pair_inst<BN_, BKE_, true, false, X3_, ST_>(ta, tb, dm, up, di.sms, st); \
     else rc = launch_pair_inst<BN_, BKE_, true, true, X3_, ST_>(ta, tb, dm, up, di.sms, st);
     if (pair) {
-        // Stages: as many as fit in 227 KB with the 32 KB epilogue staging.
-        if (bn == 256) {
-            if (!x3) { MT_PAIR_DISPATCH(256, 32, false, 6) }
-            else { MT_PAIR_DISPATCH(256, 32, true, 3) }
-        } else {
-            if (!x3) { MT_PAIR_DISPATCH(128, 32, false, 8) }
-            else { MT_PAIR_DISPATCH(128, 32, true, 4) }
-        }
+        // 256 x 256 tiles only: 256 x 128 pair tiles (N = 128 per MMA) measured at half the
+        // rate in both precisions (8192 x 1024 x 8192: 140 vs 260 TFLOP/s in 3xTF32).
+        if (!x3) { MT_PAIR_DISPATCH(256, 32, false, 6) }
+        else { MT_PAIR_DISPATCH(256, 32, true, 3) }
     } else if (!x3) {
         if (bn == 256) { MT_UMMA_DISPATCH(256, 32, false, 4) }
         else { MT_UMMA_DISPATCH(128, 32, false, 6) }
@@ -757,6 +761,62 @@ int direct_launch(void (*kern)(const mt::conv::Params), const mt::conv::Params& 
     g_launches.fetch_add(1);
     return MT_OK;
 }
+
+// ---- strict fp32: implicit GEMMs on FFMA (conv_simt.cuh) ------------------------------
+// kind: mt::convs::kFwd / kDgrad / kWgrad. `part` (wgrad) = N * C*kh*kw * C_out floats of
+// per-image partial sums. Returns MT_EUNSUPPORTED when the grid would exceed its limits
+// (the caller then takes the direct kernels).
+int conv_strict(int kind, const mt::conv::Params& cp, float* part, cudaStream_t st, const char* who) {
+    namespace cs = mt::convs;
+    cs::Params q;
+    memset(&q, 0, sizeof q);
+    q.x = cp.x; q.w = cp.w; q.dy = cp.dy; q.bias = cp.bias;
+    for (int i = 0; i < 4; ++i) { q.sx[i] = cp.sx[i]; q.sw[i] = cp.sw[i]; q.sdy[i] = cp.sdy[i]; }
+    q.N = cp.N; q.C = cp.C; q.H = cp.H; q.W = cp.W; q.Co = cp.Co; q.kh = cp.kh; q.kw = cp.kw;
+    q.Ho = cp.Ho; q.Wo = cp.Wo; q.stride = cp.stride; q.pad = cp.pad;
+    const int64_t khw = (int64_t)cp.kh * cp.kw;
+    int64_t K;
+    int images = 1;
+    if (kind == cs::kFwd) {
+        q.M = (int64_t)cp.N * cp.Ho * cp.Wo; q.Ncol = cp.Co; K = cp.C * khw;
+        q.out = cp.out;
+        q.so[0] = (int64_t)cp.Co * cp.Ho * cp.Wo; q.so[1] = (int64_t)cp.Ho * cp.Wo; q.so[2] = cp.Wo; q.so[3] = 1;
+    } else if (kind == cs::kDgrad) {
+        q.M = (int64_t)cp.N * cp.H * cp.W; q.Ncol = cp.C; K = cp.Co * khw;
+        q.out = cp.out;
+        q.so[0] = (int64_t)cp.C * cp.H * cp.W; q.so[1] = (int64_t)cp.H * cp.W; q.so[2] = cp.W; q.so[3] = 1;
+    } else {
+        q.M = cp.C * khw; q.Ncol = cp.Co; K = (int64_t)cp.Ho * cp.Wo;
+        q.out = part;
+        images = cp.N;
+    }
+    if (K > INT32_MAX) return fail(MT_EUNSUPPORTED, "%s: reduction too long for the strict kernels", who);
+    q.K = (int)K;
+    const int bn = q.Ncol <= 64 ? 64 : 128;
+    const dim3 grid((unsigned)((q.Ncol + bn - 1) / bn), (unsigned)((q.M + cs::BM - 1) / cs::BM), (unsigned)images);
+    if (grid.y > 65535 || grid.z > 65535) return fail(MT_EUNSUPPORTED, "%s: strict grid too large", who);
+#define MT_CONVS(KIND)                                                                            \
+    if (bn == 64) cs::conv_simt_kernel<KIND, 64><<<grid, cs::THREADS, 0, st>>>(q);               \
+    else cs::conv_simt_kernel<KIND, 128><<<grid, cs::THREADS, 0, st>>>(q);
+    if (kind == cs::kFwd) { MT_CONVS(cs::kFwd) }
+    else if (kind == cs::kDgrad) { MT_CONVS(cs::kDgrad) }
+    else { MT_CONVS(cs::kWgrad) }
+#undef MT_CONVS
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess && e != cudaErrorStreamCaptureUnsupported) return cuda_fail(e, who);
+    g_launches.fetch_add(1);
+    if (kind == cs::kWgrad) {
+        const int64_t total = q.M * q.Ncol;
+        const int blocks = (int)std::min<int64_t>((total + 255) / 256, 1024);
+        cs::wgrad_sum_kernel<<<blocks, 256, 0, st>>>(part, images, (int)q.M, q.Ncol, cp.out);
+        e = cudaGetLastError();
+        if (e != cudaSuccess && e != cudaErrorStreamCaptureUnsupported) return cuda_fail(e, who);
+        g_launches.fetch_add(1);
+    }
+    return MT_OK;
+}
+
+size_t strict_wgrad_bytes(const ConvShape& s) { return (size_t)s.N * s.C * s.kh * s.kw * s.Co * sizeof(float); }
 
 // ---- TMA conv path ----------------------------------------------------------------
 int launch_simple(cudaError_t e, const char* what) {
@@ -1055,6 +1115,10 @@ int conv_fwd(const mt_tensor* x, const mt_tensor* w, const mt_tensor* bias, cons
     DevInfo di = dev_info();
     if (mode == MT_STRICT_FP32 || di.cc != 100) {
         if (mode != MT_STRICT_FP32) return fail(MT_EUNSUPPORTED, "%s: tensor-core conv needs sm_100a", who);
+        if (conv_strict(mt::convs::kFwd, cp, nullptr, st, who) == MT_OK) {
+            t_path = "conv_simt_fwd_fp32";
+            return MT_OK;
+        }
         t_path = "conv_direct_fwd_fp32";
         return direct_launch(mt::conv::direct_fwd_kernel, cp, total, st, who);
     }
@@ -1108,6 +1172,10 @@ int conv_dgrad(const mt_tensor* dy, const mt_tensor* w, const mt_tensor* dx, uin
     DevInfo di = dev_info();
     if (mode == MT_STRICT_FP32 || di.cc != 100) {
         if (mode != MT_STRICT_FP32) return fail(MT_EUNSUPPORTED, "%s: tensor-core conv needs sm_100a", who);
+        if (conv_strict(mt::convs::kDgrad, cp, nullptr, st, who) == MT_OK) {
+            t_path = "conv_simt_dgrad_fp32";
+            return MT_OK;
+        }
         t_path = "conv_direct_dgrad_fp32";
         return direct_launch(mt::conv::direct_dgrad_kernel, cp, total, st, who);
     }
@@ -1267,6 +1335,27 @@ int conv_wgrad(const mt_tensor* dy, const mt_tensor* x, const mt_tensor* dw, uin
     if (mode == MT_STRICT_FP32 || di.cc != 100) {
         if (mode != MT_STRICT_FP32) return fail(MT_EUNSUPPORTED, "%s: tensor-core conv needs sm_100a", who);
         cp.out = dwp;
+        // Per-image partials: in the caller's workspace when it is large enough, else in
+        // scratch when the caller gave none; a workspace too small for them (e.g. the
+        // fixed array of the no-allocation entry point) takes the direct kernel, which
+        // needs none.
+        const size_t need = strict_wgrad_bytes(s);
+        float* part = nullptr;
+        bool owned = false;
+        if (workspace && ws_bytes >= need) {
+            part = static_cast<float*>(workspace);
+        } else if (!workspace) {
+            if ((rc = scratch_alloc(reinterpret_cast<void**>(&part), need, st, "conv strict wgrad partials"))) return rc;
+            owned = true;
+        }
+        if (part) {
+            rc = conv_strict(mt::convs::kWgrad, cp, part, st, who);
+            if (owned) scratch_free(part, need, st);
+            if (rc == MT_OK) {
+                t_path = "conv_simt_wgrad_fp32";
+                return MT_OK;
+            }
+        }
         t_path = "conv_direct_wgrad_fp32";
         return direct_launch(mt::conv::direct_wgrad_kernel, cp, total, st, who);
     }
@@ -1777,7 +1866,8 @@ MT_API size_t mt_conv2d_wgrad_workspace_bytes(const mt_tensor* dy, const mt_tens
     if (!dy || !x || !dw || dy->ndim != 4 || x->ndim != 4 || dw->ndim != 4) return 0;
     ConvShape s;
     if (conv_shape(x, dw, dy, stride, padding, "wgrad_ws", s)) return 0;
-    if (resolve_mode(mode) == MT_STRICT_FP32 || s.N * s.Ho * s.Wo == 0) return 0;
+    if (s.N * s.Ho * s.Wo == 0 || s.Co * s.C * s.kh * s.kw == 0) return 0;
+    if (resolve_mode(mode) == MT_STRICT_FP32) return strict_wgrad_bytes(s);
     const WgradTmaPlan tp = wgrad_tma_plan(s, dy, dev_info().sms, resolve_mode(mode) == MT_TF32X3);
     return tp.ok ? tp.bytes : wgrad_plan(s, dev_info().sms).ws_bytes;
 }

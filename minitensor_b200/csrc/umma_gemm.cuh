@@ -62,12 +62,17 @@ struct Params {
     // A tile cut between clusters: every contributing warp writes its raw partial to
     // sk_ws and counts itself in sk_cnt; the last to arrive sums the partials in k order
     // (a fixed order, so the result does not depend on timing) and runs the epilogue.
-    // sk_dp == num_tiles turns it off.
+    // sk_dp == num_tiles turns it off. With sk_split = S > 1 the whole tiles are themselves
+    // cut into S near-equal k-ranges handed out round-robin as separate units (the same
+    // partial slots and last-arriver sum): a sharded GEMM with few rounds of tiles then
+    // finishes tiles twice as often, so its stores to the peers start earlier.
     long long sk_dp;
     int sk_clusters;            // clusters in the launch
-    int sk_maxseg;              // partial slots per stream-K tile
-    float* sk_ws;               // [tile - sk_dp][sk_maxseg][256 rows][BN] partial sums
-    int* sk_cnt;                // [tile - sk_dp][2 CTAs][4 warps] arrivals, zero at launch
+    int sk_split;               // S: pieces per whole tile (1 = whole tiles)
+    int sk_maxseg;              // partial slots per tile that has slots
+    long long sk_t0;            // first tile with slots (0 when S > 1, else sk_dp)
+    float* sk_ws;               // [tile - sk_t0][sk_maxseg][256 rows][BN] partial sums
+    int* sk_cnt;                // [tile - sk_t0][2 CTAs][4 warps] arrivals, zero at launch
 };
 
 // Tensor maps of the ndst destinations (same view, different base pointers).

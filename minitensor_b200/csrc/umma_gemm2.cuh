@@ -71,15 +71,17 @@ struct Item {
     int kb0, kb1, seg, nseg;
 };
 
-// The work of cluster c of C, in order: whole tiles c, c + C, ... below p.sk_dp, then the
+// The work of cluster c of C, in order: units c, c + C, ... of the sk_dp * S units of the
+// tiles below p.sk_dp (unit u = piece u % S of tile u / S; S = 1: whole tiles), then the
 // cluster's contiguous range [W c / C, W (c+1) / C) of the W = (num_tiles - sk_dp) * kblocks
 // k-blocks of the stream-K tiles, cut at tile boundaries. Every role of the kernel walks
 // the same sequence.
 struct Sched {
-    long long u, x, hi, c, C, W;
-    int kblocks;
+    long long u, x, hi, c, C, W, dp_units;
+    int kblocks, S;
     __device__ Sched(const Params& p, int kblocks_, long long cluster, long long clusters)
-        : u(cluster), c(cluster), C(clusters), kblocks(kblocks_) {
+        : u(cluster), c(cluster), C(clusters), kblocks(kblocks_), S(p.sk_split > 1 ? p.sk_split : 1) {
+        dp_units = p.sk_dp * S;
         W = (p.num_tiles - p.sk_dp) * (long long)kblocks;
         x = W * c / C;
         hi = W * (c + 1) / C;
@@ -87,12 +89,13 @@ struct Sched {
     // The cluster whose range holds stream-K k-block y: the largest c with W c / C <= y.
     __device__ long long owner(long long y) const { return ((y + 1) * C + W - 1) / W - 1; }
     __device__ bool next(const Params& p, Item& it) {
-        if (u < p.sk_dp) {
-            it.tile = u;
-            it.kb0 = 0;
-            it.kb1 = kblocks;
-            it.seg = 0;
-            it.nseg = 1;
+        if (u < dp_units) {
+            it.tile = u / S;
+            const int sp = (int)(u - it.tile * S);
+            it.kb0 = (int)((long long)kblocks * sp / S);
+            it.kb1 = (int)((long long)kblocks * (sp + 1) / S);
+            it.seg = sp;
+            it.nseg = S;
             u += C;
             return true;
         }
@@ -137,10 +140,12 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     const int kblocks = (p.K + G::BKE - 1) / G::BKE;
 
     // The stream-K split is planned on the host for this many clusters and at least one
-    // k-block per cluster; any other launch does no work and says so (both CTAs return
-    // before touching a barrier, so neither waits for the other).
-    if (p.sk_dp < p.num_tiles &&
-        (p.sk_clusters != (int)step || (p.num_tiles - p.sk_dp) * (long long)kblocks < step)) {
+    // k-block per cluster, the split pieces for at least one k-block each; any other launch
+    // does no work and says so (both CTAs return before touching a barrier, so neither
+    // waits for the other).
+    if ((p.sk_dp < p.num_tiles &&
+         (p.sk_clusters != (int)step || (p.num_tiles - p.sk_dp) * (long long)kblocks < step)) ||
+        (p.sk_split > 1 && kblocks < p.sk_split)) {
         if (threadIdx.x == 0) atomicCAS(&g_dev_status, 0, (int)kDevBadLaunch);
         return;
     }
@@ -312,7 +317,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 }
             };
             const bool part = item.nseg > 1;
-            const long long skt = item.tile - p.sk_dp;
+            const long long skt = item.tile - p.sk_t0;
             // This warp's row of the partial slots of a cut tile (slot stride 256 x BN).
             const long long slot_row = ((skt * p.sk_maxseg) * BM + (int)rank * BMC + q * 32 + lane) * (long long)BN;
             const long long slot_stride = (long long)BM * BN;

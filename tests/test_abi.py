@@ -157,7 +157,9 @@ def test_workspace_query_describes_dw_by_shape(mode, x3):
     # A stride or padding that does not produce dy's shape: 0 bytes, not a crash.
     assert engine.conv2d_wgrad_workspace_bytes(_t(N, Co, H, W), _t(N, C, H, W), (Co, C, k, k), 2, 1, mode) == 0
     assert engine.conv2d_wgrad_workspace_bytes(_t(N, Co, H, W), _t(N, C, H, W), (Co, C, k, k), 1, 0, mode) == 0
-    assert engine.conv2d_wgrad_workspace_bytes(_t(N, Co, H, W), _t(N, C, H, W), (Co, C, k, k), 1, 1, "strict") == 0
+    # Strict fp32: one partial sum per image (N x C_in*kh*kw x C_out floats).
+    assert engine.conv2d_wgrad_workspace_bytes(_t(N, Co, H, W), _t(N, C, H, W), (Co, C, k, k), 1, 1,
+                                               "strict") == N * C * k * k * Co * 4
 
 
 def test_bmm_backward_shape_errors():

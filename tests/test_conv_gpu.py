@@ -69,12 +69,13 @@ def test_golden_conv(eng, gold, mode):
         assert np.allclose(db, gold[f"conv{i}_db"], rtol=1e-5, atol=1e-5), f"conv{i} bias grad"
 
 
-@pytest.mark.parametrize("mode", ["tf32", "tf32x3"])
+@pytest.mark.parametrize("mode", MODES)
 def test_config4_resnet_3x3(eng, port, mode):
     x, w, b, dy = inputs.config4()
     xd, wd, dyd = dev(x), dev(w), dev(dy)
     y = host(eng.conv2d(xd, wd, dev(b), 1, 1, mode=mode))
-    assert eng.last_path().startswith("conv_umma_fwd_" + mode), eng.last_path()
+    want = "conv_simt_fwd_fp32" if mode == "strict" else "conv_umma_fwd_" + mode
+    assert eng.last_path().startswith(want), eng.last_path()
     yr = port.conv2d(x, w, b, 1, 1, threads=THREADS)
     check(mode, y, yr, d_fwd(x, w, 1, 1), 576, "config4 fwd")
     _, dw, _ = eng.conv2d_backward(dyd, xd, wd, 1, 1, need=("weight",), mode=mode)
@@ -210,3 +211,21 @@ def test_conv_per_tap_fallback(eng, port, mode):
           "per-tap dgrad")
     check(mode, host(dw), port.conv2d_bwd_weight(dy, x, w.shape, s, p), d_wgrad(dy, x, w.shape, s, p), N * H * W,
           "per-tap shape wgrad")
+
+
+def test_strict_wgrad_paths(eng, port):
+    """Strict weight-grad: per-image partials in scratch, in a caller workspace, and, with a
+    workspace too small for them, the direct kernel -- all within the strict bound."""
+    N, C, H, W, Co, k = 3, 6, 11, 9, 10, 3
+    x = inputs.normal((N, C, H, W), 1.0, 1401)
+    dy = inputs.normal((N, Co, H, W), 1.0, 1402)
+    w = np.zeros((Co, C, k, k), np.float32)
+    ref = port.conv2d_bwd_weight(dy, x, w.shape, 1, 1)
+    D = d_wgrad(dy, x, w.shape, 1, 1)
+    need = eng.conv2d_wgrad_workspace_bytes(dev(dy), dev(x), w.shape, 1, 1, mode="strict")
+    assert need == N * C * k * k * Co * 4
+    for ws, path in ((None, "conv_simt_wgrad_fp32"), (torch.empty(need // 4, device="cuda"), "conv_simt_wgrad_fp32"),
+                     (torch.empty(need // 8, device="cuda"), "conv_direct_wgrad_fp32")):
+        _, dw, _ = eng.conv2d_backward(dev(dy), dev(x), dev(w), 1, 1, need=("weight",), mode="strict", workspace=ws)
+        assert eng.last_path() == path, eng.last_path()
+        check("strict", host(dw), ref, D, N * H * W, path)

@@ -95,7 +95,7 @@ def test_config1_512(eng, port, mode):
     check(mode, C, port.matmul(A, B), absmm(A, B), 512, "config1")
 
 
-@pytest.mark.parametrize("mode", ["tf32", "tf32x3"])
+@pytest.mark.parametrize("mode", MODES)
 def test_config2_linear(eng, port, mode):
     X, W, b, dY = inputs.config2()
     Xd, Wd, bd, dYd = dev(X), dev(W), dev(b), dev(dY)

@@ -13,24 +13,31 @@ import itertools
 import pytest
 
 
-def plan(num_tiles, clusters, kblocks):
-    """(sk_dp, maxseg) as pair_streamk_plan sets them (stream-K on)."""
-    if clusters <= 0 or num_tiles <= clusters:
-        return num_tiles, 0
-    rem = num_tiles % clusters
-    W = rem * kblocks
-    if rem == 0 or W < 8 * clusters:
-        return num_tiles, 0
-    minr = W // clusters
-    return num_tiles - rem, (kblocks + minr - 1) // minr + 1
+def plan(num_tiles, clusters, kblocks, split_dp=False):
+    """(sk_dp, S, slots) as pair_streamk_plan sets them (stream-K on)."""
+    S = 2 if split_dp and kblocks >= 16 else 1
+    units = num_tiles * S
+    sk_dp, maxseg = num_tiles, 0
+    if clusters > 0 and units > clusters:
+        dp = (units // clusters) * clusters // S
+        rem = num_tiles - dp
+        W = rem * kblocks
+        if rem > 0 and W >= 8 * clusters:
+            sk_dp = dp
+            minr = W // clusters
+            maxseg = (kblocks + minr - 1) // minr + 1
+    if S == 1 and sk_dp == num_tiles:
+        return num_tiles, 1, 0          # nothing is cut: no partial slots
+    return sk_dp, S, max(S, maxseg)
 
 
-def items(num_tiles, sk_dp, kblocks, c, C):
+def items(num_tiles, sk_dp, kblocks, c, C, S=1):
     """The Sched sequence of cluster c of C: (tile, kb0, kb1, seg, nseg)."""
     out = []
     u = c
-    while u < sk_dp:
-        out.append((u, 0, kblocks, 0, 1))
+    while u < sk_dp * S:
+        t, sp = divmod(u, S)
+        out.append((t, kblocks * sp // S, kblocks * (sp + 1) // S, sp, S))
         u += C
     W = (num_tiles - sk_dp) * kblocks
     if W == 0:
@@ -51,12 +58,12 @@ def items(num_tiles, sk_dp, kblocks, c, C):
     return out
 
 
-def check_schedule(num_tiles, C, kblocks):
-    sk_dp, maxseg = plan(num_tiles, C, kblocks)
+def check_schedule(num_tiles, C, kblocks, split_dp=False):
+    sk_dp, S, slots = plan(num_tiles, C, kblocks, split_dp)
     covered = {}
     pieces = {}
     for c in range(C):
-        for tile, kb0, kb1, seg, nseg in items(num_tiles, sk_dp, kblocks, c, C):
+        for tile, kb0, kb1, seg, nseg in items(num_tiles, sk_dp, kblocks, c, C, S):
             assert 0 <= kb0 < kb1 <= kblocks
             for kb in range(kb0, kb1):
                 assert (tile, kb) not in covered, (tile, kb)
@@ -69,30 +76,37 @@ def check_schedule(num_tiles, C, kblocks):
         assert len(nsegs) == 1 and nsegs.pop() == len(ps), (tile, ps)
         assert [p[2] for p in ps] == list(range(len(ps))), (tile, ps)   # seg in k order
         if len(ps) > 1:
-            assert tile >= sk_dp and len(ps) <= maxseg, (tile, len(ps), maxseg)
-            clusters = [p[4] for p in ps]
-            assert clusters == list(range(clusters[0], clusters[0] + len(ps)))   # consecutive clusters
-    return sk_dp, maxseg
+            assert len(ps) <= slots, (tile, len(ps), slots)
+            if tile >= sk_dp:
+                clusters = [p[4] for p in ps]
+                assert clusters == list(range(clusters[0], clusters[0] + len(ps)))   # consecutive clusters
+            else:
+                assert S > 1 and len(ps) == S
+    return sk_dp, S, slots
 
 
 def test_config5_shards():
-    # 8192^3 over 1, 2, 4, 8 GPUs with 74 clusters: 256 x 256 tiles (K = 8192 -> 256 k-blocks),
-    # and 256 x 128 tiles for the 8-GPU shard.
+    # 8192^3 over 1, 2, 4, 8 GPUs with 74 clusters: 256 x 256 tiles, K = 8192 -> 256 k-blocks.
     for tiles in (1024, 512, 256, 128):
-        sk_dp, maxseg = check_schedule(tiles, 74, 256)
-        assert sk_dp == tiles - tiles % 74 and maxseg >= 2
-    sk_dp, maxseg = check_schedule(256, 74, 256)
-    assert (sk_dp, maxseg) == (222, 4)
+        sk_dp, S, slots = check_schedule(tiles, 74, 256)
+        assert S == 1 and sk_dp == tiles - tiles % 74 and slots >= 2
+    assert plan(256, 74, 256) == (222, 1, 4)
+    # The 8-GPU shard with peers: whole tiles in two halves, 3 rounds of halves, then stream-K.
+    sk_dp, S, slots = check_schedule(128, 74, 256, split_dp=True)
+    assert (sk_dp, S) == (111, 2) and slots >= 2
 
 
 def test_off_when_ranges_would_be_short_or_rounds_are_whole():
-    assert plan(148, 74, 256) == (148, 0)          # whole rounds
-    assert plan(90, 74, 5) == (90, 0)              # 16 x 5 k-blocks < 8 per cluster
-    assert plan(60, 74, 256) == (60, 0)            # fewer tiles than clusters: not a pair launch
+    assert plan(148, 74, 256) == (148, 1, 0)       # whole rounds
+    assert plan(90, 74, 5) == (90, 1, 0)           # 16 x 5 k-blocks < 8 per cluster
+    assert plan(60, 74, 256) == (60, 1, 0)         # fewer tiles than clusters: not a pair launch
+    assert plan(128, 74, 8, split_dp=True)[1] == 1   # halves need 8 k-blocks each
     check_schedule(90, 74, 5)
 
 
 @pytest.mark.parametrize("C", [1, 2, 3, 7, 37, 74])
-def test_many_shapes(C):
-    for tiles, kblocks in itertools.product([C + 1, 2 * C - 1, 3 * C + 2, 5 * C + C // 2 + 1], [1, 2, 7, 8, 9, 31, 64, 256]):
-        check_schedule(tiles, C, kblocks)
+@pytest.mark.parametrize("split_dp", [False, True])
+def test_many_shapes(C, split_dp):
+    for tiles, kblocks in itertools.product([C + 1, 2 * C - 1, 3 * C + 2, 5 * C + C // 2 + 1],
+                                            [1, 2, 7, 8, 9, 16, 31, 64, 256]):
+        check_schedule(tiles, C, kblocks, split_dp)
