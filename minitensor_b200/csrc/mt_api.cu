@@ -288,7 +288,7 @@ bool streamk_enabled() {
     return v != 0;
 }
 
-int pair_streamk_plan(mt::umma::Params& up, int clusters, int kblocks, int bn, bool split_dp, cudaStream_t st,
+int pair_streamk_plan(mt::umma::Params& up, int clusters, int kblocks, int bn, bool split_dp, bool x3, cudaStream_t st,
                       void** ws_out, size_t* ws_bytes_out) {
     *ws_out = nullptr;
     *ws_bytes_out = 0;
@@ -306,7 +306,15 @@ int pair_streamk_plan(mt::umma::Params& up, int clusters, int kblocks, int bn, b
     const long long units = up.num_tiles * S;
     long long sk_dp = up.num_tiles;
     int maxseg = 0;
-    if (units > clusters) {
+    // The remainder goes to stream-K only where that measured faster: 3xTF32 with more than
+    // 5% of the last round idle (e.g. 3.46 rounds: +12% on the 8192 x 2048 x 8192 shard). In
+    // TF32 the remainder's k-ranges, run at different k at once, share less of A and B in L2
+    // (+24% DRAM bytes, tensor pipe 86% -> 78% active on that shape), which costs more than
+    // the idle part of the last round; with 13.8 rounds (8192^3 on one GPU) the last round
+    // is 1% of the work.
+    const long long rounds_up = (units + clusters - 1) / clusters;
+    const bool worth_it = x3 && (double)(rounds_up * clusters - units) / (double)units > 0.05;
+    if (units > clusters && worth_it) {
         const long long dp = (units / clusters) * clusters / S;   // whole tiles in whole rounds
         const long long rem = up.num_tiles - dp;
         const long long W = rem * (long long)kblocks;
@@ -341,6 +349,9 @@ int pair_streamk_plan(mt::umma::Params& up, int clusters, int kblocks, int bn, b
     *ws_bytes_out = ws_bytes + cnt_bytes;
     return MT_OK;
 }
+
+// The pair kernel's schedule for mt_last_path: " split=S" and/or " streamk=<tiles>".
+thread_local std::string t_sched;
 
 // CTA-pair kernel: grid = 2 x (clusters that fit at once, capped by the tile count), with
 // the stream-K remainder planned for exactly that many clusters.
@@ -380,8 +391,11 @@ int launch_pair_inst(const CUtensorMap& ta, const CUtensorMap& tb, const mt::umm
     // A GEMM that stores into peers (ndst > 1) with fewer than two rounds of tiles splits
     // its whole tiles in two, so that finished tiles (and their stores) come twice as often.
     const bool split_dp = up.ndst > 1 && up.num_tiles < 2LL * clusters;
-    int rc = pair_streamk_plan(up, clusters, (up.K + BKE - 1) / BKE, BN, split_dp, st, &ws, &ws_bytes);
+    int rc = pair_streamk_plan(up, clusters, (up.K + BKE - 1) / BKE, BN, split_dp, X3, st, &ws, &ws_bytes);
     if (rc) return rc;
+    t_sched.clear();
+    if (up.sk_split > 1) t_sched += " split=" + std::to_string(up.sk_split);
+    if (up.sk_dp < up.num_tiles) t_sched += " streamk=" + std::to_string(up.num_tiles - up.sk_dp);
     kern<<<2 * clusters, G::THREADS, G::SMEM_BYTES, st>>>(ta, tb, dm, up);
     cudaError_t e = cudaGetLastError();
     scratch_free(ws, ws_bytes, st);
@@ -576,6 +590,7 @@ int launch_umma(const GemmProblem& p, bool x3, cudaStream_t st, float* const* ex
                  a_mn ? "MN" : "K", b_mn ? "MN" : "K",
                  splits > 1 ? (" splitk=" + std::to_string(splits)).c_str() : "");
         t_path = buf;
+        if (pair) t_path += t_sched;
     }
     return rc;
 }

@@ -364,3 +364,28 @@ def test_one_cta_wide_tiles_batched_short_rows(eng, port, mode):
     path = eng.last_path()
     assert path.startswith(f"umma_{mode} bn=256"), path
     check(mode, host(C), port.bmm(A, B), absmm(A, B), K, "one-CTA bn=256 batched")
+
+
+@pytest.mark.parametrize("mode", ["tf32x3", "tf32"])
+def test_pair_kernel_streamk_remainder(eng, port, mode):
+    """256 tiles of 256 x 256 over 74 clusters (3.46 rounds): in 3xTF32 the last 34 tiles
+    are cut into equal k-ranges across all clusters (stream-K) and summed by the last of
+    each tile's contributors; in TF32 they run whole. Full rows of the stream-K tiles
+    (rows 6144..8191 hold them) and of whole tiles are checked."""
+    M, K, N = 8192, 2048, 2048
+    A = inputs.uniform((M, K), -1, 1, 301)
+    B = inputs.uniform((K, N), -1, 1, 302)
+    C = torch.full((M, N), float("nan"), device="cuda")
+    eng.gemm(dev(A), dev(B), C, mode=mode)
+    path = eng.last_path()
+    assert path.startswith("umma_pair_" + mode), path
+    assert ("streamk=34" in path) == (mode == "tf32x3"), path
+    rows = [0, 255, 256, 4095, 6144, 6400, 6655, 7000, 7936, 8191]
+    c = host(C)[rows]
+    check(mode, c, port.matmul_strided(A[rows], B), absmm(A[rows], B), K, f"stream-K ({path})")
+    # Run again: the arrival counters start from zero on every call and the result is
+    # bit-identical (the pieces of a tile are summed in k order whoever arrives last).
+    C2 = torch.full((M, N), float("nan"), device="cuda")
+    eng.gemm(dev(A), dev(B), C2, mode=mode)
+    assert torch.equal(C, C2)
+    assert eng.device_status(reset=True) == 0

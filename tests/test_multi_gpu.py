@@ -63,6 +63,28 @@ def test_multi_destination_epilogue_pair_kernel(eng, port, mode):
         assert np.array_equal(host(e), c)
 
 
+@pytest.mark.parametrize("mode", ["tf32x3", "tf32"])
+def test_multi_destination_split_units(eng, port, mode):
+    """A multi-destination GEMM with fewer than two rounds of pair tiles (96 tiles over 74
+    clusters, as one rank's shard at 8 GPUs): whole tiles are cut into two k-halves handed
+    out as separate units (split=2), and in 3xTF32 the remainder runs stream-K; every
+    destination gets the same, correct C."""
+    M, K, N = 4096, 1024, 1536
+    A = inputs.uniform((M, K), -1, 1, 311)
+    B = inputs.uniform((K, N), -1, 1, 312)
+    C = torch.full((M, N), float("nan"), device="cuda")
+    extras = [torch.full((M, N), -7.0, device="cuda") for _ in range(3)]
+    _multi(dev(A), dev(B), C, extras, mode)
+    path = eng.last_path()
+    assert "split=2" in path and ("streamk=" in path) == (mode == "tf32x3"), path
+    c = host(C)
+    rows = [0, 255, 256, 2047, 2048, 3071, 3072, 3583, 3584, M - 1]
+    check(mode, c[rows], port.matmul_strided(A[rows], B), absmm(A[rows], B), K, f"split units ({path})")
+    for e in extras:
+        assert np.array_equal(host(e), c)
+    assert eng.device_status(reset=True) == 0
+
+
 def test_multi_destination_ragged_columns_clipped(eng, port):
     """N = 2340 (not a multiple of 32): the last column block of each tile is partial and
     the TMA stores must clip it; every destination is a window of a wider buffer whose

@@ -13,12 +13,16 @@ import itertools
 import pytest
 
 
-def plan(num_tiles, clusters, kblocks, split_dp=False):
-    """(sk_dp, S, slots) as pair_streamk_plan sets them (stream-K on)."""
+def plan(num_tiles, clusters, kblocks, split_dp=False, gate=False):
+    """(sk_dp, S, slots) as pair_streamk_plan sets them. gate=False: the stream-K remainder
+    whenever it fits (the schedule properties are tested on every shape); gate=True: only
+    where the host enables it (3xTF32 with more than 5% of the last round idle)."""
     S = 2 if split_dp and kblocks >= 16 else 1
     units = num_tiles * S
     sk_dp, maxseg = num_tiles, 0
-    if clusters > 0 and units > clusters:
+    rounds_up = (units + clusters - 1) // clusters if clusters > 0 else 0
+    worth_it = (rounds_up * clusters - units) / units > 0.05 if units else False
+    if clusters > 0 and units > clusters and (worth_it or not gate):
         dp = (units // clusters) * clusters // S
         rem = num_tiles - dp
         W = rem * kblocks
@@ -91,6 +95,10 @@ def test_config5_shards():
         sk_dp, S, slots = check_schedule(tiles, 74, 256)
         assert S == 1 and sk_dp == tiles - tiles % 74 and slots >= 2
     assert plan(256, 74, 256) == (222, 1, 4)
+    # Where the host turns it on: the 4- and 8-GPU shards (3.46 / 1.73 rounds), not one GPU's
+    # 13.8 rounds or two GPUs' 6.9.
+    assert plan(1024, 74, 256, gate=True)[0] == 1024 and plan(512, 74, 256, gate=True)[0] == 512
+    assert plan(256, 74, 256, gate=True)[0] == 222 and plan(128, 74, 256, split_dp=True, gate=True)[0] == 111
     # The 8-GPU shard with peers: whole tiles in two halves, 3 rounds of halves, then stream-K.
     sk_dp, S, slots = check_schedule(128, 74, 256, split_dp=True)
     assert (sk_dp, S) == (111, 2) and slots >= 2
