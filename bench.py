@@ -44,6 +44,9 @@ def parse():
     ap.add_argument("--no-extras", action="store_true", help="skip the other modes, e2e and CPU legs")
     ap.add_argument("--size", type=int, default=8192,
                     help="c5 square size; 8192 is the benchmark, smaller sizes are profiling cases")
+    ap.add_argument("--cols", type=int, default=0,
+                    help="c5 profiling case on one GPU: only the first COLS columns of C (one rank's "
+                         "column shard, e.g. 2048 = the 4-GPU shard); not the benchmark")
     ap.add_argument("--gather", default="auto", choices=["auto", "epilogue", "copy"],
                     help="N>1: how shards reach the peers (auto = epilogue: TMA stores from the GEMM epilogue)")
     return ap.parse_args()
@@ -228,15 +231,21 @@ class Workload:
 class C5(Workload):
     name = "c5"
 
-    def __init__(self, gpu=True, n=8192, rank=0, world=1, gather="auto"):
+    def __init__(self, gpu=True, n=8192, rank=0, world=1, gather="auto", cols=0):
         from minitensor_b200 import inputs
         self.n, self.rank, self.world = n, rank, world
         self.gather = None if gather == "auto" else gather
-        self.desc = (f"config5: C[{n},{n}] = A[{n},{n}] . B[{n},{n}], A,B ~ U[-1,1] seed 1" if n == 8192
-                     else f"profiling case: config5 generator at {n}^3 (not the benchmark shape)")
-        self.flops = 2.0 * n ** 3
-        self.bytes = 3.0 * n * n * 4
+        self.desc = (f"config5: C[{n},{n}] = A[{n},{n}] . B[{n},{n}], A,B ~ U[-1,1] seed 1" if n == 8192 and not cols
+                     else f"profiling case: config5 generator at {n}^3" + (f", first {cols} columns of C" if cols else "")
+                     + " (not the benchmark shape)")
         self.A_h, self.B_h = inputs.config5(n)
+        if cols:
+            if world > 1:
+                raise SystemExit("--cols is a one-GPU profiling case")
+            self.B_h = np.ascontiguousarray(self.B_h[:, :cols])
+        nc = cols or n
+        self.flops = 2.0 * n * n * nc
+        self.bytes = 4.0 * (n * n + 2 * n * nc)
         super().__init__(gpu)
 
     def to_gpu(self):
@@ -245,7 +254,7 @@ class C5(Workload):
         self.engine = engine
         n = self.n
         self.A = _cuda(self.A_h)
-        self.C = torch.empty(n, n, device="cuda")
+        self.C = torch.empty(n, self.B_h.shape[1], device="cuda")
         if self.world == 1:
             Bsrc = self.B_h
         else:
@@ -254,7 +263,7 @@ class C5(Workload):
             Bsrc = np.ascontiguousarray(self.B_h[:, self.plan.n0:self.plan.n1])
         self.B = _cuda(Bsrc)
         self.h2d = [(_pin(self.A_h), self.A), (_pin(Bsrc), self.B)]
-        self.d2h = [(self.C, torch.empty(n, n).pin_memory())]
+        self.d2h = [(self.C, torch.empty(n, self.C.shape[1]).pin_memory())]
 
     def step(self, mode):
         if self.world == 1:
@@ -270,8 +279,9 @@ class C5(Workload):
         impl, kind = _ref()
         rows = threads
         _, dt = impl.matmul_rows(self.A_h, self.B_h, 0, rows, threads, timing=True)
-        return (2.0 * rows * self.n * self.n / dt / 1e12, dt, kind,
-                f"C rows 0..{rows - 1} of config5 ({rows} x {self.n} x {self.n}), {threads} threads")
+        nc = self.B_h.shape[1]
+        return (2.0 * rows * self.n * nc / dt / 1e12, dt, kind,
+                f"C rows 0..{rows - 1} of config5 ({rows} x {self.n} x {nc}), {threads} threads")
 
     def parity(self, mode, threads, C=None):
         import oracle
@@ -289,6 +299,8 @@ class C5(Workload):
     def ref_gpu(self, R, warmup, iters):
         import oracle
         n = self.n
+        if self.B_h.shape[1] != n:
+            return {"unavailable": "column-shard profiling case"}
         C = np.empty((n, n), np.float32)
         ms = R.call("ref_gpu_matmul", _fp(self.A_h), _fp(self.B_h), _fp(C), n, n, n, warmup, iters)
         rows = [0, n // 2, n - 1]
@@ -573,7 +585,7 @@ class C4(Workload):
 
 def make_workload(args, rank, world, gpu=True):
     if args.workload == "c5":
-        return C5(gpu, args.size, rank, world, getattr(args, "gather", "auto"))
+        return C5(gpu, args.size, rank, world, getattr(args, "gather", "auto"), getattr(args, "cols", 0))
     if args.workload == "c3":
         return C3(gpu, rank, world)
     if world > 1 and gpu:
@@ -761,7 +773,7 @@ def run_gpu(args, rank, world, local_rank):
         # C out; A streamed in row panels, each C panel returned while later ones compute).
         # It becomes `e2e`; the serial copy-compute-copy step above stays as `e2e_serial`.
         # Its C is checked against the oracle on the same rows as the device step.
-        if world == 1 and wl.name == "c5":
+        if world == 1 and wl.name == "c5" and wl.B_h.shape[1] == wl.n:
             try:
                 n = wl.n
                 A_pin, B_pin = wl.h2d[0][0], wl.h2d[1][0]

@@ -157,7 +157,7 @@ __device__ __forceinline__ void load_b(const Params& p, int img, int64_t n0, int
 }
 
 template <int KIND, int BN>
-__global__ void __launch_bounds__(THREADS) conv_simt_kernel(Params p) {
+__global__ void __launch_bounds__(THREADS, 2) conv_simt_kernel(Params p) {
     constexpr int NB = BN / 32, GROUPS = BK / NB, TN = BN / 16;   // TN outputs per thread along n
     __shared__ __align__(16) float As[2][BK][BM];
     __shared__ __align__(16) float Bs[2][BK][BN];

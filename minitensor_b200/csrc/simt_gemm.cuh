@@ -128,7 +128,7 @@ __device__ __forceinline__ float epilogue(float acc, const GemmProblem& p, int64
 }
 
 template <int LA, int LB>
-__global__ void __launch_bounds__(THREADS) gemm_kernel(GemmProblem p) {
+__global__ void __launch_bounds__(THREADS, 2) gemm_kernel(GemmProblem p) {
     __shared__ __align__(16) float As[2][BK][BM];
     __shared__ __align__(16) float Bs[2][BK][BN];
 
