@@ -245,8 +245,9 @@ MT_API int mt_copy_rows_async(void* dst, uint64_t dpitch, const void* src, uint6
  * the stride-1 conv's NHWC copy and reordered weights, weight-grad partials). The
  * reference takes scratch from its MemoryPool (include/MemoryPool.hpp:45-99); its drop-in
  * overlay installs the pool here. With no allocator installed (the default, or after
- * passing NULL, NULL) every buffer is a stream-ordered cudaMallocAsync / cudaFreeAsync on
- * the call's stream. With one installed, alloc(bytes, device, ctx) is called before the
+ * passing NULL, NULL) every buffer is a stream-ordered allocation on the call's stream from
+ * the library's own per-device pool (cudaMallocFromPoolAsync / cudaFreeAsync; the pool
+ * keeps freed memory cached for the next call). With one installed, alloc(bytes, device, ctx) is called before the
  * kernels are enqueued and free(ptr, bytes, device, ctx) right after: the block may be
  * handed out again while those kernels still run, so work sharing the allocator must be
  * ordered on one stream (the reference's active_stream()). A NULL from alloc fails the
