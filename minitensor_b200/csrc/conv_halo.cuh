@@ -34,7 +34,7 @@
 namespace mt {
 namespace convh {
 
-constexpr int kMaxASlots = 2;
+constexpr int kMaxASlots = 4;
 constexpr int kMaxBStages = 8;
 
 struct HaloParams {

@@ -996,30 +996,55 @@ bool halo_enabled() {
 // stages fit beside two halo slots.
 bool plan_halo(int Ho, int Wo, int Cin, int kh, int kw, int Ncol, bool x3, int& bn, mt::convh::HaloParams& hp,
                uint32_t& smem) {
-    const int TXv = std::min(Wo, 128 - (kw - 1));
-    if (TXv < 1 || kh < 1 || kw < 1) return false;
-    const int P = TXv + kw - 1;                          // <= 128
-    const int TY = std::min(Ho, (128 - TXv) / P + 1);
-    const int HR = TY + kh - 1;
-    if (HR > 256) return false;
-    const int64_t rows = std::max<int64_t>((int64_t)P * HR, (int64_t)(kh - 1) * P + (kw - 1) + 128);
-    const int64_t nr = (rows + 7) / 8 * 8;
+    if (kh < 1 || kw < 1 || Wo < 1 || Ho < 1) return false;
+    // Tile shape: TY rows of TXv output columns, pitched P = TXv + kw - 1, TY * P <= 128 MMA
+    // rows. Fewest tiles first (every tile costs the same MMA work), then the smallest halo
+    // (less L2 -> shared traffic, and room for a deeper halo ring). E.g. c4's 56 x 56: 8 x 14
+    // tiles (21 KB halos) rather than 2 x 56 (31.7 KB), both 896 tiles of 112 valid rows.
+    int TXv = 0, P = 0, TY = 0, HR = 0;
+    int64_t nr = 0, best_tiles = -1;
+    for (int tx = std::min(Wo, 128 - (kw - 1)); tx >= 1; --tx) {
+        const int p = tx + kw - 1;
+        const int ty = std::min(Ho, (128 - tx) / p + 1);
+        const int hr = ty + kh - 1;
+        if (hr > 256) continue;
+        const int64_t rows = std::max<int64_t>((int64_t)p * hr, (int64_t)(kh - 1) * p + (kw - 1) + 128);
+        const int64_t r8 = (rows + 7) / 8 * 8;
+        const int64_t tiles = (int64_t)((Ho + ty - 1) / ty) * ((Wo + tx - 1) / tx);
+        if (best_tiles < 0 || tiles < best_tiles || (tiles == best_tiles && r8 < nr)) {
+            best_tiles = tiles; TXv = tx; P = p; TY = ty; HR = hr; nr = r8;
+        }
+    }
+    if (best_tiles < 0) return false;
     const uint64_t mult = x3 ? 2 : 1;
     bn = std::min(pick_bn(Ncol), 128);
     const int taps = kh * kw;
     const uint64_t slot = (uint64_t)nr * 128, bmat = (uint64_t)bn * 128;
     const uint32_t bars = 8u * (3 * mt::convh::kMaxASlots + 2 * mt::convh::kMaxBStages + 4) + 16u;
     const uint64_t budget = kHaloSmemMax - 1024 - bars;
-    const int a_slots = mt::convh::kMaxASlots;
-    const uint64_t a_total = a_slots * slot * mult;
-    int G = 0;
-    for (int g = std::min(taps, 256); g >= 1; --g)
-        if (taps % g == 0 && a_total + 2 * (uint64_t)g * mult * bmat <= budget) { G = g; break; }
+    const int cblocks = (Cin + 31) / 32;
+    // Halo slots: 2, or more (up to kMaxASlots) while the weights can stay resident -- a
+    // deeper ring hides the TMA latency of the next channel block's halo behind more MMAs.
+    int a_slots = 2, G = 0, b_stages = 0;
+    uint64_t a_total = 0, bstage = 0;
+    for (int want = mt::convh::kMaxASlots; want >= 2; --want) {
+        const uint64_t at = want * slot * mult;
+        int g0 = 0;
+        for (int g = std::min(taps, 256); g >= 1; --g)
+            if (taps % g == 0 && at + 2 * (uint64_t)g * mult * bmat <= budget) { g0 = g; break; }
+        if (g0 == 0) continue;
+        const uint64_t bs = (uint64_t)g0 * mult * bmat;
+        const int nb = (int)std::min<uint64_t>(mt::convh::kMaxBStages, (budget - at) / bs);
+        const int all = cblocks * (taps / g0);
+        const bool resident = Ncol <= bn && all <= mt::convh::kMaxBStages && all <= nb;
+        if (resident || want == 2) {
+            a_slots = want; G = g0; b_stages = nb; a_total = at; bstage = bs;
+            break;
+        }
+    }
     if (G == 0) return false;
-    const uint64_t bstage = (uint64_t)G * mult * bmat;
-    int b_stages = (int)std::min<uint64_t>(mt::convh::kMaxBStages, (budget - a_total) / bstage);
     // Resident weights: one N tile, and every (channel block, tap group) stage fits.
-    const int cblocks = (Cin + 31) / 32, all_stages = cblocks * (taps / G);
+    const int all_stages = cblocks * (taps / G);
     hp.b_resident = (Ncol <= bn && all_stages <= mt::convh::kMaxBStages && all_stages <= b_stages) ? 1 : 0;
     if (hp.b_resident) b_stages = all_stages;
     hp.P = P; hp.TXv = TXv; hp.TY = TY; hp.HR = HR;
