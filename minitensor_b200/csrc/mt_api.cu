@@ -997,10 +997,17 @@ bool halo_enabled() {
 bool plan_halo(int Ho, int Wo, int Cin, int kh, int kw, int Ncol, bool x3, int& bn, mt::convh::HaloParams& hp,
                uint32_t& smem) {
     if (kh < 1 || kw < 1 || Wo < 1 || Ho < 1) return false;
+    const uint64_t mult = x3 ? 2 : 1;
+    bn = std::min(pick_bn(Ncol), 128);
+    const int taps = kh * kw;
+    const uint64_t bmat = (uint64_t)bn * 128;
+    const uint32_t bars = 8u * (3 * mt::convh::kMaxASlots + 2 * mt::convh::kMaxBStages + 4) + 16u;
+    const uint64_t budget = kHaloSmemMax - 1024 - bars;
     // Tile shape: TY rows of TXv output columns, pitched P = TXv + kw - 1, TY * P <= 128 MMA
-    // rows. Fewest tiles first (every tile costs the same MMA work), then the smallest halo
-    // (less L2 -> shared traffic, and room for a deeper halo ring). E.g. c4's 56 x 56: 8 x 14
-    // tiles (21 KB halos) rather than 2 x 56 (31.7 KB), both 896 tiles of 112 valid rows.
+    // rows, among the shapes whose two halo slots and two one-tap weight stages fit. Fewest
+    // tiles first (every tile costs the same MMA work), then the smallest halo (less L2 ->
+    // shared traffic, and room for a deeper halo ring). E.g. c4's 56 x 56: 8 x 14 tiles
+    // (21 KB halos) rather than 2 x 56 (31.7 KB), both 896 tiles of 112 valid rows.
     int TXv = 0, P = 0, TY = 0, HR = 0;
     int64_t nr = 0, best_tiles = -1;
     for (int tx = std::min(Wo, 128 - (kw - 1)); tx >= 1; --tx) {
@@ -1010,18 +1017,14 @@ bool plan_halo(int Ho, int Wo, int Cin, int kh, int kw, int Ncol, bool x3, int& 
         if (hr > 256) continue;
         const int64_t rows = std::max<int64_t>((int64_t)p * hr, (int64_t)(kh - 1) * p + (kw - 1) + 128);
         const int64_t r8 = (rows + 7) / 8 * 8;
+        if (2 * (uint64_t)r8 * 128 * mult + 2 * mult * bmat > budget) continue;
         const int64_t tiles = (int64_t)((Ho + ty - 1) / ty) * ((Wo + tx - 1) / tx);
         if (best_tiles < 0 || tiles < best_tiles || (tiles == best_tiles && r8 < nr)) {
             best_tiles = tiles; TXv = tx; P = p; TY = ty; HR = hr; nr = r8;
         }
     }
     if (best_tiles < 0) return false;
-    const uint64_t mult = x3 ? 2 : 1;
-    bn = std::min(pick_bn(Ncol), 128);
-    const int taps = kh * kw;
-    const uint64_t slot = (uint64_t)nr * 128, bmat = (uint64_t)bn * 128;
-    const uint32_t bars = 8u * (3 * mt::convh::kMaxASlots + 2 * mt::convh::kMaxBStages + 4) + 16u;
-    const uint64_t budget = kHaloSmemMax - 1024 - bars;
+    const uint64_t slot = (uint64_t)nr * 128;
     const int cblocks = (Cin + 31) / 32;
     // Halo slots: 2, or more (up to kMaxASlots) while the weights can stay resident -- a
     // deeper ring hides the TMA latency of the next channel block's halo behind more MMAs.
