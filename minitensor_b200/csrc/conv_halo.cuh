@@ -209,28 +209,31 @@ conv_fwd_halo_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                     tc_fence_after();
                     const uint32_t a_base = smem_u32(a_ring + as * p.slot_bytes);
                     const uint32_t alo_base = smem_u32(alo_ring + as * p.slot_bytes);
+                    // Descriptors at offset 0 of this halo slot; the start address moved by
+                    // `off` bytes is the same descriptor plus off >> 4: the 14-bit field holds
+                    // addr >> 4 of a shared address below 256 KB, so the sum never carries
+                    // out. With N = 64 an MMA takes 48 cycles, less than recomputing two
+                    // descriptors and a tap division on the one issuing thread took.
+                    const uint64_t a0 = halo_desc(a_base), alo0 = halo_desc(alo_base);
+                    int tr = 0, ts = 0;   // (r, s) of the next tap, advanced without division
                     for (int g = 0; g < p.tgroups; ++g) {
                         if (p.b_resident) bs = cb * p.tgroups + g;
                         if ((!p.b_resident || it == 0) &&
                             !mbar_wait(smem_u32(&b_full[bs]), p.b_resident ? 0u : bph, abort_flag, kDevTimeoutFull))
                             goto done;
                         tc_fence_after();
-                        const uint32_t sbase = smem_u32(b_ring + bs * p.b_bytes);
+                        const uint64_t b0 = umma_desc(smem_u32(b_ring + bs * p.b_bytes), 16, 1024, kLayoutSw128);
                         for (int gi = 0; gi < p.G; ++gi) {
-                            const int tap = g * p.G + gi;
-                            const int r = tap / p.kw, sx = tap - r * p.kw;
-                            const uint32_t o = (uint32_t)(r * p.P + sx) * 128u;
-                            const uint32_t sb = sbase + (X3 ? 2u * gi : (uint32_t)gi) * BMAT;
+                            const uint64_t ao = (uint64_t)(((uint32_t)(tr * p.P + ts) * 128u) >> 4);
+                            const uint64_t bo = (uint64_t)(((X3 ? 2u * gi : (uint32_t)gi) * BMAT) >> 4);
+                            if (++ts == p.kw) { ts = 0; ++tr; }
 #pragma unroll
                             for (int k = 0; k < 4; ++k) {
-                                const uint64_t ad = halo_desc(a_base + o + k * 32);
-                                const uint64_t bd = umma_desc(sb + k * 32, 16, 1024, kLayoutSw128);
+                                const uint64_t ad = a0 + ao + 2 * k, bd = b0 + bo + 2 * k;   // + 32 B per k-step
                                 const uint32_t acc = (!first_mma || k > 0) ? 1u : 0u;
                                 if (X3) {
-                                    const uint64_t ald = halo_desc(alo_base + o + k * 32);
-                                    const uint64_t bld = umma_desc(sb + BMAT + k * 32, 16, 1024, kLayoutSw128);
-                                    umma_tf32(d_tmem, ald, bd, idesc, acc);
-                                    umma_tf32(d_tmem, ad, bld, idesc, 1u);
+                                    umma_tf32(d_tmem, alo0 + ao + 2 * k, bd, idesc, acc);
+                                    umma_tf32(d_tmem, ad, bd + (BMAT >> 4), idesc, 1u);
                                     umma_tf32(d_tmem, ad, bd, idesc, 1u);
                                 } else {
                                     umma_tf32(d_tmem, ad, bd, idesc, acc);
@@ -276,13 +279,31 @@ conv_fwd_halo_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                     if (lane == 0) mbar_arrive(smem_u32(&acc_empty[acc_i]));
                 }
                 if (valid) {
+                    // The chunk's 32 biases are loaded once (vector loads when aligned), and
+                    // the output pointer steps one channel plane per element: a bias load, an
+                    // add and a 64-bit multiply per element made this epilogue cost more than
+                    // the MMAs of its tile.
+                    const int co0 = nt * BN + c * 32;
+                    float bv[32];
+                    if (p.bias && co0 + 32 <= p.Ncol && ((reinterpret_cast<uintptr_t>(p.bias + co0) & 15) == 0)) {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int co = nt * BN + c * 32 + j;
-                        if (co < p.Ncol) {
-                            float v = __uint_as_float(rr[j]);
-                            if (p.bias) v = v + __ldg(p.bias + co);
-                            obase[(int64_t)co * HoWo] = v;
+                        for (int j = 0; j < 8; ++j) {
+                            const float4 t = __ldg(reinterpret_cast<const float4*>(p.bias + co0) + j);
+                            bv[4 * j] = t.x; bv[4 * j + 1] = t.y; bv[4 * j + 2] = t.z; bv[4 * j + 3] = t.w;
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) bv[j] = (p.bias && co0 + j < p.Ncol) ? __ldg(p.bias + co0 + j) : 0.f;
+                    }
+                    float* o = obase + (int64_t)co0 * HoWo;
+                    if (co0 + 32 <= p.Ncol) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) { *o = __uint_as_float(rr[j]) + bv[j]; o += HoWo; }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            if (co0 + j < p.Ncol) *o = __uint_as_float(rr[j]) + bv[j];
+                            o += HoWo;
                         }
                     }
                 }

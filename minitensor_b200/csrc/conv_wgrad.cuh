@@ -151,6 +151,14 @@ conv_wgrad_wide_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_con
                     tc_fence_after();
                     const uint32_t sa = smem_u32(ring + s * G::STAGE_BYTES), sb = sa + G::A_BYTES;
                     const uint32_t la = smem_u32(ring_lo + s * G::STAGE_BYTES), lb = la + G::A_BYTES;
+                    // Descriptors at the stage's base; a start moved by `off` bytes is the same
+                    // descriptor plus off >> 4 (the address field is addr >> 4, no carry below
+                    // 256 KB), so each MMA adds a constant instead of re-encoding: at N = 64 an
+                    // MMA is only 48 cycles of work for the one issuing thread to keep up with.
+                    const uint64_t a0 = umma_desc(sa, G::CHUNK_BYTES, 512, kLayoutSw128Base32);
+                    const uint64_t b0 = umma_desc(sb, 16, 1024, kLayoutSw128);
+                    const uint64_t alo0 = umma_desc(la, G::CHUNK_BYTES, 512, kLayoutSw128Base32);
+                    const uint64_t blo0 = umma_desc(lb, 16, 1024, kLayoutSw128);
 #pragma unroll
                     for (int k = 0; k < G::KSTEPS; ++k) {
                         // A: 8 pixel rows per k-step (1024 B); chunks G::CHUNK_BYTES apart.
@@ -158,14 +166,12 @@ conv_wgrad_wide_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_con
                         // 8 pixels (32 B) per k-step inside the 32-pixel block.
                         const int blk = k >> 2, rr = blk / XCS, cc = blk - rr * XCS;
                         const uint32_t boff = cc * G::B_RUN_BYTES + rr * G::B_BLOCK_BYTES + (k & 3) * 32;
-                        const uint64_t ad = umma_desc(sa + k * 1024, G::CHUNK_BYTES, 512, kLayoutSw128Base32);
-                        const uint64_t bd = umma_desc(sb + boff, 16, 1024, kLayoutSw128);
+                        const uint64_t ad = a0 + (uint64_t)((k * 1024) >> 4);
+                        const uint64_t bd = b0 + (uint64_t)(boff >> 4);
                         const uint32_t acc = (kb > kb0 || k > 0) ? 1u : 0u;
                         if (X3) {
-                            const uint64_t ald = umma_desc(la + k * 1024, G::CHUNK_BYTES, 512, kLayoutSw128Base32);
-                            const uint64_t bld = umma_desc(lb + boff, 16, 1024, kLayoutSw128);
-                            umma_tf32(d_tmem, ald, bd, idesc, acc);
-                            umma_tf32(d_tmem, ad, bld, idesc, 1u);
+                            umma_tf32(d_tmem, alo0 + (uint64_t)((k * 1024) >> 4), bd, idesc, acc);
+                            umma_tf32(d_tmem, ad, blo0 + (uint64_t)(boff >> 4), idesc, 1u);
                             umma_tf32(d_tmem, ad, bd, idesc, 1u);
                         } else {
                             umma_tf32(d_tmem, ad, bd, idesc, acc);
