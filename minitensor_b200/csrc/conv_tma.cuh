@@ -396,15 +396,25 @@ __global__ void wgrad_reduce_kernel(const float* __restrict__ ws, int splits, in
         const int tap = m / C, c = m - tap * C;
         const float* src = ws + (int64_t)m * ws_ld + co;
         float acc = 0.f;
-        int sp = 0;
-        for (; sp + 8 <= splits; sp += 8) {
-            float v[8];
+        if (splits <= 32) {
+            // Every partial in flight at once (one L2 round trip), then added in split order.
+            float v[32];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) v[j] = __ldg(src + (int64_t)(sp + j) * plane);
+            for (int j = 0; j < 32; ++j) v[j] = j < splits ? __ldg(src + (int64_t)j * plane) : 0.f;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) acc += v[j];
+            for (int j = 0; j < 32; ++j)
+                if (j < splits) acc += v[j];
+        } else {
+            int sp = 0;
+            for (; sp + 8 <= splits; sp += 8) {
+                float v[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[j] = __ldg(src + (int64_t)(sp + j) * plane);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc += v[j];
+            }
+            for (; sp < splits; ++sp) acc += __ldg(src + (int64_t)sp * plane);
         }
-        for (; sp < splits; ++sp) acc += __ldg(src + (int64_t)sp * plane);
         dw[((int64_t)co * C + c) * taps + tap] = acc;
     }
 }
