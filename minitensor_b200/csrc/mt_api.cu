@@ -360,8 +360,9 @@ int pair_streamk_plan(mt::umma::Params& up, int clusters, int kblocks, int bn, b
     }
     if (S == 1 && sk_dp == up.num_tiles) return MT_OK;
     const long long t0 = S > 1 ? 0 : sk_dp;
-    const int slots = std::max(S, maxseg);
-    const size_t ws_bytes = (size_t)(up.num_tiles - t0) * slots * mt::umma2::BM * bn * sizeof(float);
+    // S slots for each split whole tile, maxseg for each stream-K tile (umma::sk_slot).
+    const long long nslots = (sk_dp - t0) * S + (up.num_tiles - sk_dp) * (long long)maxseg;
+    const size_t ws_bytes = (size_t)nslots * mt::umma2::BM * bn * sizeof(float);
     const size_t cnt_bytes = (size_t)(up.num_tiles - t0) * 8 * sizeof(int);
     void* ws = nullptr;
     int rc = scratch_alloc(&ws, ws_bytes + cnt_bytes, st, "stream-K workspace");
@@ -374,7 +375,7 @@ int pair_streamk_plan(mt::umma::Params& up, int clusters, int kblocks, int bn, b
     }
     up.sk_dp = sk_dp;
     up.sk_split = S;
-    up.sk_maxseg = slots;
+    up.sk_maxseg = maxseg;
     up.sk_t0 = t0;
     up.sk_ws = static_cast<float*>(ws);
     up.sk_cnt = cnt;

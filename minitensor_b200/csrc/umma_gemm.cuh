@@ -69,11 +69,18 @@ struct Params {
     long long sk_dp;
     int sk_clusters;            // clusters in the launch
     int sk_split;               // S: pieces per whole tile (1 = whole tiles)
-    int sk_maxseg;              // partial slots per tile that has slots
+    int sk_maxseg;              // partial slots per stream-K tile
     long long sk_t0;            // first tile with slots (0 when S > 1, else sk_dp)
-    float* sk_ws;               // [tile - sk_t0][sk_maxseg][256 rows][BN] partial sums
+    float* sk_ws;               // partial slots [256 rows][BN] each: S per split whole tile in
+                                // [sk_t0, sk_dp), then sk_maxseg per stream-K tile (sk_slot)
     int* sk_cnt;                // [tile - sk_t0][2 CTAs][4 warps] arrivals, zero at launch
 };
+
+// First partial slot of a tile cut into pieces (see sk_ws).
+__host__ __device__ __forceinline__ long long sk_slot(const Params& p, long long tile) {
+    return tile < p.sk_dp ? (tile - p.sk_t0) * p.sk_split
+                          : (p.sk_dp - p.sk_t0) * p.sk_split + (tile - p.sk_dp) * p.sk_maxseg;
+}
 
 // Tensor maps of the ndst destinations (same view, different base pointers).
 struct DstMaps {

@@ -319,7 +319,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             const bool part = item.nseg > 1;
             const long long skt = item.tile - p.sk_t0;
             // This warp's row of the partial slots of a cut tile (slot stride 256 x BN).
-            const long long slot_row = ((skt * p.sk_maxseg) * BM + (int)rank * BMC + q * 32 + lane) * (long long)BN;
+            const long long slot_row = (umma::sk_slot(p, item.tile) * BM + (int)rank * BMC + q * 32 + lane) * (long long)BN;
             const long long slot_stride = (long long)BM * BN;
 #pragma unroll 1
             for (int c = 0; c < BN / 32; ++c) {

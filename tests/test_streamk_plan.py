@@ -13,6 +13,11 @@ import itertools
 import pytest
 
 
+def slot_of(tile, sk_dp, S, maxseg, t0):
+    """umma::sk_slot: S slots per split whole tile, maxseg per stream-K tile."""
+    return (tile - t0) * S if tile < sk_dp else (sk_dp - t0) * S + (tile - sk_dp) * maxseg
+
+
 def plan(num_tiles, clusters, kblocks, split_dp=False, gate=False):
     """(sk_dp, S, slots) as pair_streamk_plan sets them. gate=False: the stream-K remainder
     whenever it fits (the schedule properties are tested on every shape); gate=True: only
@@ -32,7 +37,7 @@ def plan(num_tiles, clusters, kblocks, split_dp=False, gate=False):
             maxseg = (kblocks + minr - 1) // minr + 1
     if S == 1 and sk_dp == num_tiles:
         return num_tiles, 1, 0          # nothing is cut: no partial slots
-    return sk_dp, S, max(S, maxseg)
+    return sk_dp, S, maxseg
 
 
 def items(num_tiles, sk_dp, kblocks, c, C, S=1):
@@ -74,13 +79,23 @@ def check_schedule(num_tiles, C, kblocks, split_dp=False):
                 covered[(tile, kb)] = c
             pieces.setdefault(tile, []).append((kb0, kb1, seg, nseg, c))
     assert len(covered) == num_tiles * kblocks
+    # Partial slots: every piece of every cut tile gets its own slot, inside the allocation.
+    t0 = 0 if S > 1 else sk_dp
+    nslots = (sk_dp - t0) * S + (num_tiles - sk_dp) * slots
+    used = set()
+    for tile, ps in pieces.items():
+        if len(ps) > 1:
+            for p in ps:
+                slot = slot_of(tile, sk_dp, S, slots, t0) + p[2]
+                assert 0 <= slot < nslots and slot not in used, (tile, p, slot, nslots)
+                used.add(slot)
     for tile, ps in pieces.items():
         ps.sort()
         nsegs = {p[3] for p in ps}
         assert len(nsegs) == 1 and nsegs.pop() == len(ps), (tile, ps)
         assert [p[2] for p in ps] == list(range(len(ps))), (tile, ps)   # seg in k order
         if len(ps) > 1:
-            assert len(ps) <= slots, (tile, len(ps), slots)
+            assert len(ps) <= (S if tile < sk_dp else slots), (tile, len(ps), slots)
             if tile >= sk_dp:
                 clusters = [p[4] for p in ps]
                 assert clusters == list(range(clusters[0], clusters[0] + len(ps)))   # consecutive clusters
