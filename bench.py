@@ -701,7 +701,9 @@ def run_gpu(args, rank, world, local_rank):
     ms = t / args.steps * 1e3
 
     # Output parity of the timed mode (rank 0 holds the whole C at every N), before the
-    # other modes overwrite the outputs. Outside the timed region.
+    # other modes overwrite the outputs. Outside the timed region. The barrier after it keeps
+    # the other ranks from starting the next mode, whose epilogues store into rank 0's C,
+    # while rank 0 is still reading it.
     par = None
     if rank == 0:
         try:
@@ -709,6 +711,8 @@ def run_gpu(args, rank, world, local_rank):
             par = wl.parity(args.mode, cpu_threads())
         except Exception as exc:
             par = {"error": f"{type(exc).__name__}: {exc}"[:200], "ok": False}
+    if dist:
+        dist.barrier()
 
     extras, e2e, cpu, e2e_ov, ref_gpu = {}, None, None, None, None   # e2e_ov: set only on failure
     if not args.no_extras:
