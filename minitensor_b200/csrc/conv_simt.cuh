@@ -181,7 +181,7 @@ __global__ void __launch_bounds__(THREADS, 2) conv_simt_kernel(Params p) {
             acc[i][j] = (KIND == kFwd && p.bias && n < p.Ncol) ? __ldg(p.bias + n) : 0.f;
         }
 
-    float ra[4], rb[NB];
+    float ra[4] = {}, rb[NB] = {};
     const int ktiles = (p.K + BK - 1) / BK;
     auto stage = [&](int buf) {
         *reinterpret_cast<float4*>(&As[buf][t >> 5][(t & 31) * 4]) = make_float4(ra[0], ra[1], ra[2], ra[3]);

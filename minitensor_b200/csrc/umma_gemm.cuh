@@ -51,9 +51,11 @@ struct Params {
     int splits;
     int64_t split_stride;
     long long num_units;        // num_tiles * splits
-    // Several destinations: the epilogue hands each warp's 32 x 32 block to the TMA engine,
-    // one tensor store per destination (maps in DstMaps, C as {N, M, batch}, box {32, 32, 1},
-    // 128-byte swizzle). SM stores to peer memory top out far below the link rate.
+    // TMA epilogue: each warp hands its 32 x 32 blocks to the TMA engine, one tensor store
+    // per destination (maps in DstMaps, C as {N, M, batch}, box {32, 32, 1}, 128-byte
+    // swizzle), whole lines instead of a 16-byte piece of 32 rows per store instruction,
+    // and SM stores to peer memory top out far below the link rate. Off (0) for split-K
+    // partials, rows that are not 16-byte aligned, or with MT_TMA_EPILOGUE=0.
     int tma_multi;
     // Stream-K remainder (CTA-pair kernel only; splits == 1 there). Tiles [0, sk_dp) run
     // whole, round-robin over the clusters. The k-blocks of tiles [sk_dp, num_tiles),
@@ -116,10 +118,29 @@ struct Cfg {
 // Tile t -> (batch, m block, n block); m blocks are grouped by 8 so that consecutive CTAs
 // share B tiles in L2.
 __device__ __forceinline__ void tile_coords(const Params& p, long long t, int& b, int& mb, int& nb) {
+    constexpr int G = 8;
+    if (p.num_tiles < (1ll << 28)) {
+        // Every quotient below fits 32 bits (8 * tiles_n <= 8 * num_tiles < 2^31): 32-bit
+        // division, several times cheaper than the 64-bit routine, which matters on the
+        // epilogue warps of short-K problems where this runs once per tile per role.
+        const unsigned per_batch = (unsigned)p.tiles_m * (unsigned)p.tiles_n;
+        const unsigned tt = (unsigned)t;
+        const unsigned bb = tt / per_batch;
+        const unsigned r = tt - bb * per_batch;
+        const unsigned gw = (unsigned)G * (unsigned)p.tiles_n;
+        const unsigned group = r / gw;
+        const int first_m = (int)(group * G);
+        const unsigned gsize = (unsigned)min(p.tiles_m - first_m, G);
+        const unsigned in_group = r - group * gw;
+        const unsigned q = in_group / gsize;
+        b = (int)bb;
+        mb = first_m + (int)(in_group - q * gsize);
+        nb = (int)q;
+        return;
+    }
     const long long per_batch = (long long)p.tiles_m * p.tiles_n;
     b = (int)(t / per_batch);
     long long r = t % per_batch;
-    constexpr int G = 8;
     long long group = r / ((long long)G * p.tiles_n);
     int first_m = (int)(group * G);
     int gsize = min(p.tiles_m - first_m, G);
@@ -354,12 +375,18 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                 }
                 const int n0 = nb * BN + c * 32;
                 float v[32];
+                if (p.epi == 0 && !no_k) {
+                    // plain product: no per-element tests in a loop that one warp runs alone
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    float x = (no_k ? 0.f : __uint_as_float(r[j])) + bias_row;
-                    if (p.epi & 2) x = x + ((n0 + j < p.N) ? __ldg(p.bias + n0 + j) : 0.f);
-                    if (p.epi & 4) x = x > 0.f ? x : 0.f;
-                    v[j] = x;
+                    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        float x = (no_k ? 0.f : __uint_as_float(r[j])) + bias_row;
+                        if (p.epi & 2) x = x + ((n0 + j < p.N) ? __ldg(p.bias + n0 + j) : 0.f);
+                        if (p.epi & 4) x = x > 0.f ? x : 0.f;
+                        v[j] = x;
+                    }
                 }
                 if (p.tma_multi) {
                     store_block_tma(dm, p.ndst, epi_stage + q * 512, seq, v, lane, n0, mb * BM + q * 32, b, p.M, p.N);
@@ -368,8 +395,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                     store_block_lines(epi_stage + q * 512, v, lane, p,
                                       (int64_t)b * p.sc_b + (int64_t)sp * p.split_stride, mb * BM + q * 32, n0);
                 } else if (p.vec_store && n0 + 32 <= p.N) {
-                    // one local destination: straight from registers (the shared-memory
-                    // round trip costs more than it saves when the epilogue is the bound)
+                    // one destination without tensor maps (split-K partials, or the TMA
+                    // epilogue switched off): straight from registers
                     if (m < p.M) {
                         float* crow = p.dst[0] + row_off;
 #pragma unroll

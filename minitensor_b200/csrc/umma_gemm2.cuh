@@ -284,12 +284,14 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             // Epilogue of one finished 32-column chunk c: bias / ReLU, then the stores.
             auto finish = [&](float (&v)[32], int c) {
                 const int n0 = nb * BN + c * 32;
+                if (p.epi) {   // plain product: no per-element tests in a loop one warp runs alone
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    float x = v[j] + bias_row;
-                    if (p.epi & 2) x = x + ((n0 + j < p.N) ? __ldg(p.bias + n0 + j) : 0.f);
-                    if (p.epi & 4) x = x > 0.f ? x : 0.f;
-                    v[j] = x;
+                    for (int j = 0; j < 32; ++j) {
+                        float x = v[j] + bias_row;
+                        if (p.epi & 2) x = x + ((n0 + j < p.N) ? __ldg(p.bias + n0 + j) : 0.f);
+                        if (p.epi & 4) x = x > 0.f ? x : 0.f;
+                        v[j] = x;
+                    }
                 }
                 if (p.tma_multi) {
                     umma::store_block_tma(dm, p.ndst, epi_stage + q * 512, seq, v, lane, n0, m0w, b, p.M, p.N);
@@ -297,8 +299,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                     // several destinations (peers over NVLink): whole-row stores
                     umma::store_block_lines(epi_stage + q * 512, v, lane, p, (int64_t)b * p.sc_b, m0w, n0);
                 } else if (p.vec_store && n0 + 32 <= p.N) {
-                    // one local destination: straight from registers (the shared-memory
-                    // round trip costs more than it saves when the epilogue is the bound)
+                    // one destination without tensor maps (the TMA epilogue switched
+                    // off): straight from registers
                     if (m < p.M) {
                         float* crow = p.dst[0] + row_off;
 #pragma unroll

@@ -389,3 +389,39 @@ def test_pair_kernel_streamk_remainder(eng, port, mode):
     eng.gemm(dev(A), dev(B), C2, mode=mode)
     assert torch.equal(C, C2)
     assert eng.device_status(reset=True) == 0
+
+
+# ------------------------------------------------------------ epilogue store forms ---
+
+def test_tma_store_epilogue_matches_register_stores(eng, port, tmp_path):
+    """The epilogue writes C through TMA tensor stores (whole lines) unless
+    MT_TMA_EPILOGUE=0 selects stores straight from registers. Both write the same
+    accumulator values, so the outputs must agree bit for bit: ragged pair and one-CTA
+    tiles, batched tiles with a row bias, config 3's broadcast bmm, and a C window whose
+    surroundings must keep their sentinel. One process per setting (read once)."""
+    import subprocess
+    import sys
+    script = os.path.join(os.path.dirname(__file__), "tma_store_cases.py")
+    res = {}
+    for flag in ("1", "0"):
+        out = str(tmp_path / f"tma{flag}.npz")
+        env = dict(os.environ, MT_TMA_EPILOGUE=flag)
+        r = subprocess.run([sys.executable, script, out], env=env, capture_output=True, text=True, timeout=600)
+        assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+        res[flag] = np.load(out)
+    tma, reg = res["1"], res["0"]
+    names = [k for k in tma.files if not k.startswith("path_")]
+    assert len(names) == 10
+    for k in names:
+        assert "tma_store" in str(tma["path_" + k]), (k, str(tma["path_" + k]))
+        assert "tma_store" not in str(reg["path_" + k]), (k, str(reg["path_" + k]))
+        assert tma[k].shape == reg[k].shape and np.array_equal(tma[k], reg[k]), k
+    for mode in ("tf32", "tf32x3"):
+        big = tma[f"window_{mode}"]
+        M, N = 1030, 1000
+        mask = np.ones_like(big, dtype=bool)
+        mask[8:8 + M, 4:4 + N] = False
+        assert np.all(big[mask] == 12345.0), mode
+        A = inputs.uniform((M, 64), -1, 1, 199)
+        B = inputs.uniform((64, N), -1, 1, 200)
+        check(mode, big[8:8 + M, 4:4 + N], port.matmul(A, B), absmm(A, B), 64, f"window {mode}")
