@@ -528,7 +528,10 @@ class C4(Workload):
         self.x, self.w, self.b, self.dy = (_cuda(a) for a in (x, w, b, dy))
         self.y = torch.empty(32, 64, 56, 56, device="cuda")
         self.dw = torch.empty(64, 64, 3, 3, device="cuda")
-        nbytes = engine.conv2d_wgrad_workspace_bytes(self.dy, self.x, tuple(self.w.shape), 1, 1, mode="tf32x3")
+        # x's channels-last copy, made once per step and read by both convolutions
+        self.x_cl = torch.empty_like(self.x, memory_format=torch.channels_last)
+        nbytes = max(engine.conv2d_wgrad_workspace_bytes(self.dy, xv, tuple(self.w.shape), 1, 1, mode=md)
+                     for xv in (self.x, self.x_cl) for md in ("tf32x3", "tf32"))
         self.ws = torch.empty(max(1, nbytes // 4), device="cuda")
         self.h2d = [(_pin(x), self.x), (_pin(dy), self.dy)]
         self.d2h = [(self.y, torch.empty(32, 64, 56, 56).pin_memory()), (self.dw, torch.empty(64, 64, 3, 3).pin_memory())]
@@ -537,9 +540,14 @@ class C4(Workload):
         e = self.engine
         L = e.lib()
         m, s = e._mode(mode), e._stream(None)
-        e._check(L.mt_conv2d_fwd(ctypes.byref(e.view(self.x)), ctypes.byref(e.view(self.w)),
+        # strict fp32 reads NCHW directly; the tensor-core paths share one NHWC copy of x
+        x = self.x
+        if m != e.STRICT_FP32:
+            e._check(L.mt_nchw_to_nhwc(ctypes.byref(e.view(self.x)), ctypes.byref(e.view(self.x_cl)), s))
+            x = self.x_cl
+        e._check(L.mt_conv2d_fwd(ctypes.byref(e.view(x)), ctypes.byref(e.view(self.w)),
                                  ctypes.byref(e.view(self.b)), ctypes.byref(e.view(self.y)), 1, 1, m, s))
-        e._check(L.mt_conv2d_wgrad(ctypes.byref(e.view(self.dy)), ctypes.byref(e.view(self.x)),
+        e._check(L.mt_conv2d_wgrad(ctypes.byref(e.view(self.dy)), ctypes.byref(e.view(x)),
                                    ctypes.byref(e.view(self.dw)), 1, 1, m, self.ws.data_ptr(),
                                    self.ws.numel() * 4, s))
 

@@ -166,6 +166,16 @@ MT_API int mt_conv2d_wgrad(const mt_tensor* dy, const mt_tensor* x, const mt_ten
 MT_API size_t mt_conv2d_wgrad_workspace_bytes(const mt_tensor* dy, const mt_tensor* x, const mt_tensor* dw,
                                               uint64_t stride, uint64_t padding, int mode);
 
+/* Channels-last copy of an (N, C, H, W) view: out has x's shape with strides
+ * (H*W*C, 1, W*C, C), C a multiple of 4, start 16-byte aligned; x and out must not overlap.
+ * No counterpart in the reference, which keeps every tensor NCHW. The stride-1 tensor-core
+ * convolutions work on NHWC and transform an NCHW input on every call; given such a copy
+ * (for x, or dy in mt_conv2d_dgrad) they read it in place. A training step whose forward
+ * and weight gradient share one input therefore transforms it once: mt_conv2d_fwd and
+ * mt_conv2d_wgrad on the same copy (the path string ends in " nhwc_in"). Results are
+ * bitwise those of the NCHW input. */
+MT_API int mt_nchw_to_nhwc(const mt_tensor* x, const mt_tensor* out, void* stream);
+
 /* Weight gradient that allocates nothing: no counterpart in the reference. For callers
  * that cannot allocate device memory during the call (a graph capture that forbids
  * allocation nodes, a host that owns all device memory, a latency-critical loop). It

@@ -75,6 +75,34 @@ __device__ __forceinline__ uint64_t halo_desc(uint32_t start) {
     return umma_desc(start, 16, 1024, kLayoutSw128);
 }
 
+// The MMAs of NT taps of a 3x3 filter (whole filter rows starting at row `row0`) over one
+// 32-channel block: 4 k-steps per tap, 3 MMAs per k-step in TF32X3. Unrolled so that every
+// descriptor offset but the pitch is a constant: a 128 x 64 x 8 MMA takes ~48 cycles, and
+// the loop's per-tap arithmetic on the one issuing thread had cost as much again (c4
+// forward: 3.84 -> 3.52 us of issue per tile).
+template <int NT, bool X3, uint32_t BMAT>
+__device__ __forceinline__ void issue_row_taps(uint32_t d_tmem, uint64_t a0, uint64_t alo0, uint64_t b0,
+                                               uint32_t idesc, uint32_t P8, uint32_t row0, bool& first_mma) {
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+        const uint64_t ao = (uint64_t)((row0 + t / 3) * P8 + (t % 3) * 8u);   // (r * P + s) * 128 B >> 4
+        const uint64_t bo = (uint64_t)(((X3 ? 2u * t : (uint32_t)t) * BMAT) >> 4);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint64_t ad = a0 + ao + 2 * k, bd = b0 + bo + 2 * k;
+            const uint32_t acc = (!first_mma || t > 0 || k > 0) ? 1u : 0u;
+            if (X3) {
+                umma_tf32(d_tmem, alo0 + ao + 2 * k, bd, idesc, acc);
+                umma_tf32(d_tmem, ad, bd + (BMAT >> 4), idesc, 1u);
+                umma_tf32(d_tmem, ad, bd, idesc, 1u);
+            } else {
+                umma_tf32(d_tmem, ad, bd, idesc, acc);
+            }
+        }
+    }
+    first_mma = false;
+}
+
 template <bool X3>
 struct HaloCfg {
     static constexpr int NUM_WARPS = X3 ? 11 : 7;
@@ -223,6 +251,13 @@ conv_fwd_halo_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
                             goto done;
                         tc_fence_after();
                         const uint64_t b0 = umma_desc(smem_u32(b_ring + bs * p.b_bytes), 16, 1024, kLayoutSw128);
+                        if (p.kw == 3 && ts == 0 && (p.G == 9 || p.G == 3)) {
+                            // 3x3 filter, a stage of whole filter rows
+                            const uint32_t P8 = (uint32_t)p.P * 8u;
+                            if (p.G == 9) issue_row_taps<9, X3, BMAT>(d_tmem, a0, alo0, b0, idesc, P8, (uint32_t)tr, first_mma);
+                            else issue_row_taps<3, X3, BMAT>(d_tmem, a0, alo0, b0, idesc, P8, (uint32_t)tr, first_mma);
+                            tr += p.G / 3;
+                        } else
                         for (int gi = 0; gi < p.G; ++gi) {
                             const uint64_t ao = (uint64_t)(((uint32_t)(tr * p.P + ts) * 128u) >> 4);
                             const uint64_t bo = (uint64_t)(((X3 ? 2u * gi : (uint32_t)gi) * BMAT) >> 4);

@@ -709,6 +709,21 @@ bool is_contig(const mt_tensor* t) {
     return true;
 }
 
+// A 4-D (N, C, H, W) view already laid out as the conv kernels' NHWC copy: channel stride
+// 1, then W, H, N densely, C a multiple of 4 (no channel padding) and a 16-byte-aligned
+// start -- what mt_nchw_to_nhwc writes. The stride-1 tensor-core paths read such an input
+// in place instead of transforming it. Strides of size-1 dimensions are not looked at.
+bool nhwc_dense(const mt_tensor* t) {
+    if (!t || t->ndim != 4 || !t->data) return false;
+    const uint64_t N = t->shape[0], C = t->shape[1], H = t->shape[2], W = t->shape[3];
+    if (N * C * H * W == 0 || C % 4 != 0) return false;
+    if (t->strides[1] != 1) return false;
+    if (W > 1 && t->strides[3] != C) return false;
+    if (H > 1 && t->strides[2] != W * C) return false;
+    if (N > 1 && t->strides[0] != H * W * C) return false;
+    return aligned16(t->data + t->offset);
+}
+
 uint64_t numel(const mt_tensor* t) {
     if (!t) return 0;
     uint64_t n = 1;
@@ -1167,9 +1182,14 @@ int run_fwd_tma(const float* act, int N, int Hin, int Win, int Cin, const float*
     return rc;
 }
 
-size_t fwd_tma_scratch(int64_t N, int64_t H, int64_t W, int64_t C, int64_t Co, int64_t taps) {
+// Floats of the NHWC copy at the head of the forward's scratch (0 when the input is read in
+// place), rounded so that the reordered weights after it start 256-byte aligned.
+int64_t fwd_xt_floats(int64_t N, int64_t H, int64_t W, int64_t C, bool in_place) {
+    return in_place ? 0 : ((N * H * W * ((C + 3) & ~3) + 63) & ~int64_t(63));
+}
+size_t fwd_tma_scratch(int64_t N, int64_t H, int64_t W, int64_t C, int64_t Co, int64_t taps, bool in_place) {
     const int64_t Cp = (C + 3) & ~3;
-    return (size_t)(N * H * W * Cp + 2 * taps * Co * Cp) * sizeof(float) + 256;   // weights: room for hi + lo
+    return (size_t)(fwd_xt_floats(N, H, W, C, in_place) + 2 * taps * Co * Cp) * sizeof(float) + 256;   // weights: hi + lo
 }
 
 int conv_fwd(const mt_tensor* x, const mt_tensor* w, const mt_tensor* bias, const mt_tensor* y, uint64_t stride,
@@ -1205,19 +1225,22 @@ int conv_fwd(const mt_tensor* x, const mt_tensor* w, const mt_tensor* bias, cons
     }
     const bool x3 = mode == MT_TF32X3;
     if (s.stride == 1) {
-        // TMA path: x -> NHWC and W -> [tap][co][ci] in a stream-ordered scratch buffer.
-        const size_t bytes = fwd_tma_scratch(s.N, s.H, s.W, s.C, s.Co, s.kh * s.kw);
+        // TMA path: x -> NHWC (unless x already is) and W -> [tap][co][ci] in a
+        // stream-ordered scratch buffer.
+        const bool in_place = nhwc_dense(x);
+        const size_t bytes = fwd_tma_scratch(s.N, s.H, s.W, s.C, s.Co, s.kh * s.kw, in_place);
         float* scratch = nullptr;
         if ((rc = scratch_alloc(reinterpret_cast<void**>(&scratch), bytes, st, "conv fwd scratch"))) return rc;
-        float* xt = scratch;
-        float* wt = scratch + ((s.N * s.H * s.W * ((s.C + 3) & ~3) + 63) & ~int64_t(63));
+        float* xt = in_place ? const_cast<float*>(cp.x) : scratch;
+        float* wt = scratch + fwd_xt_floats(s.N, s.H, s.W, s.C, in_place);
         std::string path;
-        rc = to_nhwc(cp.x, cp.sx, xt, (int)s.N, (int)s.C, (int)s.H, (int)s.W, st);
+        if (!in_place) rc = to_nhwc(cp.x, cp.sx, xt, (int)s.N, (int)s.C, (int)s.H, (int)s.W, st);
         if (!rc) rc = run_fwd_tma(xt, (int)s.N, (int)s.H, (int)s.W, (int)s.C, cp.w, cp.sw, false, wt, (int)s.Co,
                                   (int)s.kh, (int)s.kw,
                                   (int)s.pad, cp.out, (int)s.Ho, (int)s.Wo, bp, x3, st, di.sms, path);
         scratch_free(scratch, bytes, st);
-        if (rc == MT_OK) t_path = std::string("conv_umma_fwd_") + (x3 ? "tf32x3 " : "tf32 ") + path;
+        if (rc == MT_OK)
+            t_path = std::string("conv_umma_fwd_") + (x3 ? "tf32x3 " : "tf32 ") + path + (in_place ? " nhwc_in" : "");
         return rc;
     }
     if (!offsets_fit_32(x) || !offsets_fit_32(w))
@@ -1267,18 +1290,20 @@ int conv_dgrad(const mt_tensor* dy, const mt_tensor* w, const mt_tensor* dx, uin
         // one padding for both dimensions, as the reference's conv does, so this mapping
         // needs a square filter: kh != kw would need kw-1-pad across. Non-square filters
         // take the gather kernel below, which indexes dy per dimension.
-        const size_t bytes = fwd_tma_scratch(s.N, s.Ho, s.Wo, s.Co, s.C, s.kh * s.kw);
+        const bool in_place = nhwc_dense(dy);
+        const size_t bytes = fwd_tma_scratch(s.N, s.Ho, s.Wo, s.Co, s.C, s.kh * s.kw, in_place);
         float* scratch = nullptr;
         if ((rc = scratch_alloc(reinterpret_cast<void**>(&scratch), bytes, st, "conv dgrad scratch"))) return rc;
-        float* dyt = scratch;
-        float* wt = scratch + ((s.N * s.Ho * s.Wo * ((s.Co + 3) & ~3) + 63) & ~int64_t(63));
+        float* dyt = in_place ? const_cast<float*>(cp.dy) : scratch;
+        float* wt = scratch + fwd_xt_floats(s.N, s.Ho, s.Wo, s.Co, in_place);
         std::string path;
-        rc = to_nhwc(cp.dy, cp.sdy, dyt, (int)s.N, (int)s.Co, (int)s.Ho, (int)s.Wo, st);
+        if (!in_place) rc = to_nhwc(cp.dy, cp.sdy, dyt, (int)s.N, (int)s.Co, (int)s.Ho, (int)s.Wo, st);
         if (!rc) rc = run_fwd_tma(dyt, (int)s.N, (int)s.Ho, (int)s.Wo, (int)s.Co, cp.w, cp.sw, true, wt, (int)s.C,
                                   (int)s.kh, (int)s.kw,
                                   (int)(s.kh - 1 - s.pad), cp.out, (int)s.H, (int)s.W, nullptr, x3, st, di.sms, path);
         scratch_free(scratch, bytes, st);
-        if (rc == MT_OK) t_path = std::string("conv_umma_dgrad_") + (x3 ? "tf32x3 " : "tf32 ") + path;
+        if (rc == MT_OK)
+            t_path = std::string("conv_umma_dgrad_") + (x3 ? "tf32x3 " : "tf32 ") + path + (in_place ? " nhwc_in" : "");
         return rc;
     }
     if (!offsets_fit_32(dy) || !offsets_fit_32(w))
@@ -1323,12 +1348,12 @@ WgradPlan wgrad_plan(const ConvShape& s, int sms) {
 
 // Weight-grad on the TMA path: x -> NHWC (xt), partials [splits][taps*C][Cop].
 struct WgradTmaPlan {
-    bool ok;
+    bool ok, x_in_place;
     int bn, xcs, rs, tiles_m, tiles_n, xblocks, kb_per_img, kb_total, splits, M, ws_ld;
     size_t xt_floats, part_floats, bytes;
 };
 
-WgradTmaPlan wgrad_tma_plan(const ConvShape& s, const mt_tensor* dy, int sms, bool x3) {
+WgradTmaPlan wgrad_tma_plan(const ConvShape& s, const mt_tensor* dy, const mt_tensor* x, int sms, bool x3) {
     WgradTmaPlan w;
     memset(&w, 0, sizeof w);
     const bool dy_ok = dy->strides[3] == 1 && dy->strides[2] % 4 == 0 && dy->strides[1] % 4 == 0 &&
@@ -1348,7 +1373,8 @@ WgradTmaPlan wgrad_tma_plan(const ConvShape& s, const mt_tensor* dy, int sms, bo
     w.kb_total = (int)s.N * w.kb_per_img;
     const int tiles = w.tiles_m * w.tiles_n;
     w.splits = std::max(1, std::min(tiles >= sms ? 1 : sms / tiles, w.kb_total));
-    w.xt_floats = (size_t)(s.N * s.H * s.W * ((s.C + 3) & ~3));
+    w.x_in_place = nhwc_dense(x);   // read x where it is, no NHWC copy
+    w.xt_floats = w.x_in_place ? 0 : (size_t)(s.N * s.H * s.W * ((s.C + 3) & ~3));
     w.xt_floats = (w.xt_floats + 63) & ~size_t(63);
     w.part_floats = (size_t)w.splits * w.M * w.ws_ld;
     w.bytes = (w.xt_floats + w.part_floats) * sizeof(float);
@@ -1357,9 +1383,9 @@ WgradTmaPlan wgrad_tma_plan(const ConvShape& s, const mt_tensor* dy, int sms, bo
 
 int conv_wgrad_tma(const ConvShape& s, const WgradTmaPlan& w, const mt::conv::Params& cp, float* dwp, float* scratch,
                    bool x3, cudaStream_t st, int sms, const char* who) {
-    float* xt = scratch;
+    float* xt = w.x_in_place ? const_cast<float*>(cp.x) : scratch;
     float* part = scratch + w.xt_floats;
-    int rc = to_nhwc(cp.x, cp.sx, xt, (int)s.N, (int)s.C, (int)s.H, (int)s.W, st);
+    int rc = w.x_in_place ? MT_OK : to_nhwc(cp.x, cp.sx, xt, (int)s.N, (int)s.C, (int)s.H, (int)s.W, st);
     if (rc) return rc;
     mt::convt::WgradParams wp;
     memset(&wp, 0, sizeof wp);
@@ -1443,7 +1469,7 @@ int conv_wgrad(const mt_tensor* dy, const mt_tensor* x, const mt_tensor* dw, uin
     if (!offsets_fit_32(dy) || !offsets_fit_32(x))
         return fail(MT_EUNSUPPORTED, "%s: a view spans 2^31 elements or more", who);
     const bool x3w = mode == MT_TF32X3;
-    const WgradTmaPlan tp = allow_tma ? wgrad_tma_plan(s, dy, di.sms, x3w) : WgradTmaPlan{};
+    const WgradTmaPlan tp = allow_tma ? wgrad_tma_plan(s, dy, x, di.sms, x3w) : WgradTmaPlan{};
     if (tp.ok) {
         float* scratch = static_cast<float*>(workspace);
         bool owned = false;
@@ -1458,7 +1484,7 @@ int conv_wgrad(const mt_tensor* dy, const mt_tensor* x, const mt_tensor* dw, uin
         if (owned) scratch_free(scratch, tp.bytes, st);
         if (rc == MT_OK)
             t_path = std::string("conv_umma_wgrad_") + (x3w ? "tf32x3" : "tf32") + " tma bn=" + std::to_string(tp.bn) +
-                     " splits=" + std::to_string(tp.splits);
+                     " splits=" + std::to_string(tp.splits) + (tp.x_in_place ? " nhwc_in" : "");
         return rc;
     }
     WgradPlan wp = wgrad_plan(s, di.sms);
@@ -1846,6 +1872,24 @@ MT_API int mt_conv2d_fwd(const mt_tensor* x, const mt_tensor* w, const mt_tensor
     if (mode < MT_MODE_DEFAULT || mode > MT_TF32X3) return fail(MT_EINVAL, "conv2d_fwd: bad mode %d", mode);
     return conv_fwd(x, w, bias, y, stride, padding, mode, static_cast<cudaStream_t>(stream), "conv2d_fwd");
 }
+MT_API int mt_nchw_to_nhwc(const mt_tensor* x, const mt_tensor* out, void* stream) {
+    const char* who = "nchw_to_nhwc";
+    int rc;
+    if ((rc = check4(x, who, "input")) || (rc = check4(out, who, "output"))) return rc;
+    for (int i = 0; i < 4; ++i)
+        if (x->shape[i] != out->shape[i]) return fail(MT_EINVAL, "%s: output shape differs from the input's", who);
+    if (numel(x) == 0) return MT_OK;
+    if (!nhwc_dense(out))
+        return fail(MT_EINVAL, "%s: output must be a channels-last dense (N, C, H, W) view, C a multiple of 4, "
+                               "16-byte aligned", who);
+    if (!offsets_fit_32(x)) return fail(MT_EUNSUPPORTED, "%s: a view spans 2^31 elements or more", who);
+    int64_t sv[4];
+    fill_strides(sv, x);
+    rc = to_nhwc(x->data + x->offset, sv, out->data + out->offset, (int)x->shape[0], (int)x->shape[1],
+                 (int)x->shape[2], (int)x->shape[3], static_cast<cudaStream_t>(stream));
+    if (rc == MT_OK) t_path = "nchw_to_nhwc";
+    return rc;
+}
 MT_API int mt_conv2d_dgrad(const mt_tensor* dy, const mt_tensor* w, const mt_tensor* dx, uint64_t stride,
                            uint64_t padding, int mode, void* stream) {
     if (mode < MT_MODE_DEFAULT || mode > MT_TF32X3) return fail(MT_EINVAL, "conv2d_dgrad: bad mode %d", mode);
@@ -1949,7 +1993,7 @@ MT_API size_t mt_conv2d_wgrad_workspace_bytes(const mt_tensor* dy, const mt_tens
     if (conv_shape(x, dw, dy, stride, padding, "wgrad_ws", s)) return 0;
     if (s.N * s.Ho * s.Wo == 0 || s.Co * s.C * s.kh * s.kw == 0) return 0;
     if (resolve_mode(mode) == MT_STRICT_FP32) return strict_wgrad_bytes(s);
-    const WgradTmaPlan tp = wgrad_tma_plan(s, dy, dev_info().sms, resolve_mode(mode) == MT_TF32X3);
+    const WgradTmaPlan tp = wgrad_tma_plan(s, dy, x, dev_info().sms, resolve_mode(mode) == MT_TF32X3);
     return tp.ok ? tp.bytes : wgrad_plan(s, dev_info().sms).ws_bytes;
 }
 

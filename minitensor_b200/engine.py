@@ -82,6 +82,8 @@ def lib() -> ctypes.CDLL:
     L.mt_conv2d_wgrad.restype = ctypes.c_int
     L.mt_conv2d_wgrad_workspace_bytes.argtypes = [P, P, P, u64, u64, ctypes.c_int]
     L.mt_conv2d_wgrad_workspace_bytes.restype = ctypes.c_size_t
+    L.mt_nchw_to_nhwc.argtypes = [P, P, vp]
+    L.mt_nchw_to_nhwc.restype = ctypes.c_int
     L.mt_sum_rows_gpu.argtypes = [P, P, vp]
     L.mt_sum_rows_gpu.restype = ctypes.c_int
     L.mt_conv2d_wgrad_noalloc.argtypes = [P, P, P, u64, u64, ctypes.c_int, vp]
@@ -425,6 +427,18 @@ def conv2d_backward_weight_gpu(dy, x, dw, stride, padding, stream=None):
 def conv2d_backward_bias_gpu(dy, db, stream=None):
     """include/TensorOps.hpp:712."""
     _check(lib().mt_conv2d_backward_bias_gpu(_ref(view(dy)), _ref(view(db)), _stream(stream)))
+
+
+def nchw_to_nhwc(x, out=None, stream=None):
+    """Channels-last copy of a 4-D (N, C, H, W) tensor through mt_nchw_to_nhwc; C must be a
+    multiple of 4. The stride-1 tensor-core convolutions read such a copy in place, so a step
+    that runs the forward and the weight gradient on the same input transforms it once."""
+    if x.dim() != 4:
+        raise ValueError("nchw_to_nhwc expects a 4-D tensor")
+    if out is None:
+        out = torch.empty_like(x, memory_format=torch.channels_last)
+    _check(lib().mt_nchw_to_nhwc(_ref(view(x)), _ref(view(out)), _stream(stream)))
+    return out
 
 
 def conv2d(x, w, bias=None, stride=1, padding=0, mode=MODE_DEFAULT, stream=None):

@@ -150,6 +150,10 @@ def test_workspace_query_describes_dw_by_shape(mode, x3):
     n = engine.conv2d_wgrad_workspace_bytes(_t(N, Co, H, W), _t(N, C, H, W), (Co, C, k, k), 1, 1, mode)
     want, _ = tma_bytes(N, C, H, W, Co, k, k, H, W, _sms(), x3)
     assert n == want > 0
+    # x given as a channels-last copy (mt_nchw_to_nhwc's layout): read in place, no NHWC copy.
+    x_cl = _t(N, C, H, W).contiguous(memory_format=torch.channels_last)
+    n_cl = engine.conv2d_wgrad_workspace_bytes(_t(N, Co, H, W), x_cl, (Co, C, k, k), 1, 1, mode)
+    assert n_cl == tma_bytes(N, C, H, W, Co, k, k, H, W, _sms(), x3, x_in_place=True)[0] < n
     # Stride 2: the gather plan, whose only scratch is the split-K partials.
     n2 = engine.conv2d_wgrad_workspace_bytes(_t(N, Co, 4, 4), _t(N, C, H, W), (Co, C, k, k), 2, 1, mode)
     from wgrad_plan import gather_bytes
@@ -245,3 +249,17 @@ def test_scratch_allocator_needs_both_functions():
     assert lib.mt_set_scratch_allocator(None, None, None) == engine.MT_OK   # back to stream-ordered
     a, b = engine.scratch_counts()
     assert a >= 0 and b >= 0
+
+
+def test_nchw_to_nhwc_argument_errors():
+    # Checked before any device call: shapes, the output's channels-last layout, C % 4.
+    lib = engine.lib()
+    x = _t(2, 8, 5, 6)
+    v = engine.view
+    bad = [(x, _t(2, 8, 5, 7).contiguous(memory_format=torch.channels_last), b"shape"),
+           (x, _t(2, 8, 5, 6), b"channels-last"),
+           (_t(2, 6, 5, 6), _t(2, 6, 5, 6).contiguous(memory_format=torch.channels_last), b"channels-last")]
+    for a, o, msg in bad:
+        assert lib.mt_nchw_to_nhwc(ctypes.byref(v(a)), ctypes.byref(v(o)), None) == engine.MT_EINVAL
+        assert msg in lib.mt_last_error()
+    assert lib.mt_nchw_to_nhwc(None, ctypes.byref(v(x)), None) == engine.MT_EINVAL

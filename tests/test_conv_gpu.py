@@ -232,3 +232,55 @@ def test_strict_wgrad_paths(eng, port):
         _, dw, _ = eng.conv2d_backward(dev(dy), dev(x), dev(w), 1, 1, need=("weight",), mode="strict", workspace=ws)
         assert eng.last_path() == path, eng.last_path()
         check("strict", host(dw), ref, D, N * H * W, path)
+
+
+@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("stride", [1, 2])
+def test_channels_last_inputs(eng, port, mode, stride):
+    """mt_nchw_to_nhwc's copy is the same tensor in the layout the stride-1 tensor-core
+    kernels work on: the forward and the weight gradient read x from it in place, the
+    input gradient dy (path " nhwc_in"), with results bitwise those of the NCHW inputs. Other
+    paths (stride 2, strict fp32) read the copy as any strided view, also bitwise equal."""
+    N, C, H, W, Co, k, p = 3, 64, 18, 20, 48, 3, 1   # W % 4 == 0: dy's rows suit the TMA weight-grad
+    x = inputs.normal((N, C, H, W), 1.0, 1501)
+    w = inputs.normal((Co, C, k, k), 0.05, 1502)
+    b = inputs.normal((Co,), 0.1, 1503)
+    Ho, Wo = (H + 2 * p - k) // stride + 1, (W + 2 * p - k) // stride + 1
+    dy = inputs.normal((N, Co, Ho, Wo), 1.0, 1504)
+    xd, wd, bd, dyd = dev(x), dev(w), dev(b), dev(dy)
+    x_cl = eng.nchw_to_nhwc(xd)
+    assert x_cl.stride() == (H * W * C, 1, W * C, C) and torch.equal(x_cl, xd)
+    dy_cl = eng.nchw_to_nhwc(dyd)
+    assert torch.equal(dy_cl, dyd)
+    in_place = stride == 1 and mode != "strict"
+
+    y0 = eng.conv2d(xd, wd, bd, stride, p, mode=mode)
+    y1 = eng.conv2d(x_cl, wd, bd, stride, p, mode=mode)
+    assert ("nhwc_in" in eng.last_path()) == in_place, eng.last_path()
+    assert torch.equal(y0, y1)
+    dx0, dw0, _ = eng.conv2d_backward(dyd, xd, wd, stride, p, need=("input", "weight"), mode=mode)
+    _, dw1, _ = eng.conv2d_backward(dyd, x_cl, wd, stride, p, need=("weight",), mode=mode)
+    assert ("nhwc_in" in eng.last_path()) == in_place, eng.last_path()
+    assert torch.equal(dw0, dw1)
+    dx1, _, _ = eng.conv2d_backward(dy_cl, xd, wd, stride, p, need=("input",), mode=mode)
+    assert ("nhwc_in" in eng.last_path()) == in_place, eng.last_path()
+    assert torch.equal(dx0, dx1)
+    check(mode, host(y1), port.conv2d(x, w, b, stride, p, THREADS), d_fwd(x, w, stride, p) + np.abs(b)[None, :, None, None],
+          C * k * k, "fwd from channels-last x")
+    check(mode, host(dw1), port.conv2d_bwd_weight(dy, x, w.shape, stride, p, THREADS),
+          d_wgrad(dy, x, w.shape, stride, p), N * Ho * Wo, "wgrad from channels-last x")
+
+
+def test_nchw_to_nhwc_views_and_errors(eng):
+    """The copy from a strided NCHW view (a crop), and the layouts the output must have."""
+    base = torch.randn(2, 40, 17, 23, device="cuda")
+    xv = base[:, 4:36, 1:16, 2:21]                     # 32 channels, not contiguous
+    out = eng.nchw_to_nhwc(xv)
+    assert torch.equal(out, xv) and out.stride() == (15 * 19 * 32, 1, 19 * 32, 32)
+    with pytest.raises(ValueError, match="channels-last"):
+        eng.nchw_to_nhwc(xv, out=torch.empty(2, 32, 15, 19, device="cuda"))       # NCHW output
+    with pytest.raises(ValueError, match="channels-last"):
+        x6 = torch.randn(1, 6, 4, 4, device="cuda")                              # C % 4 != 0
+        eng.nchw_to_nhwc(x6, out=torch.empty_like(x6, memory_format=torch.channels_last))
+    with pytest.raises(ValueError, match="shape"):
+        eng.nchw_to_nhwc(xv, out=torch.empty(2, 32, 15, 18, device="cuda").to(memory_format=torch.channels_last))

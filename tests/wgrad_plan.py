@@ -25,8 +25,9 @@ def gather_bytes(N, C, Co, kh, kw, Ho, Wo, sms):
     return (s * Co * M * 4 if s > 1 else 0), s
 
 
-def tma_bytes(N, C, H, W, Co, kh, kw, Ho, Wo, sms, x3):
-    """NHWC copy of x (channels padded to 4, rounded to 64 floats) + split partials."""
+def tma_bytes(N, C, H, W, Co, kh, kw, Ho, Wo, sms, x3, x_in_place=False):
+    """NHWC copy of x (channels padded to 4, rounded to 64 floats; none when x is already
+    a channels-last copy, read in place) + split partials."""
     xcs, rs = (1, 1) if x3 else (2, 1)
     M = kh * kw * C
     bn = pick_bn(Co)
@@ -35,6 +36,6 @@ def tma_bytes(N, C, H, W, Co, kh, kw, Ho, Wo, sms, x3):
     xblocks = (Wo + 32 * xcs - 1) // (32 * xcs)
     kb_total = N * ((Ho + rs - 1) // rs) * xblocks
     s = _splits(tiles, kb_total, sms)
-    xt = N * H * W * ((C + 3) & ~3)
+    xt = 0 if x_in_place else N * H * W * ((C + 3) & ~3)
     xt = (xt + 63) & ~63
     return (xt + s * M * tiles_n * bn) * 4, s
