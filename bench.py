@@ -17,6 +17,7 @@ from __future__ import annotations
 import argparse
 import ctypes
 import json
+import math
 import os
 import statistics
 import sys
@@ -69,7 +70,7 @@ class ClockSampler:
     REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
                0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, device_index: int, period: float = 0.02):
+    def __init__(self, device_index: int, period: float = 0.005):
         self.samples, self.reasons, self.max_mhz = [], set(), None
         self.period = period
         self._stop = threading.Event()
@@ -665,7 +666,16 @@ def run_gpu(args, rank, world, local_rank):
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         return float(tt.item())
 
+    t_w = time.perf_counter()
     for _ in range(args.warmup):
+        wl.step(args.mode)
+    torch.cuda.synchronize()
+    # Clock settling: a GPU that was idle before this run ramps its clocks up over a
+    # fraction of a second, so the warm-up runs on (same step) until it has lasted 0.25 s.
+    # The count is the largest any rank needs, so every rank takes the same steps.
+    per_step = (time.perf_counter() - t_w) / max(1, args.warmup)
+    settle = int(max_over_ranks(float(max(0, math.ceil(0.25 / max(per_step, 1e-6)) - args.warmup))))
+    for _ in range(settle):
         wl.step(args.mode)
     torch.cuda.synchronize()
     if dist:
@@ -691,14 +701,38 @@ def run_gpu(args, rank, world, local_rank):
             print(f"graph capture failed ({exc}); timing eager launches", file=sys.stderr)
             return None, 0
 
+    # Working sets that fit the 126 MB L2 (every workload but c5) are timed cold: before each
+    # step a 256 MB buffer is written, outside the events, and each step is timed alone (the
+    # replay of a one-step graph on one GPU, the eager step on several).
+    flush = wl.name != "c5"
+    flush_buf = torch.empty(64 << 20, dtype=torch.float32, device="cuda") if flush else None
+
     def timed(mode, steps, graph):
         """(seconds for `steps` steps, kernel launches per timed region)."""
+        if flush:
+            n0 = engine.launch_count()
+            evs = []
+            for i in range(steps):
+                flush_buf.fill_(float(i))
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                if graph is not None:
+                    graph.replay()
+                else:
+                    wl.step(mode)
+                b.record(stream)
+                evs.append((a, b))
+            torch.cuda.synchronize()
+            t = sum(a.elapsed_time(b) for a, b in evs) / 1e3
+            return t, (None if graph is not None else engine.launch_count() - n0)
         if graph is not None:
             return time_steps(graph.replay, 1, stream), None
         n0 = engine.launch_count()
         return time_steps(lambda: wl.step(mode), steps, stream), engine.launch_count() - n0
 
-    graph, launches = capture(args.mode, args.steps)
+    graph, launches = capture(args.mode, 1 if flush else args.steps)
+    if flush and graph is not None:
+        launches *= args.steps
     with ClockSampler(local_rank) as clk:
         t, eager_launches = timed(args.mode, args.steps, graph)
     if eager_launches is not None:
@@ -733,7 +767,7 @@ def run_gpu(args, rank, world, local_rank):
             torch.cuda.synchronize()
             if dist:
                 dist.barrier()
-            gm, _ = capture(m, s)
+            gm, _ = capture(m, 1 if flush else s)
             tm = max_over_ranks(timed(m, s, gm)[0])
             del gm
             extras[m] = {"value": wl.flops * s / tm / 1e12, "ms_per_step": tm / s * 1e3}
@@ -849,14 +883,16 @@ def run_gpu(args, rank, world, local_rank):
                                        "strict": "fp32"}[args.mode],
         "data": "synthetic (seeded, no dataset)",
         "config": {"workload": wl.desc, "mode": args.mode,
-                   "timing": "one CUDA-graph replay of the K captured steps" if graph is not None
+                   "timing": ("K replays of a one-step CUDA graph, each timed alone" if flush else
+                              "one CUDA-graph replay of the K captured steps") if graph is not None
                              else "K eager steps",
+                   "warmup_settle_steps": settle,
                    "parallelism": ("single GPU" if world == 1 else
                                    f"batch shards x{world}, all-gather by epilogue peer stores" if wl.name == "c3" else
                                    f"N-column shards x{world}, all-gather by "
                                    + ("epilogue peer stores" if wl.plan.gather == "epilogue" else "copy engines")),
-                   "l2": "inputs larger than the 126 MB L2, no flush" if wl.name == "c5" else
-                         "steps back to back without an L2 flush (working set fits L2)"},
+                   "l2": "inputs larger than the 126 MB L2, no flush" if not flush else
+                         "L2 flushed before every timed step (256 MB written outside the events)"},
         "roofline": roofline, "parity": par, "cpu_baseline": cpu, "ref_gpu_baseline": ref_gpu, "e2e": e2e, **({"e2e_host_api_error": e2e_ov} if e2e_ov else {}), "modes": extras,
         "clocks": clk.summary(), "gpu_launches": launches,
     }
