@@ -180,10 +180,19 @@ int launch_simt(const GemmProblem& p, cudaStream_t st) {
     else if (okB && p.sb_k == 1 && p.sb_n % 4 == 0) lb = kLdKContigVec;
     dim3 grid((unsigned)((p.N + simt::BN - 1) / simt::BN), (unsigned)((p.M + simt::BM - 1) / simt::BM),
               (unsigned)p.batch);
+    // Fewer 128 x 128 tiles than SMs: 64 x 64 tiles, 4x the CTAs (the per-output order and
+    // so the bits are the same; strict fp32 cannot split K).
+    const bool small = (long long)grid.x * grid.y * grid.z < (long long)dev_info().sms;
+    if (small)
+        grid = dim3((unsigned)((p.N + simt::small::BN - 1) / simt::small::BN),
+                    (unsigned)((p.M + simt::small::BM - 1) / simt::small::BM), (unsigned)p.batch);
     if (grid.y > 65535 || grid.z > 65535) return fail(MT_EUNSUPPORTED, "simt: grid too large (M=%lld batch=%lld)",
                                                       (long long)p.M, (long long)p.batch);
-#define MT_SIMT_CASE(LA, LB) \
-    if (la == LA && lb == LB) simt::gemm_kernel<LA, LB><<<grid, simt::THREADS, 0, st>>>(p);
+#define MT_SIMT_CASE(LA, LB)                                                                          \
+    if (la == LA && lb == LB) {                                                                       \
+        if (small) simt::small::gemm_kernel<LA, LB><<<grid, simt::small::THREADS, 0, st>>>(p);        \
+        else simt::gemm_kernel<LA, LB><<<grid, simt::THREADS, 0, st>>>(p);                            \
+    }
     MT_SIMT_CASE(kLdKContigVec, kLdMNContigVec)
     else MT_SIMT_CASE(kLdKContigVec, kLdKContigVec)
     else MT_SIMT_CASE(kLdKContigVec, kLdGeneric)
@@ -198,7 +207,7 @@ int launch_simt(const GemmProblem& p, cudaStream_t st) {
     if (e != cudaSuccess && e != cudaErrorStreamCaptureUnsupported) return cuda_fail(e, "simt gemm launch");
     g_launches.fetch_add(1);
     static const char* names[3] = {"K", "MN", "gen"};
-    t_path = std::string("simt_fp32 a=") + names[la] + " b=" + names[lb];
+    t_path = std::string(small ? "simt_fp32 tile=64 a=" : "simt_fp32 a=") + names[la] + " b=" + names[lb];
     return MT_OK;
 }
 

@@ -425,3 +425,37 @@ def test_tma_store_epilogue_matches_register_stores(eng, port, tmp_path):
         A = inputs.uniform((M, 64), -1, 1, 199)
         B = inputs.uniform((64, N), -1, 1, 200)
         check(mode, big[8:8 + M, 4:4 + N], port.matmul(A, B), absmm(A, B), 64, f"window {mode}")
+
+
+@pytest.mark.parametrize("layout", ["NN", "NT", "TN", "gen"])
+def test_strict_small_grid_tiles_match_large_tiles(eng, port, layout):
+    """Strict fp32 on fewer 128x128 tiles than SMs runs 64x64 tiles (4x the CTAs). Each
+    output is the same FFMA chain in k order either way, so a small product equals, bit for
+    bit, the top-left block of a large one over the same rows, columns and K; ragged
+    edges, every operand layout, an unaligned view, and a bias + ReLU epilogue."""
+    Mb, Nb, K = 4100, 1000, 301
+    a = inputs.uniform((Mb, K + 1), -1, 1, 1701)
+    b = inputs.uniform((K + 1, Nb), -1, 1, 1702)
+    bias = inputs.uniform((Nb,), -1, 1, 1703)
+    ad, bd = dev(a), dev(b)
+    if layout == "gen":
+        A, B = ad[:, 1:], bd[1:, :]                     # start 4 bytes in: no vector loads for A
+    elif layout == "NT":
+        bt = np.zeros((Nb, K + 3), np.float32)          # rows of 304: the K-contiguous vector path
+        bt[:, :K] = b[:K].T
+        A, B = ad[:, :K], dev(bt)[:, :K].t()
+    elif layout == "TN":
+        A, B = dev(np.ascontiguousarray(a[:, :K].T)).t(), bd[:K]
+    else:
+        A, B = ad[:, :K], bd[:K]
+    Cb = torch.empty(Mb, Nb, device="cuda")
+    eng.gemm(A, B, Cb, bias=dev(bias), epi=eng.EPI_BIAS_COL | eng.EPI_RELU, mode="strict")
+    assert eng.last_path().startswith("simt_fp32") and "tile=64" not in eng.last_path(), eng.last_path()
+    Ms, Ns = 300, 200
+    Cs = torch.empty(Ms, Ns, device="cuda")
+    eng.gemm(A[:Ms], B[:, :Ns], Cs, bias=dev(bias[:Ns]), epi=eng.EPI_BIAS_COL | eng.EPI_RELU, mode="strict")
+    assert "tile=64" in eng.last_path(), eng.last_path()
+    assert torch.equal(Cs, Cb[:Ms, :Ns])
+    An, Bn = host(A[:Ms]), host(B[:, :Ns])
+    ref = np.maximum(port.matmul_strided(np.ascontiguousarray(An), np.ascontiguousarray(Bn)) + bias[:Ns], 0)
+    check("strict", host(Cs), ref, absmm(An, Bn) + np.abs(bias[:Ns]), K, f"small grid {layout}")
