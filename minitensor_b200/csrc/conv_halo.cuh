@@ -79,8 +79,13 @@ __device__ __forceinline__ uint64_t halo_desc(uint32_t start) {
 // 32-channel block: 4 k-steps per tap, 3 MMAs per k-step in TF32X3. Unrolled so that every
 // descriptor offset but the pitch is a constant: a 128 x 64 x 8 MMA takes ~48 cycles, and
 // the loop's per-tap arithmetic on the one issuing thread had cost as much again (c4
-// forward: 3.84 -> 3.52 us of issue per tile).
-template <int NT, bool X3, uint32_t BMAT>
+// forward: 3.84 -> 3.52 us of issue per tile). CG2: the CTA-pair form (M = 256, each
+// CTA's halo rows and half of the weight matrix, BMAT = that half's bytes).
+__device__ __forceinline__ void umma_tf32_cg(bool cg2, uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    if (cg2) umma_tf32_pair(d, a, b, idesc, acc);
+    else umma_tf32(d, a, b, idesc, acc);
+}
+template <int NT, bool X3, uint32_t BMAT, bool CG2 = false>
 __device__ __forceinline__ void issue_row_taps(uint32_t d_tmem, uint64_t a0, uint64_t alo0, uint64_t b0,
                                                uint32_t idesc, uint32_t P8, uint32_t row0, bool& first_mma) {
 #pragma unroll
@@ -92,11 +97,11 @@ __device__ __forceinline__ void issue_row_taps(uint32_t d_tmem, uint64_t a0, uin
             const uint64_t ad = a0 + ao + 2 * k, bd = b0 + bo + 2 * k;
             const uint32_t acc = (!first_mma || t > 0 || k > 0) ? 1u : 0u;
             if (X3) {
-                umma_tf32(d_tmem, alo0 + ao + 2 * k, bd, idesc, acc);
-                umma_tf32(d_tmem, ad, bd + (BMAT >> 4), idesc, 1u);
-                umma_tf32(d_tmem, ad, bd, idesc, 1u);
+                umma_tf32_cg(CG2, d_tmem, alo0 + ao + 2 * k, bd, idesc, acc);
+                umma_tf32_cg(CG2, d_tmem, ad, bd + (BMAT >> 4), idesc, 1u);
+                umma_tf32_cg(CG2, d_tmem, ad, bd, idesc, 1u);
             } else {
-                umma_tf32(d_tmem, ad, bd, idesc, acc);
+                umma_tf32_cg(CG2, d_tmem, ad, bd, idesc, acc);
             }
         }
     }

@@ -19,6 +19,7 @@
 #include "conv_gemm.cuh"
 #include "conv_tma.cuh"
 #include "conv_halo.cuh"
+#include "conv_halo2.cuh"
 #include "conv_wgrad.cuh"
 #include "conv_simt.cuh"
 
@@ -1010,6 +1011,53 @@ int launch_halo_inst(const CUtensorMap& ta, const CUtensorMap& tb, const mt::con
     return launch_simple(cudaGetLastError(), "conv fwd halo");
 }
 
+// The CTA-pair halo kernel: clusters of 2 on the TPCs, as many as fit at once.
+template <int BN, bool X3>
+int launch_halo_pair_inst(const CUtensorMap& ta, const CUtensorMap& tb, const mt::convh::HaloParams& hp,
+                          uint32_t smem, int sms, cudaStream_t st) {
+    auto kern = mt::convh::conv_fwd_halo_pair_kernel<BN, X3>;
+    static std::atomic<uint64_t> mask{0};
+    static std::atomic<int> max_clusters[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(mask.load() & bit)) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kHaloSmemMax);
+        if (e != cudaSuccess) return cuda_fail(e, "conv halo pair: set smem attribute");
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * (sms / 2), 1, 1);
+        cfg.blockDim = dim3(mt::convh::HaloCfg<X3>::THREADS, 1, 1);
+        cfg.dynamicSmemBytes = kHaloSmemMax;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2; attr[0].val.clusterDim.y = 1; attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            n = sms / 2;
+        }
+        max_clusters[dev & 63].store(std::min(n, sms / 2));
+        mask.fetch_or(bit);
+    }
+    const int clusters = (int)std::min<long long>(hp.num_tiles, (long long)max_clusters[dev & 63].load());
+    kern<<<2 * clusters, mt::convh::HaloCfg<X3>::THREADS, smem, st>>>(ta, tb, hp);
+    return launch_simple(cudaGetLastError(), "conv fwd halo pair");
+}
+
+// MT_CONV_PAIR=1 runs the halo forward on CTA pairs (M = 256). Off by default: on config 4
+// it measured slower than one CTA per tile (TF32 33.1 vs 31.1 us, 3xTF32 81.4 vs 77.6 us,
+// bitwise equal): halving the MMA instructions issued per output did not help, so the
+// forward is bound by each SM's own MMA work, not by the issuing thread.
+bool conv_pair_enabled() {
+    static int v = [] {
+        const char* e = std::getenv("MT_CONV_PAIR");
+        return (e && e[0] == '1') ? 1 : 0;
+    }();
+    return v != 0;
+}
+
 // The halo kernel serves stride-1 forward-shaped convs whose halo ring fits in shared
 // memory; MT_CONV_HALO=0 turns it off (the per-tap TMA kernel then runs).
 bool halo_enabled() {
@@ -1024,12 +1072,13 @@ bool halo_enabled() {
 // The weight stage takes the largest G (a divisor of the tap count) for which two
 // stages fit beside two halo slots.
 bool plan_halo(int Ho, int Wo, int Cin, int kh, int kw, int Ncol, bool x3, int& bn, mt::convh::HaloParams& hp,
-               uint32_t& smem) {
+               uint32_t& smem, bool pair = false) {
     if (kh < 1 || kw < 1 || Wo < 1 || Ho < 1) return false;
     const uint64_t mult = x3 ? 2 : 1;
     bn = std::min(pick_bn(Ncol), 128);
+    if (pair && bn != 64 && bn != 128) return false;
     const int taps = kh * kw;
-    const uint64_t bmat = (uint64_t)bn * 128;
+    const uint64_t bmat = (uint64_t)(pair ? bn / 2 : bn) * 128;   // a CTA of a pair holds half the columns
     const uint32_t bars = 8u * (3 * mt::convh::kMaxASlots + 2 * mt::convh::kMaxBStages + 4) + 16u;
     const uint64_t budget = kHaloSmemMax - 1024 - bars;
     // Tile shape: TY rows of TXv output columns, pitched P = TXv + kw - 1, TY * P <= 128 MMA
@@ -1097,12 +1146,13 @@ bool plan_halo(int Ho, int Wo, int Cin, int kh, int kw, int Ncol, bool x3, int& 
 // (hi, lo) for TF32X3.
 int run_fwd_halo(const float* act, int N, int Hin, int Win, int Cin, const float* wt, int Ncol, int kh, int kw,
                  int pad, float* out, int Ho, int Wo, const float* bias, bool x3, cudaStream_t st, int sms,
-                 const mt::convh::HaloParams& plan, int bn, uint32_t smem, std::string& path) {
+                 const mt::convh::HaloParams& plan, int bn, uint32_t smem, std::string& path, bool pair = false) {
     mt::convh::HaloParams hp = plan;
     const int Cinp = (Cin + 3) & ~3;
     hp.N = N; hp.Ho = Ho; hp.Wo = Wo; hp.Ncol = Ncol; hp.C = Cin; hp.kh = kh; hp.kw = kw; hp.pad = pad;
     hp.tiles_y = (Ho + hp.TY - 1) / hp.TY;
     hp.tiles_x = (Wo + hp.TXv - 1) / hp.TXv;
+    if (pair) hp.tiles_x = (hp.tiles_x + 1) / 2;   // a pair tile: two tiles side by side
     hp.tiles_n = (Ncol + bn - 1) / bn;
     hp.cblocks = (Cin + 31) / 32;
     hp.taps = kh * kw;
@@ -1115,16 +1165,23 @@ int run_fwd_halo(const float* act, int N, int Hin, int Win, int Cin, const float
                    {rowb, rowb * Win, rowb * Win * Hin}, {32u, (uint32_t)hp.P, (uint32_t)hp.HR, 1u}, 128))
         return fail(MT_EUNSUPPORTED, "conv halo: activation tensor map rejected");
     const uint64_t taps_all = (uint64_t)(kh * kw);
+    const uint32_t bbox = (uint32_t)(pair ? bn / 2 : bn);   // a pair's CTA loads half the columns
     bool ok;
     if (x3)
         ok = encode_4d(&tb, wt, {(uint64_t)Cin, (uint64_t)Ncol, 2, taps_all}, {rowb, rowb * Ncol, rowb * Ncol * 2},
-                       {32u, (uint32_t)bn, 2u, (uint32_t)hp.G}, 128);
+                       {32u, bbox, 2u, (uint32_t)hp.G}, 128);
     else
         ok = encode_4d(&tb, wt, {(uint64_t)Cin, (uint64_t)Ncol, taps_all, 1},
-                       {rowb, rowb * Ncol, rowb * Ncol * taps_all}, {32u, (uint32_t)bn, (uint32_t)hp.G, 1u}, 128);
+                       {rowb, rowb * Ncol, rowb * Ncol * taps_all}, {32u, bbox, (uint32_t)hp.G, 1u}, 128);
     if (!ok) return fail(MT_EUNSUPPORTED, "conv halo: weight tensor map rejected");
     const int grid = (int)std::min<long long>(hp.num_tiles, sms);
     int rc;
+    if (pair) {
+        rc = bn == 64 ? (x3 ? launch_halo_pair_inst<64, true>(ta, tb, hp, smem, sms, st)
+                            : launch_halo_pair_inst<64, false>(ta, tb, hp, smem, sms, st))
+                      : (x3 ? launch_halo_pair_inst<128, true>(ta, tb, hp, smem, sms, st)
+                            : launch_halo_pair_inst<128, false>(ta, tb, hp, smem, sms, st));
+    } else
     switch (bn) {
         case 32:  rc = x3 ? launch_halo_inst<32, true>(ta, tb, hp, smem, grid, st)
                           : launch_halo_inst<32, false>(ta, tb, hp, smem, grid, st); break;
@@ -1135,7 +1192,7 @@ int run_fwd_halo(const float* act, int N, int Hin, int Win, int Cin, const float
     }
     path = std::string("tma_halo bn=") + std::to_string(bn) + " tile=" + std::to_string(hp.TY) + "x" +
            std::to_string(hp.TXv) + " pitch=" + std::to_string(hp.P) + " taps/stage=" + std::to_string(hp.G) +
-           " bstages=" + std::to_string(hp.b_stages) + (hp.b_resident ? " resident" : "");
+           " bstages=" + std::to_string(hp.b_stages) + (hp.b_resident ? " resident" : "") + (pair ? " pair" : "");
     return rc;
 }
 
@@ -1152,11 +1209,19 @@ int run_fwd_tma(const float* act, int N, int Hin, int Win, int Cin, const float*
         memset(&plan, 0, sizeof plan);
         int bn = 0;
         uint32_t smem = 0;
-        if (plan_halo(Ho, Wo, Cin, kh, kw, Ncol, x3, bn, plan, smem)) {
+        // CTA pairs when the pair tiles fill at least one round of the GPU's TPCs.
+        bool pair = false;
+        if (conv_pair_enabled() && plan_halo(Ho, Wo, Cin, kh, kw, Ncol, x3, bn, plan, smem, true)) {
+            const long long ptiles = (long long)N * ((Ho + plan.TY - 1) / plan.TY) *
+                                     (((Wo + plan.TXv - 1) / plan.TXv + 1) / 2) * ((Ncol + bn - 1) / bn);
+            pair = ptiles >= sms / 2;
+        }
+        if (!pair) memset(&plan, 0, sizeof plan);
+        if (pair || plan_halo(Ho, Wo, Cin, kh, kw, Ncol, x3, bn, plan, smem)) {
             int rc = reorder_w(w, sw, wt, Co, Ci, kh, kw, dgrad, st, x3);
             if (rc) return rc;
             return run_fwd_halo(act, N, Hin, Win, Cin, wt, Ncol, kh, kw, pad, out, Ho, Wo, bias, x3, st, sms, plan,
-                                bn, smem, path);
+                                bn, smem, path, pair);
         }
     }
     int rc = reorder_w(w, sw, wt, Co, Ci, kh, kw, dgrad, st, false);

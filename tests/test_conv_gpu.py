@@ -284,3 +284,32 @@ def test_nchw_to_nhwc_views_and_errors(eng):
         eng.nchw_to_nhwc(x6, out=torch.empty_like(x6, memory_format=torch.channels_last))
     with pytest.raises(ValueError, match="shape"):
         eng.nchw_to_nhwc(xv, out=torch.empty(2, 32, 15, 18, device="cuda").to(memory_format=torch.channels_last))
+
+
+def test_cta_pair_forward_matches_one_cta(eng, port, tmp_path):
+    """The CTA-pair halo forward (M = 256 over two SMs; opt-in with MT_CONV_PAIR=1, since it
+    measured slower than one CTA per tile) runs every output through the same MMA k-steps,
+    so its results must equal the one-CTA kernel's bit for bit: config 4's forward and
+    input gradient in both tensor-core precisions, and a shape whose last pair has its
+    second tile past the right edge."""
+    import subprocess
+    import sys
+    script = os.path.join(os.path.dirname(__file__), "conv_pair_cases.py")
+    res = {}
+    for flag in ("1", "0"):
+        out = str(tmp_path / f"pair{flag}.npz")
+        env = dict(os.environ, MT_CONV_PAIR=flag)
+        r = subprocess.run([sys.executable, script, out], env=env, capture_output=True, text=True, timeout=600)
+        assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+        res[flag] = np.load(out)
+    pair, one = res["1"], res["0"]
+    names = [k for k in pair.files if not k.startswith("path_")]
+    assert len(names) == 6
+    for k in names:
+        assert str(pair["path_" + k]).endswith(" pair"), (k, str(pair["path_" + k]))
+        assert " pair" not in str(one["path_" + k]), (k, str(one["path_" + k]))
+        assert np.array_equal(pair[k], one[k]), k
+    x, w, b, _ = inputs.config4()
+    xs = np.ascontiguousarray(x[:2])
+    check("tf32x3", pair["fwd_tf32x3"][:2], port.conv2d(xs, w, b, 1, 1, THREADS),
+          d_fwd(xs, w, 1, 1) + np.abs(b)[None, :, None, None], 576, "pair forward, images 0-1")
