@@ -979,21 +979,35 @@ int launch_wgrad_wide_inst(const CUtensorMap& ta, const CUtensorMap& tb, const m
     return launch_simple(cudaGetLastError(), "conv wgrad wide");
 }
 
-// Stage shape per precision: XCS runs of 32 pixels of one output row (RS = 1) and ring
-// depth, rings of <= ~192 KB (doubled for the TF32X3 lo copies). Measured on c4: TF32
-// takes 2 runs with 4 stages; TF32X3 is better with 1 run and 4 stages than with 2 runs
-// and only 2 stages (a second output row per stage gained nothing either way).
+// Stage shape: XCS runs of 32 pixels of RS output rows, and ring depth, rings of <= ~192 KB
+// (doubled for the TF32X3 lo copies). Measured on c4 (weight-grad alone):
+// - TF32 at C_out <= 64: 2 runs x 2 rows, 2 stages (16 MMAs per stage), 36.4 us, against
+//   42.0 us with 1 row and 4 stages. Per-stage stamps of the issuer showed ~330 cycles of
+//   wait, commit and loop per 8-MMA stage, which the deeper stage amortises.
+// - TF32X3: 1 run x 1 row, 4 stages. 2 rows and 2 stages measured 104.8 against 91.9 us.
+// Wider C_out tiles keep 1 row: a 2-row stage of 128 channels would need 256 KB.
 struct WideShape { int xcs, rs; };
-WideShape wgrad_shape(bool x3) { return x3 ? WideShape{1, 1} : WideShape{2, 1}; }
+WideShape wgrad_shape(bool x3, int bn) {
+    if (x3) return WideShape{1, 1};
+    return bn <= 64 ? WideShape{2, 2} : WideShape{2, 1};
+}
 template <bool X3>
 int launch_wgrad_wide(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const mt::convt::WgradParams& wp,
                       int grid, cudaStream_t st) {
-    constexpr int XCS = X3 ? 1 : 2;
-    switch (bn) {
-        case 32:  return launch_wgrad_wide_inst<32, X3, X3 ? 4 : 4, XCS, 1>(ta, tb, wp, grid, st);
-        case 64:  return launch_wgrad_wide_inst<64, X3, X3 ? 4 : 4, XCS, 1>(ta, tb, wp, grid, st);
-        case 128: return launch_wgrad_wide_inst<128, X3, X3 ? 3 : 3, XCS, 1>(ta, tb, wp, grid, st);
-        default:  return launch_wgrad_wide_inst<256, X3, X3 ? 2 : 2, XCS, 1>(ta, tb, wp, grid, st);
+    if constexpr (X3) {
+        switch (bn) {
+            case 32:  return launch_wgrad_wide_inst<32, true, 4, 1, 1>(ta, tb, wp, grid, st);
+            case 64:  return launch_wgrad_wide_inst<64, true, 4, 1, 1>(ta, tb, wp, grid, st);
+            case 128: return launch_wgrad_wide_inst<128, true, 3, 1, 1>(ta, tb, wp, grid, st);
+            default:  return launch_wgrad_wide_inst<256, true, 2, 1, 1>(ta, tb, wp, grid, st);
+        }
+    } else {
+        switch (bn) {
+            case 32:  return launch_wgrad_wide_inst<32, false, 2, 2, 2>(ta, tb, wp, grid, st);
+            case 64:  return launch_wgrad_wide_inst<64, false, 2, 2, 2>(ta, tb, wp, grid, st);
+            case 128: return launch_wgrad_wide_inst<128, false, 3, 2, 1>(ta, tb, wp, grid, st);
+            default:  return launch_wgrad_wide_inst<256, false, 2, 2, 1>(ta, tb, wp, grid, st);
+        }
     }
 }
 
@@ -1439,7 +1453,7 @@ WgradTmaPlan wgrad_tma_plan(const ConvShape& s, const mt_tensor* dy, const mt_te
     w.tiles_m = (w.M + 127) / 128;
     w.tiles_n = ((int)s.Co + w.bn - 1) / w.bn;
     w.ws_ld = w.tiles_n * w.bn;
-    const WideShape ws = wgrad_shape(x3);
+    const WideShape ws = wgrad_shape(x3, w.bn);
     w.xcs = ws.xcs;
     w.rs = ws.rs;
     w.xblocks = (int)((s.Wo + 32 * w.xcs - 1) / (32 * w.xcs));   // runs of 32 * xcs pixels per row

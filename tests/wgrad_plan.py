@@ -28,9 +28,10 @@ def gather_bytes(N, C, Co, kh, kw, Ho, Wo, sms):
 def tma_bytes(N, C, H, W, Co, kh, kw, Ho, Wo, sms, x3, x_in_place=False):
     """NHWC copy of x (channels padded to 4, rounded to 64 floats; none when x is already
     a channels-last copy, read in place) + split partials."""
-    xcs, rs = (1, 1) if x3 else (2, 1)
     M = kh * kw * C
     bn = pick_bn(Co)
+    # stage shape (runs of 32 pixels, rows): TF32 takes 2 rows per stage at C_out <= 64
+    xcs, rs = (1, 1) if x3 else ((2, 2) if bn <= 64 else (2, 1))
     tiles_n = (Co + bn - 1) // bn
     tiles = ((M + 127) // 128) * tiles_n
     xblocks = (Wo + 32 * xcs - 1) // (32 * xcs)
