@@ -388,9 +388,7 @@ class C2(Workload):
     def step(self, mode):
         e = self.engine
         e.gemm(self.X, self.W, self.Y, bias=self.b.reshape(-1), epi=e.EPI_BIAS_COL, mode=mode)
-        e.gemm(self.dY, self.W.t(), self.dX, mode=mode)
-        e.gemm(self.X.t(), self.dY, self.dW, mode=mode)
-        e.sum_rows(self.dY, self.db)
+        e.linear_backward_into(self.X, self.W, self.dY, self.dX, self.dW, self.db, mode=mode)
 
     def cpu_sample(self, threads):
         impl, kind = _ref()

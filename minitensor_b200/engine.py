@@ -282,18 +282,52 @@ def linear_forward(x, W, bias=None, relu=False, mode=MODE_DEFAULT, stream=None):
     return Y
 
 
+_side_streams = {}
+
+
+def _side_stream(device):
+    """One extra stream per device for work that overlaps the caller's stream."""
+    key = torch.device(device).index if torch.device(device).index is not None else torch.cuda.current_device()
+    if key not in _side_streams:
+        _side_streams[key] = torch.cuda.Stream(device=key)
+    return _side_streams[key]
+
+
+def linear_backward_into(x, W, dY, dX, dW, db, mode=MODE_DEFAULT, stream=None):
+    """MatmulBackward for Linear into caller buffers. dX = dY @ W^T runs on `stream`; dW =
+    x^T @ dY and db run at the same time on a side stream, since neither waits for the
+    other and each fills only part of the GPU at Linear sizes. Events fork the side stream
+    from `stream` and join it back, so `stream` orders everything that follows, CUDA-graph
+    capture included."""
+    if stream is None:
+        s0 = torch.cuda.current_stream(x.device)
+    elif isinstance(stream, torch.cuda.Stream):
+        s0 = stream
+    else:
+        s0 = torch.cuda.ExternalStream(int(stream), device=x.device)
+    side = _side_stream(x.device)
+    fork = torch.cuda.Event()
+    fork.record(s0)
+    side.wait_event(fork)
+    gemm(dY, W.t(), dX, mode=mode, stream=s0)
+    with torch.cuda.stream(side):
+        gemm(x.t(), dY, dW, mode=mode, stream=side)
+        sum_rows(dY, db, stream=side)
+    join = torch.cuda.Event()
+    join.record(side)
+    s0.wait_event(join)
+    return dX, dW, db
+
+
 def linear_backward(x, W, dY, mode=MODE_DEFAULT, stream=None):
     """MatmulBackward for Linear (include/Autograd.hpp:124-141): dX = dY @ W^T and
     dW = x^T @ dY, both read through transposed views (no copies), plus the bias gradient
     db = the sum of dY over rows (the reference's unbroadcast of the bias add,
-    include/TensorOps.hpp:1305-1345)."""
+    include/TensorOps.hpp:1305-1345). dX and (dW, db) run concurrently on two streams."""
     dX = torch.empty_like(x)
     dW = torch.empty_like(W)
-    gemm(dY, W.t(), dX, mode=mode, stream=stream)
-    gemm(x.t(), dY, dW, mode=mode, stream=stream)
     db = torch.empty((1, dY.shape[1]), dtype=torch.float32, device=dY.device)
-    sum_rows(dY, db, stream=stream)
-    return dX, dW, db
+    return linear_backward_into(x, W, dY, dX, dW, db, mode=mode, stream=stream)
 
 
 def matmul_host(A, B, C=None, mode=MODE_DEFAULT, panels=0, workspace=None, stream=None, sync=True):
