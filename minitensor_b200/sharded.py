@@ -9,9 +9,10 @@ CUDA IPC, then pushes its columns into every peer's C in one of two ways:
 
 * ``gather="epilogue"`` (default): the GEMM and the all-gather are ONE kernel -- the
   tcgen05 epilogue hands each finished 32x32 block of a tile to the TMA engine, which
-  stores it into the local C and, over NVLink, into the same columns of every peer's C
-  while the next tile's main loop runs (measured ~630 GB/s of egress per GPU with 2 and
-  4 ranks).
+  stores it into the local C and, over NVLink, into the same columns of every peer's C,
+  meant to run while the next tile's main loop runs. Measured on 8192^3, the gather is
+  hidden on 2 ranks. On 4 and 8 ranks it adds about the time the received bytes take
+  over the link (0.25-0.5 ms per step), so it is not hidden there.
 * ``gather="copy"``: the GEMM runs in row chunks into the local C; after each chunk the
   copy engines push that chunk's columns to every peer (one 2-D copy per peer, each peer
   on its own stream) while the next chunk is computed. Slower here at every size (the
